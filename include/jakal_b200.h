@@ -1,0 +1,157 @@
+/*
+ * jakal_b200.h — C ABI of the B200-native (sm_100a) Jakal-Net operator hot path.
+ *
+ * Every entry point takes raw device pointers, sizes, dtype codes and a CUDA stream,
+ * launches asynchronously on that stream and returns an int status (JK_OK == 0, negative
+ * codes below). No entry point allocates device memory except where stated; callers own
+ * every buffer. Inputs are read-only and C-contiguous; outputs are fully overwritten.
+ *
+ * Reference interfaces (Ahnd6474/Jakal-Net, paths relative to that project) that each
+ * entry point replaces are cited beside the declaration.
+ */
+#ifndef JAKAL_B200_H_
+#define JAKAL_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (jk_status_string gives the text) ---------------------------------- */
+#define JK_OK 0
+#define JK_ERR_BAD_SHAPE (-1)          /* sizes inconsistent or out of the supported range */
+#define JK_ERR_BAD_DTYPE (-2)          /* dtype code unknown or not supported by this op  */
+#define JK_ERR_UNSUPPORTED_KIND (-3)   /* compress / scorer kind not implemented          */
+#define JK_ERR_UNSUPPORTED_DEVICE (-4) /* no sm_100 device, or pointer not on the device  */
+#define JK_ERR_LAUNCH (-5)             /* CUDA launch / runtime error                     */
+#define JK_ERR_DEVICE_TIMEOUT (-6)     /* a bounded device-side wait gave up              */
+#define JK_ERR_BAD_ARG (-7)            /* null pointer, negative k, bad window, ...       */
+#define JK_ERR_ALIGNMENT (-8)          /* pointer not 16-byte aligned where required      */
+
+/* ---- dtype codes --------------------------------------------------------------------- */
+#define JK_F32 0
+#define JK_BF16 1
+#define JK_F16 2
+
+/* ---- edge / route compressors --------------------------------------------------------- */
+#define JK_SOFTSIGN 0              /* s / (1 + |s|)                       propagation.py:85   */
+#define JK_SIGNED_ABS_SOFTMAX 1    /* sign(s) * softmax(|s|)              propagation.py:74-82 */
+#define JK_SIGNED_ENTMAX15 2       /* sign(s) * entmax15(|s|)             kernels.py:155-236  */
+#define JK_SOFTMAX 3               /* softmax(s)  (routes)                transition.py:187-194 */
+
+typedef struct CUstream_st* jk_stream_t; /* == cudaStream_t; NULL = legacy default stream */
+
+/* Human-readable text for a status code. */
+const char* jk_status_string(int status);
+
+/* Library / device probe. Returns JK_OK when the current device is sm_100 and the
+ * kernels can launch; otherwise JK_ERR_UNSUPPORTED_DEVICE. Replaces the loader probes
+ * native_backend.py:98-178 (supported_devices) / jakal_net_native.cpp:5914-5931. */
+int jk_device_check(void);
+
+/* Synchronises `stream`, then reads and clears the library's device-side error word
+ * (set by a kernel whose bounded wait gave up). *device_status receives JK_OK or
+ * JK_ERR_DEVICE_TIMEOUT. */
+int jk_device_status(jk_stream_t stream, int* device_status);
+
+/* Padded projection width the fused kernels expect for a score rank `rank`
+ * (rank rounded up to a multiple of 64). */
+int64_t jk_padded_rank(int64_t rank);
+
+/*
+ * Low-rank projection prologue (tcgen05 GEMM):
+ *   out[r, c] = round(x[r, :] . w[c, :])                         c <  rank
+ *   then, if core != NULL:  out = round(out * core[c])
+ *   then, if temperature != 1: out = round(out / temperature)
+ *   out[r, c] = 0 for rank <= c < out_stride (padding)
+ * x [rows, dim], w [rank, dim], core [rank], out [rows, out_stride]; all in `dtype`
+ * (JK_BF16 or JK_F16); round() = round-to-nearest into dtype, matching a torch.matmul in
+ * the input dtype followed by the elementwise ops in that dtype.
+ * Requirements: dim % 8 == 0, rank <= 128, out_stride == jk_padded_rank(rank).
+ * Replaces the projection steps of jakal_net_native.cpp:6236-6239 (propagation) and
+ * :6977-6986 (pairwise-route transition); native_backend.py:4445-4458.
+ */
+int jk_lowrank_project(const void* x, int64_t rows, int64_t dim, const void* w, int64_t rank,
+                       const void* core, float temperature, int dtype, void* out,
+                       int64_t out_stride, jk_stream_t stream);
+
+/*
+ * Fused per-row top-k aggregate (tcgen05 score GEMM + streaming top-k + gather):
+ *   score[b,t,s] = row_proj[b,t,:] . col_proj[b,s,:]              (f32 accumulation)
+ *   visible(t,s) = s < n_cols and (window < 0 or t - window <= s <= t)
+ *   sel(t)       = the min(k, #visible) visible s with the largest score, ties to the
+ *                  lower s
+ *   e[t,s]       = compress(score + score_bias) over sel(t)        (compress = JK_*)
+ *   w[t,s]       = e[t,s] * (col_sender ? col_sender[b,s] : 1)
+ *   out_state[b,t]  = sum_{s in sel(t)} w[t,s] * col_state[b,s]
+ *   out_val[b,t,:]  = sum_{s in sel(t)} w[t,s] * col_val[b,s,:]
+ * score_bias is added to every score; when bias_dev != NULL the f32 it points to (device
+ * memory) is added as well, so a bias tensor needs no host synchronisation.
+ * Shapes: row_proj [B, n_rows, rp], col_proj [B, n_cols, rp] (rp = jk_padded_rank, dtype
+ * proj_dtype = JK_BF16 | JK_F16); col_state and col_sender [B, n_cols] in state_dtype;
+ * col_val [B, n_cols, dim] in val_dtype; out_state [B, n_rows], out_val [B, n_rows, dim] in
+ * out_dtype. Optional out_scores f32 [B, n_rows, k] (score + bias, sorted descending,
+ * -inf in empty slots) and out_index int64 [B, n_rows, k] (-1 in empty slots).
+ * 1 <= k <= 64. rp <= 128.
+ * Replaces low_rank_propagation_topk_forward_cuda (jakal_net_native_cuda.cu:2545-2660,
+ * kernel :1029-1183) as called from propagation_topk (jakal_net_native.cpp:6355-6389);
+ * the window > 0 form is the window-intersect-top-k operator built from
+ * kernel_common.py:433-456 + propagation.py:67-88.
+ */
+int jk_propagation_topk_forward(const void* row_proj, const void* col_proj, int64_t batch,
+                                int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
+                                const void* col_state, const void* col_sender, int state_dtype,
+                                const void* col_val, int64_t dim, int val_dtype, int64_t k,
+                                int64_t window, float score_bias, const float* bias_dev,
+                                int compress, void* out_state, void* out_val, int out_dtype,
+                                float* out_scores, int64_t* out_index, jk_stream_t stream);
+
+/*
+ * Per-query ("query top-k") transition: identical contract to
+ * jk_propagation_topk_forward with rows = query slots (row_proj = target-side route
+ * projection of query_val), columns = source nodes (col_proj = core-weighted,
+ * temperature-scaled source projection), compress = JK_SOFTMAX and
+ * col_sender = sender strength softplus(src.state); window must be -1.
+ * Replaces transition_query_topk (jakal_net_native.cpp:7089-7246) and
+ * query_topk_reduce_cuda (jakal_net_native_cuda.cu:2335-2417).
+ */
+int jk_transition_query_topk_forward(const void* query_proj, const void* source_proj,
+                                     int64_t batch, int64_t n_query, int64_t n_source,
+                                     int64_t rp, int proj_dtype, const void* source_state,
+                                     const void* source_sender, int state_dtype,
+                                     const void* source_val, int64_t dim, int val_dtype,
+                                     int64_t k, float score_bias, const float* bias_dev,
+                                     int compress, void* out_state, void* out_val,
+                                     int out_dtype, float* out_scores, int64_t* out_index,
+                                     jk_stream_t stream);
+
+/*
+ * Per-source sparse transition (SparseTransition):
+ *   logit[b,i,j] = src_proj[b,i,:] . dst_proj[b,j,:] + score_bias (+ *bias_dev)
+ *                  (src_proj already core-weighted and temperature-scaled)
+ *   sel(i)       = top-k destinations j of source i, ties to the lower j
+ *   r[i,j]       = compress(logit) over sel(i)        (JK_SOFTMAX / SIGNED_ABS / ENTMAX15)
+ *   out_state[b,j] = sum_i r[i,j] * src_sender[b,i] * src_state[b,i]
+ *   out_val[b,j,:] = sum_i r[i,j] * src_sender[b,i] * src_val[b,i,:]
+ * src_state / src_sender in state_dtype, src_val in val_dtype. `accum` is caller-provided
+ * f32 scratch of B*n_dst*(dim+1) elements, 16-byte aligned (zeroed by the call); outputs
+ * are written in out_dtype. 1 <= k <= 64.
+ * Replaces low_rank_pairwise_topk_forward_cuda (jakal_net_native_cuda.cu:2420-2542,
+ * kernel :740-878) as called from transition_pairwise_topk
+ * (jakal_net_native.cpp:6958-7007).
+ */
+int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_proj,
+                                        int64_t batch, int64_t n_src, int64_t n_dst,
+                                        int64_t rp, int proj_dtype, const void* src_state,
+                                        const void* src_sender, int state_dtype,
+                                        const void* src_val, int64_t dim, int val_dtype,
+                                        int64_t k, float score_bias, const float* bias_dev,
+                                        int compress, float* accum, void* out_state,
+                                        void* out_val, int out_dtype, jk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JAKAL_B200_H_ */

@@ -1,0 +1,32 @@
+// Host-side helpers shared by the Jakal-Net B200 entry points: status handling,
+// device checks and TMA tensor-map encoding through the driver entry point (so the
+// library needs no link-time dependency on libcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/jakal_b200.h"
+
+namespace jk {
+
+// Device-side error word (JK_OK or JK_ERR_DEVICE_TIMEOUT), written by kernels whose
+// bounded wait gave up; read and cleared by jk_device_status. The library is built as a
+// single translation unit (jk_lib.cu), so the definition lives here.
+__device__ int g_device_error = 0;
+
+// Returns JK_OK when the current device is sm_100 (cached per device ordinal).
+int check_device();
+
+// Maps the last CUDA runtime error to a status code (JK_OK when none).
+int launch_status();
+
+// Encodes a 3-D tiled tensor map over a contiguous [d2][d1][d0] array of 16-bit elements
+// with a {box0, box1, 1} box and 128-byte swizzle. Returns JK_OK or an error status.
+int make_tmap_3d_16bit(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                       uint32_t box0, uint32_t box1, bool bf16);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace jk

@@ -1,0 +1,5 @@
+// Single translation unit of libjakal_b200.so: the device error word and every
+// kernel live in one module, so no relocatable device code is needed.
+#include "jk_host.cu"
+#include "jk_project.cu"
+#include "jk_topk.cu"

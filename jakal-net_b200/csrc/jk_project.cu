@@ -1,0 +1,225 @@
+// Low-rank projection prologue: out = round(x . w^T) [* core] [/ temperature], written
+// into a rank-padded [rows, rp] buffer the fused kernels read with TMA.
+//
+// One CTA per 128 rows: warp 4 issues TMA loads of x / w chunks (64 columns of the
+// model dimension per stage, 128-byte swizzle) and the tcgen05 MMAs (M=128, N=rp,
+// K=16 steps) into a TMEM accumulator; warps 0-3 read the accumulator back
+// (thread = row) and apply the rounding chain of the reference:
+//   jakal_net_native.cpp:6236-6239  projected = torch::matmul(val, W^T)   (input dtype)
+//                                  weighted  = projected * w.to(dtype)
+//   jakal_net_native.cpp:6979-6983  weighted  = weighted / temperature     (routes)
+#include "jk_host.h"
+#include "jk_sm100.cuh"
+
+namespace jk {
+namespace proj {
+
+constexpr int kRows = 128;
+constexpr int kStages = 4;
+constexpr int kThreads = 160;
+
+struct Params {
+  int64_t rows;
+  int64_t dim;
+  int64_t rank;
+  int64_t rp;
+  const void* core;
+  float temperature;
+  int bf16;
+  void* out;
+};
+
+__host__ __device__ constexpr int a_bytes() { return kRows * 128; }
+
+template <int RP>
+__global__ void __launch_bounds__(kThreads, 1)
+    project_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                   Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kABytes = a_bytes();
+  constexpr int kBBytes = RP * 128;
+  constexpr int kStageBytes = kABytes + kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* done = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
+  const int nchunks = static_cast<int>((p.dim + 63) / 64);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, RP < 32 ? 32 : RP);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_x);
+      prefetch_tmap(&tm_w);
+      const uint32_t idesc = idesc_f16(128, RP, p.bf16 ? 1u : 0u);
+      bool ok = true;
+      // Prefill.
+      const int pre = nchunks < kStages ? nchunks : kStages;
+      for (int c = 0; c < pre; ++c) {
+        uint8_t* st = smem + c * kStageBytes;
+        mbar_arrive_expect_tx(&full[c], kStageBytes);
+        tma_load_3d(st, &tm_x, &full[c], c * 64, static_cast<int>(row0), 0);
+        tma_load_3d(st + kABytes, &tm_w, &full[c], c * 64, 0, 0);
+      }
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int s = c % kStages;
+        if (!mbar_wait(&full[s], (c / kStages) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * kStageBytes);
+        const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_f16_ss(tmem, sdesc_kmajor_sw128(a_addr + kk * 32), sdesc_kmajor_sw128(b_addr + kk * 32),
+                     idesc, (c > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty[s]);
+        // Refill the stage of the previous chunk once its MMAs retired.
+        const int cp = c - 1;
+        if (cp >= 0 && cp + kStages < nchunks) {
+          const int sp = cp % kStages;
+          if (!mbar_wait(&empty[sp], (cp / kStages) & 1)) { ok = false; break; }
+          uint8_t* st = smem + sp * kStageBytes;
+          mbar_arrive_expect_tx(&full[sp], kStageBytes);
+          tma_load_3d(st, &tm_x, &full[sp], (cp + kStages) * 64, static_cast<int>(row0), 0);
+          tma_load_3d(st + kABytes, &tm_w, &full[sp], (cp + kStages) * 64, 0, 0);
+        }
+      }
+      if (ok) {
+        mma_commit(done);
+        const int last = nchunks - 1;
+        ok = mbar_wait(&empty[last % kStages], (last / kStages) & 1);
+      }
+      if (!ok) {
+        atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
+        *abort_flag = 1;
+      }
+    }
+  } else {
+    // Epilogue: thread = row.
+    bool ok = mbar_wait(done, 0);
+    if (!ok) {
+      atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
+    } else {
+      tc_fence_after();
+      const int r_in = warp * 32 + lane;
+      const int64_t row = row0 + r_in;
+      uint8_t* out_row = reinterpret_cast<uint8_t*>(p.out) + row * p.rp * 2;
+#pragma unroll
+      for (int cb = 0; cb < RP; cb += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + cb, v);
+        tmem_ld_wait();
+        if (row < p.rows) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float f[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int c = cb + i + h;
+              float x = __uint_as_float(v[i + h]);
+              if (c >= p.rank) {
+                x = 0.f;
+              } else if (p.bf16) {
+                x = __bfloat162float(__float2bfloat16_rn(x));
+                if (p.core) {
+                  const float cw = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.core)[c]);
+                  x = __bfloat162float(__float2bfloat16_rn(x * cw));
+                }
+                if (p.temperature != 1.f) x = __bfloat162float(__float2bfloat16_rn(x / p.temperature));
+              } else {
+                x = __half2float(__float2half_rn(x));
+                if (p.core) {
+                  const float cw = __half2float(reinterpret_cast<const __half*>(p.core)[c]);
+                  x = __half2float(__float2half_rn(x * cw));
+                }
+                if (p.temperature != 1.f) x = __half2float(__float2half_rn(x / p.temperature));
+              }
+              f[h] = x;
+            }
+            if (p.bf16) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(f[0], f[1]);
+              packed[i / 2] = *reinterpret_cast<uint32_t*>(&b2);
+            } else {
+              __half2 h2 = __floats2half2_rn(f[0], f[1]);
+              packed[i / 2] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+          }
+          uint4* dst = reinterpret_cast<uint4*>(out_row + cb * 2);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, RP < 32 ? 32 : RP);
+  }
+}
+
+template <int RP>
+constexpr int smem_bytes() {
+  return 1024 + kStages * (a_bytes() + RP * 128) + 256;
+}
+
+}  // namespace proj
+}  // namespace jk
+
+extern "C" int jk_lowrank_project(const void* x, int64_t rows, int64_t dim, const void* w,
+                                  int64_t rank, const void* core, float temperature, int dtype,
+                                  void* out, int64_t out_stride, jk_stream_t stream) {
+  using namespace jk;
+  if (x == nullptr || w == nullptr || out == nullptr) return JK_ERR_BAD_ARG;
+  if (dtype != JK_BF16 && dtype != JK_F16) return JK_ERR_BAD_DTYPE;
+  if (rows <= 0 || dim <= 0 || rank <= 0 || rank > 128 || dim % 8 != 0) return JK_ERR_BAD_SHAPE;
+  if (rows > (int64_t(1) << 31) - 256 || dim > (int64_t(1) << 30)) return JK_ERR_BAD_SHAPE;
+  const int64_t rp = jk_padded_rank(rank);
+  if (out_stride != rp) return JK_ERR_BAD_SHAPE;
+  if (!(temperature > 0.f)) return JK_ERR_BAD_ARG;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return JK_ERR_ALIGNMENT;
+  int st = check_device();
+  if (st != JK_OK) return st;
+
+  const bool bf16 = dtype == JK_BF16;
+  CUtensorMap tm_x, tm_w;
+  st = make_tmap_3d_16bit(&tm_x, x, dim, rows, 1, 64, 128, bf16);
+  if (st != JK_OK) return st;
+  st = make_tmap_3d_16bit(&tm_w, w, dim, rank, 1, 64, static_cast<uint32_t>(rp), bf16);
+  if (st != JK_OK) return st;
+
+  proj::Params p{rows, dim, rank, rp, core, temperature, bf16 ? 1 : 0, out};
+  const dim3 grid(static_cast<unsigned>((rows + 127) / 128));
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (rp == 64) {
+    constexpr int sm = proj::smem_bytes<64>();
+    cudaFuncSetAttribute(proj::project_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    proj::project_kernel<64><<<grid, proj::kThreads, sm, s>>>(tm_x, tm_w, p);
+  } else {
+    constexpr int sm = proj::smem_bytes<128>();
+    cudaFuncSetAttribute(proj::project_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    proj::project_kernel<128><<<grid, proj::kThreads, sm, s>>>(tm_x, tm_w, p);
+  }
+  return launch_status();
+}

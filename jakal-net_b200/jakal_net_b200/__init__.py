@@ -1,0 +1,351 @@
+"""B200-native (sm_100a) backend for the Jakal-Net operator hot path.
+
+This module is a drop-in for the reference's native extension module: the reference
+loader (``jakal_net.native_backend._load_native_module``, native_backend.py:98-160)
+imports the module named by ``JAKAL_NET_NATIVE_MODULE``; with
+``JAKAL_NET_NATIVE_MODULE=jakal_net_b200`` it reads ``supported_ops()``,
+``supported_devices()`` and ``backend_name()`` from here and then calls the op functions
+below positionally, exactly as it calls ``jakal_net_native`` (native_backend.py:5359-6021).
+
+Every op runs on the GPU through ``libjakal_b200.so`` (C ABI in include/jakal_b200.h).
+There is no CPU path: CPU tensors, unsupported kinds or dtypes raise instead of falling
+back to another implementation.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import _lib
+from ._lib import JakalB200Error, check, load
+
+__all__ = [
+    "supported_ops",
+    "supported_devices",
+    "backend_name",
+    "propagation_topk",
+    "propagation_window_topk",
+    "transition_query_topk",
+    "transition_pairwise_topk",
+    "lowrank_project",
+    "topk_aggregate",
+    "JakalB200Error",
+]
+
+_LIBRARY = load()  # import fails loudly when the library is missing
+
+_DTYPE_CODE = {torch.float32: _lib.JK_F32, torch.bfloat16: _lib.JK_BF16, torch.float16: _lib.JK_F16}
+_EDGE_CODE = {
+    "softsign": _lib.JK_SOFTSIGN,
+    "signed_abs_softmax": _lib.JK_SIGNED_ABS_SOFTMAX,
+    "signed_entmax15": _lib.JK_SIGNED_ENTMAX15,
+}
+_ROUTE_CODE = {
+    "softmax": _lib.JK_SOFTMAX,
+    "signed_abs_softmax": _lib.JK_SIGNED_ABS_SOFTMAX,
+    "signed_entmax15": _lib.JK_SIGNED_ENTMAX15,
+}
+_MAX_K = 64
+
+_SUPPORTED_OPS = (
+    "propagation_topk",
+    "transition_pairwise_topk",
+    "transition_query_topk",
+)
+
+
+def supported_ops() -> list[str]:
+    """Ops this module implements (jakal_net_native.cpp:5863-5912 contract). The
+    ``*_cuda`` autograd entry points are deliberately not advertised: this backend is
+    forward-only, and advertising them would route training through them
+    (native_backend.py:659-667)."""
+    return list(_SUPPORTED_OPS)
+
+
+def supported_devices() -> list[str]:
+    return ["cuda"]
+
+
+def backend_name() -> str:
+    return "b200_sm100a"
+
+
+# ----------------------------------------------------------------------------- helpers
+def _ptr(t: Optional[Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(name: str, t: Tensor) -> None:
+    if not isinstance(t, Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if t.device.type != "cuda":
+        raise RuntimeError(f"{name} must be a CUDA tensor in the b200_sm100a backend (got {t.device}).")
+
+
+def _dtype_code(name: str, t: Tensor) -> int:
+    code = _DTYPE_CODE.get(t.dtype)
+    if code is None:
+        raise RuntimeError(f"{name}: unsupported dtype {t.dtype}")
+    return code
+
+
+def _proj_dtype(val: Tensor) -> int:
+    if val.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError(
+            "b200_sm100a scores low-rank projections on tcgen05 tensor cores in the input "
+            f"dtype; bfloat16 or float16 inputs are required (got {val.dtype})."
+        )
+    return _DTYPE_CODE[val.dtype]
+
+
+def _flatten_val(t: Tensor) -> Tensor:
+    return t.reshape(-1, t.shape[-2], t.shape[-1]).contiguous()
+
+
+def _flatten_state(t: Tensor) -> Tensor:
+    return t.reshape(-1, t.shape[-1]).contiguous()
+
+
+def lowrank_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None,
+                    temperature: float = 1.0) -> Tensor:
+    """round(x @ weight^T) [* core] [/ temperature] in x's dtype, padded to a multiple of
+    64 columns (jakal_net_native.cpp:6236-6239, 6977-6986). x [..., D] -> [..., rp]."""
+    _require_cuda("x", x)
+    code = _proj_dtype(x)
+    rank, dim = weight.shape
+    if x.shape[-1] != dim:
+        raise ValueError(f"projection weight expects dim {dim}, got {x.shape[-1]}")
+    x2 = x.reshape(-1, dim).contiguous()
+    w = weight.detach().to(device=x.device, dtype=x.dtype).contiguous()
+    c = None if core is None else core.detach().reshape(-1).to(device=x.device, dtype=x.dtype).contiguous()
+    rp = int(_LIBRARY.jk_padded_rank(rank))
+    out = torch.empty((x2.shape[0], rp), device=x.device, dtype=x.dtype)
+    with torch.cuda.device(x.device):
+        check(
+            _LIBRARY.jk_lowrank_project(x2.data_ptr(), x2.shape[0], dim, w.data_ptr(), rank, _ptr(c),
+                                        float(temperature), code, out.data_ptr(), rp, _stream(x.device)),
+            "jk_lowrank_project",
+        )
+    return out.reshape(*x.shape[:-1], rp)
+
+
+def _bias_tensor(bias: Optional[Tensor], device: torch.device, scale: float = 1.0) -> Optional[Tensor]:
+    if bias is None:
+        return None
+    b = bias.detach().reshape(-1)
+    if b.numel() == 0:
+        return None
+    if b.numel() != 1:
+        raise RuntimeError("score bias must be a scalar")
+    b = b.to(device=device, dtype=torch.float32)
+    return b / scale if scale != 1.0 else b.contiguous()
+
+
+def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, k: int, *,
+                   window: int = -1, compress: int = _lib.JK_SOFTSIGN, col_sender: Optional[Tensor] = None,
+                   bias: Optional[Tensor] = None, score_bias: float = 0.0,
+                   out_dtype: Optional[torch.dtype] = None, return_selection: bool = False):
+    """Raw fused top-k aggregate over already-projected inputs (jk_propagation_topk_forward).
+
+    row_proj [B, T, rp], col_proj [B, S, rp], col_state [B, S], col_val [B, S, D].
+    Returns (state [B, T], val [B, T, D]) and, with return_selection, also the selected
+    scores (f32 [B, T, k]) and indices (int64 [B, T, k]).
+    """
+    for name, t in (("row_proj", row_proj), ("col_proj", col_proj), ("col_state", col_state), ("col_val", col_val)):
+        _require_cuda(name, t)
+    B, T, rp = row_proj.shape
+    S = col_proj.shape[1]
+    D = col_val.shape[-1]
+    dev = col_val.device
+    out_dtype = out_dtype or col_val.dtype
+    out_state = torch.empty((B, T), device=dev, dtype=out_dtype)
+    out_val = torch.empty((B, T, D), device=dev, dtype=out_dtype)
+    scores = torch.empty((B, T, k), device=dev, dtype=torch.float32) if return_selection else None
+    index = torch.empty((B, T, k), device=dev, dtype=torch.int64) if return_selection else None
+    sender = None if col_sender is None else col_sender.to(col_state.dtype).contiguous()
+    with torch.cuda.device(dev):
+        check(
+            _LIBRARY.jk_propagation_topk_forward(
+                row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj),
+                col_state.data_ptr(), _ptr(sender), _dtype_code("state", col_state),
+                col_val.data_ptr(), D, _dtype_code("val", col_val),
+                k, window, float(score_bias), _ptr(bias), compress,
+                out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state),
+                _ptr(scores), _ptr(index), _stream(dev)),
+            "jk_propagation_topk_forward",
+        )
+    if return_selection:
+        return out_state, out_val, scores, index
+    return out_state, out_val
+
+
+def _lowrank_pair_projections(kind: str, weight: Tensor, in_weight: Optional[Tensor], in_bias, out_weight, out_bias,
+                              layer_val: Tensor):
+    if kind != "low_rank_bilinear":
+        raise RuntimeError(f"Unsupported pairwise kernel kind for b200_sm100a: {kind}")
+    if in_weight is None or out_weight is None:
+        raise RuntimeError("Low-rank bilinear pairwise kernel is missing projection weights.")
+    if in_bias is not None or out_bias is not None:
+        raise RuntimeError("Low-rank bilinear projections take no bias.")
+    row_proj = lowrank_project(layer_val, out_weight)              # target side
+    col_proj = lowrank_project(layer_val, in_weight, core=weight)  # source side, * w_hat
+    return row_proj, col_proj
+
+
+def _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
+                           layer_val, projected_state, projected_val, topk: int, window: int):
+    if edge_compress_name not in _EDGE_CODE:
+        raise RuntimeError(
+            "Only edge_compress_name in {softsign, signed_abs_softmax, signed_entmax15} is supported by the native backend."
+        )
+    if topk <= 0:
+        raise RuntimeError("topk must be positive.")
+    for name, t in (("layer_val", layer_val), ("projected_state", projected_state), ("projected_val", projected_val)):
+        _require_cuda(name, t)
+    batch_shape = layer_val.shape[:-2]
+    n = layer_val.shape[-2]
+    out_dim = projected_val.shape[-1]
+    val = _flatten_val(layer_val)
+    pstate = _flatten_state(projected_state)
+    pval = _flatten_val(projected_val)
+    k = min(int(topk), n)
+    if k > _MAX_K:
+        raise RuntimeError(f"b200_sm100a top-k supports k <= {_MAX_K} (got {k}).")
+    row_proj, col_proj = _lowrank_pair_projections(kind, weight, in_weight, in_bias, out_weight, out_bias, val)
+    same = projected_state.dtype == projected_val.dtype
+    out_dtype = projected_val.dtype if same else torch.float32
+    bias_t = _bias_tensor(bias, val.device)
+    state, out = topk_aggregate(row_proj, col_proj, pstate, pval, k, window=window,
+                                compress=_EDGE_CODE[edge_compress_name], bias=bias_t, out_dtype=out_dtype)
+    state = state.to(projected_state.dtype).reshape(*batch_shape, n)
+    out = out.to(projected_val.dtype).reshape(*batch_shape, n, out_dim)
+    return state, out
+
+
+def propagation_topk(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
+                     layer_val, projected_state, projected_val, topk, target_block_size, source_block_size):
+    """SparsePropagation(sparse_type="topk") forward: per target, top-k over every source
+    (no causal mask), edges over the k, aggregate. Reference op: jakal_net_native.cpp:6305-6447
+    (CUDA fast path :6355-6389). Block sizes are accepted for signature parity; the fused
+    kernel tiles internally."""
+    return _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
+                                  edge_compress_name, layer_val, projected_state, projected_val, topk, -1)
+
+
+def propagation_window_topk(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
+                            layer_val, projected_state, projected_val, window, topk, target_block_size=0,
+                            source_block_size=0):
+    """Window-intersect-top-k propagation: causal window mask (kernel_common.py:443-456),
+    then top-k among the visible sources (rows with fewer visible sources use all of them),
+    edges over the survivors (propagation.py:67-88). Not a reference op; the benchmark
+    configurations that combine a causal window with top-k use it."""
+    if window < 0:
+        raise RuntimeError("window must be non-negative.")
+    return _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
+                                  edge_compress_name, layer_val, projected_state, projected_val, topk, int(window))
+
+
+def _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                       hidden_weight, hidden_bias, out_weight, out_bias, temperature, src_val, dst_val):
+    if route_kind != "low_rank_bilinear_route":
+        raise TypeError(f"Unsupported pairwise route kind for b200_sm100a: {route_kind}")
+    if source_weight is None or target_weight is None:
+        raise RuntimeError("Low-rank route kernel is missing projection weights.")
+    if any(t is not None for t in (source_bias, target_bias, hidden_weight, hidden_bias, out_weight, out_bias)):
+        raise TypeError("Low-rank route projections take no bias / hidden layers.")
+    temperature = float(temperature)
+    if temperature <= 0.0:
+        raise RuntimeError("route temperature must be positive.")
+    src_proj = lowrank_project(src_val, source_weight, core=core_weight, temperature=temperature)
+    dst_proj = lowrank_project(dst_val, target_weight)
+    return src_proj, dst_proj, _bias_tensor(bias, src_val.device, temperature)
+
+
+def transition_query_topk(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                          hidden_weight, hidden_bias, out_weight, out_bias, temperature, sender_strength, src_val,
+                          query_val, projected_state, projected_val, topk, query_block_size, source_block_size,
+                          use_cuda_reduce=True):
+    """Per-query transition (jakal_net_native.cpp:7089-7246): each query slot takes its
+    top-k sources by route logit, softmax over the k, sender-weighted gather."""
+    for name, t in (("sender_strength", sender_strength), ("src_val", src_val), ("query_val", query_val),
+                    ("projected_state", projected_state), ("projected_val", projected_val)):
+        _require_cuda(name, t)
+    if topk <= 0:
+        raise RuntimeError("topk must be positive.")
+    batch_shape = query_val.shape[:-2]
+    n_query = query_val.shape[-2]
+    n_src = src_val.shape[-2]
+    out_dim = projected_val.shape[-1]
+    sv = _flatten_val(src_val)
+    qv = _flatten_val(query_val)
+    k = min(int(topk), n_src)
+    if k > _MAX_K:
+        raise RuntimeError(f"b200_sm100a top-k supports k <= {_MAX_K} (got {k}).")
+    src_proj, q_proj, bias_t = _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias,
+                                                  core_weight, bias, hidden_weight, hidden_bias, out_weight,
+                                                  out_bias, temperature, sv, qv)
+    pstate = _flatten_state(projected_state)
+    sender = _flatten_state(sender_strength).to(pstate.dtype)
+    pval = _flatten_val(projected_val)
+    same = projected_state.dtype == projected_val.dtype
+    out_dtype = projected_val.dtype if same else torch.float32
+    state, out = topk_aggregate(q_proj, src_proj, pstate, pval, k, window=-1, compress=_lib.JK_SOFTMAX,
+                                col_sender=sender, bias=bias_t, out_dtype=out_dtype)
+    return (state.to(projected_state.dtype).reshape(*batch_shape, n_query),
+            out.to(projected_val.dtype).reshape(*batch_shape, n_query, out_dim))
+
+
+def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                             hidden_weight, hidden_bias, out_weight, out_bias, temperature, sender_strength, src_val,
+                             dst_val, projected_state, projected_val, topk, src_block_size, dst_block_size,
+                             route_compress_name="softmax"):
+    """SparseTransition forward (jakal_net_native.cpp:6916-7087): each source takes its
+    top-k destinations by route logit, routes compressed over the k, sender-weighted
+    scatter-add into the destinations."""
+    for name, t in (("sender_strength", sender_strength), ("src_val", src_val), ("dst_val", dst_val),
+                    ("projected_state", projected_state), ("projected_val", projected_val)):
+        _require_cuda(name, t)
+    if topk <= 0:
+        raise RuntimeError("topk must be positive.")
+    if route_compress_name not in _ROUTE_CODE:
+        raise RuntimeError(f"Unsupported route compress {route_compress_name!r}")
+    batch_shape = src_val.shape[:-2]
+    n_src = src_val.shape[-2]
+    n_dst = dst_val.shape[-2]
+    out_dim = projected_val.shape[-1]
+    sv = _flatten_val(src_val)
+    dv = _flatten_val(dst_val)
+    k = min(int(topk), n_dst)
+    if k > _MAX_K:
+        raise RuntimeError(f"b200_sm100a top-k supports k <= {_MAX_K} (got {k}).")
+    src_proj, dst_proj, bias_t = _route_projections(route_kind, source_weight, source_bias, target_weight,
+                                                    target_bias, core_weight, bias, hidden_weight, hidden_bias,
+                                                    out_weight, out_bias, temperature, sv, dv)
+    pstate = _flatten_state(projected_state)
+    sender = _flatten_state(sender_strength).to(pstate.dtype)
+    pval = _flatten_val(projected_val)
+    B = sv.shape[0]
+    dev = sv.device
+    same = projected_state.dtype == projected_val.dtype
+    out_dtype = projected_val.dtype if same else torch.float32
+    accum = torch.empty(B * n_dst * (out_dim + 1) + 4, device=dev, dtype=torch.float32)
+    out_state = torch.empty((B, n_dst), device=dev, dtype=out_dtype)
+    out_val = torch.empty((B, n_dst, out_dim), device=dev, dtype=out_dtype)
+    with torch.cuda.device(dev):
+        check(
+            _LIBRARY.jk_transition_pairwise_topk_forward(
+                src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1], _proj_dtype(src_proj),
+                pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
+                pval.data_ptr(), out_dim, _dtype_code("val", pval),
+                k, 0.0, _ptr(bias_t), _ROUTE_CODE[route_compress_name], accum.data_ptr(),
+                out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state), _stream(dev)),
+            "jk_transition_pairwise_topk_forward",
+        )
+    return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
+            out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))

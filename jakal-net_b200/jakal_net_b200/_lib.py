@@ -1,0 +1,99 @@
+"""ctypes binding of libjakal_b200.so (the C ABI declared in include/jakal_b200.h).
+
+The library is built in-tree (``python jakal-net_b200/build.py``) and loaded from this
+package directory. There is no fallback: if the library is missing or a call fails, the
+error is raised to the caller.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_NAME = "libjakal_b200.so"
+LIB_PATH = Path(os.environ.get("JAKAL_B200_LIB", Path(__file__).resolve().parent / LIB_NAME))
+
+JK_OK = 0
+JK_ERR_BAD_SHAPE = -1
+JK_ERR_BAD_DTYPE = -2
+JK_ERR_UNSUPPORTED_KIND = -3
+JK_ERR_UNSUPPORTED_DEVICE = -4
+JK_ERR_LAUNCH = -5
+JK_ERR_DEVICE_TIMEOUT = -6
+JK_ERR_BAD_ARG = -7
+JK_ERR_ALIGNMENT = -8
+
+JK_F32, JK_BF16, JK_F16 = 0, 1, 2
+JK_SOFTSIGN, JK_SIGNED_ABS_SOFTMAX, JK_SIGNED_ENTMAX15, JK_SOFTMAX = 0, 1, 2, 3
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_f32 = ctypes.c_float
+
+# name -> (restype, argtypes); must list every symbol the header declares.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "jk_status_string": (ctypes.c_char_p, [_i32]),
+    "jk_device_check": (_i32, []),
+    "jk_device_status": (_i32, [_p, ctypes.POINTER(_i32)]),
+    "jk_padded_rank": (_i64, [_i64]),
+    "jk_lowrank_project": (_i32, [_p, _i64, _i64, _p, _i64, _p, _f32, _i32, _p, _i64, _p]),
+    "jk_propagation_topk_forward": (
+        _i32,
+        [_p, _p, _i64, _i64, _i64, _i64, _i32,  # row_proj, col_proj, B, n_rows, n_cols, rp, proj_dtype
+         _p, _p, _i32,                          # col_state, col_sender, state_dtype
+         _p, _i64, _i32,                        # col_val, dim, val_dtype
+         _i64, _i64, _f32, _p, _i32,            # k, window, score_bias, bias_dev, compress
+         _p, _p, _i32, _p, _p, _p],             # out_state, out_val, out_dtype, out_scores, out_index, stream
+    ),
+    "jk_transition_query_topk_forward": (
+        _i32,
+        [_p, _p, _i64, _i64, _i64, _i64, _i32,
+         _p, _p, _i32,
+         _p, _i64, _i32,
+         _i64, _f32, _p, _i32,
+         _p, _p, _i32, _p, _p, _p],
+    ),
+    "jk_transition_pairwise_topk_forward": (
+        _i32,
+        [_p, _p, _i64, _i64, _i64, _i64, _i32,
+         _p, _p, _i32,
+         _p, _i64, _i32,
+         _i64, _f32, _p, _i32,
+         _p, _p, _p, _i32, _p],
+    ),
+}
+
+_LIB: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library once and attaches the declared signatures."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_NAME} not found at {LIB_PATH}; build it with `python jakal-net_b200/build.py`"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _LIB = lib
+    return lib
+
+
+class JakalB200Error(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, status: int, where: str):
+        self.status = status
+        text = load().jk_status_string(status).decode()
+        super().__init__(f"{where}: {text} (status {status})")
+
+
+def check(status: int, where: str) -> None:
+    if status != JK_OK:
+        raise JakalB200Error(status, where)
