@@ -10,19 +10,21 @@
 //   * per-source transition    native/jakal_net_native_cuda.cu:740-878 (rows = sources,
 //                              softmax over the k picked destinations, scatter-add).
 //
-// Per CTA: 128 rows of one batch item.
-//   warp 4  (producer): TMA-loads the row-side projection tile once and streams the
+// Per CTA: 128 rows of one batch item, 9 warps.
+//   warp 8  (producer): TMA-loads the row-side projection tile once and streams the
 //           column-side tiles (128 columns x rp) through a multi-stage smem ring; issues
 //           tcgen05.mma (M=128 rows, N=128 columns, K=rp) into one of two TMEM
-//           accumulators, so the MMA of tile j+1 overlaps the epilogue of tile j.
-//   warps 0-3 (epilogue): thread i owns row i (TMEM lane i). It reads its 128 scores with
-//           tcgen05.ld, applies the visibility mask, and keeps a k-entry min-heap (root =
-//           current k-th best) in shared memory laid out [slot][thread] so every access
-//           is bank-conflict free. Candidates above the root are queued per thread and
-//           merged into the heap in warp-wide flushes, so lanes do not diverge per
-//           candidate. After the last tile the heap is sorted, compressed into edges, and
-//           each warp aggregates its 32 rows with 16-byte vector loads of the selected
-//           value rows (gather) or vector atomics into the destination rows (scatter).
+//           accumulators, so the MMA of tile j+1 overlaps the selection of tile j.
+//   warps 0-7 (selection): two threads per row (warps w and w+4 read the same TMEM lanes);
+//           each owns 64 of the 128 columns of every tile. A thread keeps a k-entry
+//           min-heap (root = its current k-th best) in shared memory laid out
+//           [slot][row] so every access is bank-conflict free. Candidates are filtered
+//           against max(own root, partner's published root) -- a valid lower bound of the
+//           row's k-th best -- queued per thread and merged into the heap in warp-wide
+//           flushes, so lanes do not diverge per candidate. After the last tile both heaps
+//           are sorted and merged, compressed into edges, and all 8 warps aggregate the
+//           128 rows with 16-byte vector loads of the picked value rows (gather) or vector
+//           atomics into the destination rows (scatter).
 #include "jk_host.h"
 #include "jk_sm100.cuh"
 
@@ -32,10 +34,27 @@
 namespace jk {
 namespace topk {
 
-constexpr int kRows = 128;     // rows per CTA (MMA M)
-constexpr int kCols = 128;     // columns per tile (MMA N)
-constexpr int kQueue = 8;      // per-thread candidate queue depth
-constexpr int kThreads = 160;  // 4 epilogue warps + 1 producer warp
+#ifdef JK_PHASE_PROFILE
+// Debug-only phase timer (sum over selection warps of clock64 deltas per phase).
+__device__ unsigned long long g_phase[8];
+#define JK_PHASE_MARK(i, t_prev)                                                                \
+  do {                                                                                         \
+    const long long _now = clock64();                                                          \
+    if ((threadIdx.x & 31) == 0) atomicAdd(&g_phase[i], (unsigned long long)(_now - (t_prev))); \
+    t_prev = _now;                                                                             \
+  } while (0)
+#else
+#define JK_PHASE_MARK(i, t_prev) \
+  do {                           \
+  } while (0)
+#endif
+
+constexpr int kRows = 128;       // rows per CTA (MMA M)
+constexpr int kCols = 128;       // columns per tile (MMA N)
+constexpr int kHalfCols = 64;    // columns per selection thread per tile
+constexpr int kQueue = 8;        // per-thread candidate queue depth
+constexpr int kSelWarps = 8;     // selection / aggregation warps
+constexpr int kThreads = (kSelWarps + 1) * 32;
 constexpr int kSentinel = INT_MAX;
 
 enum Mode { kGather = 0, kScatter = 1 };
@@ -57,7 +76,7 @@ struct Params {
   float* out_scores;
   int64_t* out_index;
   // scatter: f32 accumulators [B, n_cols] and [B, n_cols, dim]; the row side supplies
-  // state / value / sender (row_state etc.).
+  // state / value / sender (col_state / col_val / col_sender are indexed by the row).
   float* acc_state;
   float* acc_val;
 };
@@ -66,199 +85,166 @@ __device__ __forceinline__ bool worse(float av, int ai, float bv, int bi) {
   return av < bv || (av == bv && ai > bi);
 }
 
-struct Smem {
-  float* hv;  // [KMAX][128]
-  int* hi;    // [KMAX][128]
-  float* qv;  // [kQueue][128]
-  int* qi;    // [kQueue][128]
-  float* aux; // [KMAX][128]
-  int* nsel;  // [128]
+// One thread's slice of a [slot][row] array pair (stride kRows).
+struct Lane {
+  float* v;
+  int* i;
+  __device__ __forceinline__ float& val(int slot) const { return v[slot * kRows]; }
+  __device__ __forceinline__ int& idx(int slot) const { return i[slot * kRows]; }
 };
 
-// Sift (v, id) down from the root of the thread's heap of size k.
-__device__ __forceinline__ void heap_sift_root(const Smem& s, int tid, int k, float v, int id) {
+// Sift (x, id) down from the root of a min-heap of size n ("min" = worst).
+__device__ __forceinline__ void heap_sift_root(const Lane& h, int n, float x, int id) {
   int pos = 0;
   while (true) {
     int c = 2 * pos + 1;
-    if (c >= k) break;
-    float cv = s.hv[c * kRows + tid];
-    int ci = s.hi[c * kRows + tid];
-    if (c + 1 < k) {
-      const float rv = s.hv[(c + 1) * kRows + tid];
-      const int ri = s.hi[(c + 1) * kRows + tid];
-      if (worse(rv, ri, cv, ci)) { c = c + 1; cv = rv; ci = ri; }
+    if (c >= n) break;
+    float cv = h.val(c);
+    int ci = h.idx(c);
+    if (c + 1 < n) {
+      const float rv = h.val(c + 1);
+      const int ri = h.idx(c + 1);
+      if (worse(rv, ri, cv, ci)) {
+        c = c + 1;
+        cv = rv;
+        ci = ri;
+      }
     }
-    if (worse(cv, ci, v, id)) {
-      s.hv[pos * kRows + tid] = cv;
-      s.hi[pos * kRows + tid] = ci;
-      pos = c;
-    } else {
-      break;
-    }
+    if (!worse(cv, ci, x, id)) break;
+    h.val(pos) = cv;
+    h.idx(pos) = ci;
+    pos = c;
   }
-  s.hv[pos * kRows + tid] = v;
-  s.hi[pos * kRows + tid] = id;
+  h.val(pos) = x;
+  h.idx(pos) = id;
 }
 
-// Merge the queued candidates of this thread into its heap; returns the new threshold.
-__device__ __forceinline__ float flush_queue(const Smem& s, int tid, int k, int& qn) {
-  float root_v = s.hv[tid];
-  int root_i = s.hi[tid];
-  for (int q = 0; q < qn; ++q) {
-    const float v = s.qv[q * kRows + tid];
-    const int id = s.qi[q * kRows + tid];
-    if (worse(root_v, root_i, v, id)) {
-      heap_sift_root(s, tid, k, v, id);
-      root_v = s.hv[tid];
-      root_i = s.hi[tid];
+// Merges the queued candidates into the heap; returns the new root value.
+__device__ __forceinline__ float flush_queue(const Lane& h, const Lane& q, int k, int& qn) {
+  float root_v = h.val(0);
+  int root_i = h.idx(0);
+  for (int e = 0; e < qn; ++e) {
+    const float x = q.val(e);
+    const int id = q.idx(e);
+    if (worse(root_v, root_i, x, id)) {
+      heap_sift_root(h, k, x, id);
+      root_v = h.val(0);
+      root_i = h.idx(0);
     }
   }
   qn = 0;
   return root_v;
 }
 
-// In-place heapsort of the thread's min-heap -> entries sorted best first.
-__device__ __forceinline__ void heap_sort(const Smem& s, int tid, int k) {
+// In-place heapsort of a min-heap -> entries sorted best first.
+__device__ __forceinline__ void heap_sort(const Lane& h, int k) {
   for (int end = k - 1; end > 0; --end) {
-    const float v = s.hv[end * kRows + tid];
-    const int id = s.hi[end * kRows + tid];
-    s.hv[end * kRows + tid] = s.hv[tid];
-    s.hi[end * kRows + tid] = s.hi[tid];
-    heap_sift_root(s, tid, end, v, id);
+    const float x = h.val(end);
+    const int id = h.idx(end);
+    h.val(end) = h.val(0);
+    h.idx(end) = h.idx(0);
+    heap_sift_root(h, end, x, id);
   }
 }
 
-// Replaces hv[0..n) (sorted scores, bias included) by compressed edges.
-__device__ void compress_row(const Smem& s, int tid, int n, int compress) {
+__device__ __forceinline__ float sgn(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
+
+// Replaces f.val(0..n) (sorted scores, bias included) by compressed edges.
+__device__ void compress_row(const Lane& f, int n, int compress) {
   if (n <= 0) return;
   if (compress == JK_SOFTSIGN) {
-    for (int i = 0; i < n; ++i) {
-      const float x = s.hv[i * kRows + tid];
-      s.hv[i * kRows + tid] = x / (1.f + fabsf(x));
+    for (int e = 0; e < n; ++e) {
+      const float x = f.val(e);
+      f.val(e) = x / (1.f + fabsf(x));
     }
   } else if (compress == JK_SOFTMAX) {
-    const float m = s.hv[tid];  // sorted: first is the max
+    const float m = f.val(0);  // sorted: first is the max
     float z = 0.f;
-    for (int i = 0; i < n; ++i) z += expf(s.hv[i * kRows + tid] - m);
+    for (int e = 0; e < n; ++e) z += expf(f.val(e) - m);
     const float inv = 1.f / z;
-    for (int i = 0; i < n; ++i) s.hv[i * kRows + tid] = expf(s.hv[i * kRows + tid] - m) * inv;
+    for (int e = 0; e < n; ++e) f.val(e) = expf(f.val(e) - m) * inv;
   } else if (compress == JK_SIGNED_ABS_SOFTMAX) {
     float m = 0.f;
-    for (int i = 0; i < n; ++i) m = fmaxf(m, fabsf(s.hv[i * kRows + tid]));
+    for (int e = 0; e < n; ++e) m = fmaxf(m, fabsf(f.val(e)));
     float z = 0.f;
-    for (int i = 0; i < n; ++i) z += expf(fabsf(s.hv[i * kRows + tid]) - m);
+    for (int e = 0; e < n; ++e) z += expf(fabsf(f.val(e)) - m);
     const float inv = 1.f / z;
-    for (int i = 0; i < n; ++i) {
-      const float x = s.hv[i * kRows + tid];
-      const float sg = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
-      s.hv[i * kRows + tid] = sg * expf(fabsf(x) - m) * inv;
+    for (int e = 0; e < n; ++e) {
+      const float x = f.val(e);
+      f.val(e) = sgn(x) * expf(fabsf(x) - m) * inv;
     }
-  } else {  // JK_SIGNED_ENTMAX15 over |s| (kernels.py:155-210 restated)
-    // Magnitudes sorted descending by insertion sort into aux.
-    for (int i = 0; i < n; ++i) {
-      const float a = fabsf(s.hv[i * kRows + tid]);
-      int j = i;
-      while (j > 0 && s.aux[(j - 1) * kRows + tid] < a) {
-        s.aux[j * kRows + tid] = s.aux[(j - 1) * kRows + tid];
-        --j;
+  } else {
+    // sign(s) * entmax15(|s|) (kernels.py:155-236). z = (|s| - max|s|) / 2; the threshold
+    // tau solves sum_{z_j > tau} (z_j - tau)^2 = 1. The reference finds the support by
+    // sorting; here the support is found by the equivalent fixed-point iteration (start
+    // from all entries, drop those at or below tau, recompute) with the same closed form
+    // tau = mean - sqrt(max(0, (1 - rho * (mean_sq - mean^2)) / rho)) over the support.
+    float zmax = 0.f;
+    for (int e = 0; e < n; ++e) zmax = fmaxf(zmax, fabsf(f.val(e)));
+    float tau = -INFINITY;
+    for (int iter = 0; iter < n + 1; ++iter) {
+      float sum = 0.f, sum_sq = 0.f;
+      int rho = 0;
+      for (int e = 0; e < n; ++e) {
+        const float z = (fabsf(f.val(e)) - zmax) * 0.5f;
+        if (z > tau || iter == 0) {
+          sum += z;
+          sum_sq += z * z;
+          ++rho;
+        }
       }
-      s.aux[j * kRows + tid] = a;
+      const float r = static_cast<float>(rho);
+      const float mean = sum / r;
+      const float mean_sq = sum_sq / r;
+      const float delta = fmaxf((1.f - r * (mean_sq - mean * mean)) / r, 0.f);
+      const float next = mean - sqrtf(delta);
+      if (iter > 0 && next == tau) break;
+      tau = next;
     }
-    const float zmax = s.aux[tid];
-    // tau_rho for rho = 1..n on shifted = (z - zmax) / 2; support = #{rho : tau_rho <= z_rho}.
-    float cum = 0.f, cum_sq = 0.f, tau_star = 0.f;
-    int support = 0;
-    float tau_first = 0.f;
-    for (int r = 0; r < n; ++r) {
-      const float x = (s.aux[r * kRows + tid] - zmax) * 0.5f;
-      cum += x;
-      cum_sq += x * x;
-      const float rho = static_cast<float>(r + 1);
-      const float mean = cum / rho;
-      const float mean_sq = cum_sq / rho;
-      const float var = rho * (mean_sq - mean * mean);
-      const float delta = fmaxf((1.f - var) / rho, 0.f);
-      const float tau = mean - sqrtf(delta);
-      if (r == 0) tau_first = tau;
-      if (tau <= x) { ++support; tau_star = tau; }
+    float z_sum = 0.f;
+    for (int e = 0; e < n; ++e) {
+      const float pz = fmaxf((fabsf(f.val(e)) - zmax) * 0.5f - tau, 0.f);
+      z_sum += pz * pz;
     }
-    // torch: tau.gather(support - 1) with support >= 1 -> tau at index (support-1).
-    // Recompute tau at that rho exactly as the reference (cumulative formula).
-    if (support == 0) tau_star = tau_first;
-    else {
-      cum = 0.f; cum_sq = 0.f;
-      for (int r = 0; r < support; ++r) {
-        const float x = (s.aux[r * kRows + tid] - zmax) * 0.5f;
-        cum += x;
-        cum_sq += x * x;
-      }
-      const float rho = static_cast<float>(support);
-      const float mean = cum / rho;
-      const float mean_sq = cum_sq / rho;
-      const float var = rho * (mean_sq - mean * mean);
-      const float delta = fmaxf((1.f - var) / rho, 0.f);
-      tau_star = mean - sqrtf(delta);
-    }
-    float z = 0.f;
-    for (int i = 0; i < n; ++i) {
-      const float x = (fabsf(s.hv[i * kRows + tid]) - zmax) * 0.5f;
-      const float pv = fmaxf(x - tau_star, 0.f);
-      z += pv * pv;
-    }
-    const float inv = z > 0.f ? 1.f / fmaxf(z, FLT_EPSILON) : 0.f;
-    for (int i = 0; i < n; ++i) {
-      const float x = s.hv[i * kRows + tid];
-      const float sh = (fabsf(x) - zmax) * 0.5f;
-      const float pv = fmaxf(sh - tau_star, 0.f);
-      const float sg = x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f);
-      s.hv[i * kRows + tid] = sg * pv * pv * inv;
+    const float inv = z_sum > 0.f ? 1.f / fmaxf(z_sum, FLT_EPSILON) : 0.f;
+    for (int e = 0; e < n; ++e) {
+      const float x = f.val(e);
+      const float pz = fmaxf((fabsf(x) - zmax) * 0.5f - tau, 0.f);
+      f.val(e) = sgn(x) * pz * pz * inv;
     }
   }
 }
 
-template <typename T>
-struct Vec8;  // 16-byte vector of T loaded and widened to float
+// ---------------------------------------------------------------- value loads / stores
+template <typename VT>
+__device__ __forceinline__ void widen8(const uint4& u, float (&f)[8]);
 
 template <>
-struct Vec8<__nv_bfloat16> {
-  static constexpr int kElems = 8;
-  __device__ __forceinline__ static void load(const void* base, int64_t elem, float (&f)[8]) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + elem));
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+__device__ __forceinline__ void widen8<__nv_bfloat16>(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 t = __bfloat1622float2(h[i]);
-      f[2 * i] = t.x;
-      f[2 * i + 1] = t.y;
-    }
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
   }
-};
+}
 
 template <>
-struct Vec8<__half> {
-  static constexpr int kElems = 8;
-  __device__ __forceinline__ static void load(const void* base, int64_t elem, float (&f)[8]) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(base) + elem));
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
+__device__ __forceinline__ void widen8<__half>(const uint4& u, float (&f)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 t = __half22float2(h[i]);
-      f[2 * i] = t.x;
-      f[2 * i + 1] = t.y;
-    }
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
   }
-};
+}
 
 template <>
-struct Vec8<float> {
-  static constexpr int kElems = 8;
-  __device__ __forceinline__ static void load(const void* base, int64_t elem, float (&f)[8]) {
-    const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + elem);
-    const float4 a = __ldg(q), b = __ldg(q + 1);
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-  }
-};
+__device__ __forceinline__ void widen8<float>(const uint4&, float (&f)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = 0.f;  // f32 values take the generic path
+}
 
 __device__ __forceinline__ void store8(void* base, int64_t elem, int dtype, const float (&f)[8]) {
   if (dtype == JK_F32) {
@@ -280,84 +266,125 @@ __device__ __forceinline__ void store8(void* base, int64_t elem, int dtype, cons
   }
 }
 
-// Gather-aggregate of one row by one warp: out[row] = sum_i w_i * val[idx_i].
+// Generic aggregation of one row by one warp (any dim / f32 values): lanes stride the
+// value dimension; the final weights already include the sender strength.
+__device__ void gather_row_generic(const Lane& f, int n, int64_t col_base, int64_t row, const Params& p, int lane) {
+  const int64_t D = p.dim;
+  for (int64_t d0 = 0; d0 < D; d0 += 32) {
+    const int64_t d = d0 + lane;
+    float acc = 0.f;
+    for (int e = 0; e < n; ++e) {
+      const int j = f.idx(e);
+      if (d < D) acc = fmaf(f.val(e), ld_elem(p.col_val, (col_base + j) * D + d, p.val_dtype), acc);
+    }
+    if (d < D) st_elem(p.out_val, row * D + d, p.out_dtype, acc);
+  }
+}
+
+// Aggregation of `nrows` rows (tile rows rt0 ..) by one warp for 16-bit values.
+//
+// Work items are (row, 8-element chunk) pairs of a group of rows spread over the 32
+// lanes, so every lane keeps up to 16 independent 16-byte loads in flight per step (8
+// items x 2 neighbours) whatever the value width, which hides the L2 / HBM latency of the
+// random gathers. Accumulation is f32; each item is stored once.
 template <typename VT>
-__device__ void gather_row(const Smem& s, int col_tid, int n, int64_t b, int64_t row,
-                           const Params& p, int lane) {
+__device__ void gather_warp(float* fv, int* fi, int* nsel, int rt0, int nrows, int64_t t0, int64_t b,
+                            const Params& p, int lane) {
+  constexpr int kItems = 8;
   const int64_t D = p.dim;
   const int64_t col_base = b * p.n_cols;
-  float acc_state = 0.f;
-  const bool vec = (D % 8) == 0;
-  if (vec && D <= 1024) {
-    const int nch = static_cast<int>(D / 8);
-    float acc[4][8];
+  if ((D % 8) != 0 || D > 8 * 32 * kItems || sizeof(VT) == 4) {
+    for (int r = 0; r < nrows; ++r) {
+      const int rt = rt0 + r;
+      const int64_t row = t0 + rt;
+      if (row >= p.n_rows) break;
+      gather_row_generic(Lane{fv + rt, fi + rt}, nsel[rt], col_base, b * p.n_rows + row, p, lane);
+    }
+    return;
+  }
+  const VT* vbase = reinterpret_cast<const VT*>(p.col_val) + col_base * D;
+  const int nch = static_cast<int>(D / 8);
+  int rg = (32 * kItems) / nch;
+  if (rg < 1) rg = 1;
+  for (int g0 = 0; g0 < nrows; g0 += rg) {
+    int rq[kItems], nq[kItems], off[kItems];
+    float acc[kItems][8];
+    int kmax = 0;
 #pragma unroll
-    for (int m = 0; m < 4; ++m)
+    for (int m = 0; m < kItems; ++m) {
+      const int it = lane + 32 * m;
+      const int r = g0 + it / nch;
+      const bool act = it < rg * nch && r < nrows && t0 + rt0 + r < p.n_rows;
+      rq[m] = rt0 + (act ? r : 0);
+      off[m] = (it % nch) * 8;
+      nq[m] = act ? nsel[rt0 + r] : 0;
+      kmax = nq[m] > kmax ? nq[m] : kmax;
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[m][e] = 0.f;
-    for (int i = 0; i < n; ++i) {
-      const int j = s.hi[i * kRows + col_tid];
-      float w = s.hv[i * kRows + col_tid];
-      if (p.col_sender) w *= ld_elem(p.col_sender, col_base + j, p.state_dtype);
-      if (lane == 0) acc_state += w * ld_elem(p.col_state, col_base + j, p.state_dtype);
-      const int64_t rbase = (col_base + j) * D;
+    }
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    for (int i = 0; i < kmax; i += 2) {
+      uint4 raw[kItems][2];
+      float w[kItems][2];
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int c = lane + 32 * m;
-        if (c < nch) {
-          float f[8];
-          Vec8<VT>::load(p.col_val, rbase + c * 8, f);
+      for (int m = 0; m < kItems; ++m) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[m][e] = fmaf(w, f[e], acc[m][e]);
+        for (int u = 0; u < 2; ++u) {
+          const bool on = i + u < nq[m];
+          const int slot = (on ? i + u : 0) * kRows + rq[m];
+          const int j = fi[slot];
+          w[m][u] = on ? fv[slot] : 0.f;
+          raw[m][u] = on ? __ldg(reinterpret_cast<const uint4*>(vbase + static_cast<int64_t>(j) * D + off[m]))
+                         : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < kItems; ++m) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          float x[8];
+          widen8<VT>(raw[m][u], x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[m][e] = fmaf(w[m][u], x[e], acc[m][e]);
         }
       }
     }
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int c = lane + 32 * m;
-      if (c < nch) store8(p.out_val, row * D + c * 8, p.out_dtype, acc[m]);
-    }
-  } else {
-    // Generic path: any dim, one element per lane per step.
-    for (int64_t d0 = 0; d0 < D; d0 += 32) {
-      const int64_t d = d0 + lane;
-      float acc = 0.f;
-      for (int i = 0; i < n; ++i) {
-        const int j = s.hi[i * kRows + col_tid];
-        float w = s.hv[i * kRows + col_tid];
-        if (p.col_sender) w *= ld_elem(p.col_sender, col_base + j, p.state_dtype);
-        if (d0 == 0 && lane == 0) acc_state += w * ld_elem(p.col_state, col_base + j, p.state_dtype);
-        if (d < D) acc = fmaf(w, ld_elem(p.col_val, (col_base + j) * D + d, p.val_dtype), acc);
+    for (int m = 0; m < kItems; ++m) {
+      const int it = lane + 32 * m;
+      const int r = g0 + it / nch;
+      if (it < rg * nch && r < nrows && t0 + rt0 + r < p.n_rows) {
+        const int64_t row = b * p.n_rows + t0 + rt0 + r;
+        store8(p.out_val, row * D + off[m], p.out_dtype, acc[m]);
       }
-      if (d < D) st_elem(p.out_val, row * D + d, p.out_dtype, acc);
     }
   }
-  if (lane == 0) st_elem(p.out_state, row, p.out_dtype, acc_state);
 }
 
 // Scatter of one source row by one warp into the f32 destination accumulators.
 template <typename VT>
-__device__ void scatter_row(const Smem& s, int col_tid, int n, int64_t b, int64_t src,
-                            const Params& p, int lane) {
-  // In scatter mode the "row side" is the source: state / value / sender are indexed by
-  // the row, destinations are the selected columns.
+__device__ void scatter_row(const Lane& f, int n, int64_t b, int64_t src, const Params& p, int lane) {
   const int64_t D = p.dim;
   float sender = 1.f;
   if (p.col_sender) sender = ld_elem(p.col_sender, src, p.state_dtype);
   const float sstate = ld_elem(p.col_state, src, p.state_dtype);
-  const bool vec = (D % 8) == 0 && D <= 1024;
+  const bool vec = (D % 8) == 0 && D <= 1024 && sizeof(VT) == 2;
   const int nch = static_cast<int>(D / 8);
   float v[4][8];
   if (vec) {
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
       const int c = lane + 32 * m;
-      if (c < nch) Vec8<VT>::load(p.col_val, src * D + c * 8, v[m]);
+      if (c < nch) {
+        const uint4 u =
+            __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const VT*>(p.col_val) + src * D + c * 8));
+        widen8<VT>(u, v[m]);
+      }
     }
   }
-  for (int i = 0; i < n; ++i) {
-    const int j = s.hi[i * kRows + col_tid];
-    const float w = s.hv[i * kRows + col_tid] * sender;
+  for (int e = 0; e < n; ++e) {
+    const int j = f.idx(e);
+    const float w = f.val(e) * sender;
     const int64_t dst = b * p.n_cols + j;
     if (lane == 0) atomicAdd(p.acc_state + dst, w * sstate);
     if (vec) {
@@ -378,26 +405,44 @@ __device__ void scatter_row(const Smem& s, int col_tid, int n, int64_t b, int64_
   }
 }
 
+__device__ __forceinline__ void sel_barrier() {
+  asm volatile("bar.sync 1, %0;" ::"r"(kSelWarps * 32) : "memory");
+}
+
+template <int KMAX, int KATOMS, int STAGES>
+struct Layout {
+  static constexpr int kAtomBytes = kRows * 128;  // 128 rows x 64 (16-bit) elements
+  static constexpr int kABytes = KATOMS * kAtomBytes;
+  static constexpr int kBBytes = KATOMS * kAtomBytes;
+  static constexpr int kRegion0 = kABytes + STAGES * kBBytes;  // A + ring; reused for the final lists
+  static constexpr int kFinalBytes = 2 * KMAX * kRows * 4;
+  static_assert(kFinalBytes <= kRegion0, "final lists must fit in the MMA operand region");
+  static constexpr int kHeapBytes = 2 * 2 * KMAX * kRows * 4;  // 2 halves x (value, index)
+  static constexpr int kQueueBytes = 2 * 2 * kQueue * kRows * 4;
+  static constexpr int kPubBytes = 2 * kRows * 4;
+  static constexpr int kNselBytes = kRows * 4;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kTotal = 1024 + kRegion0 + kHeapBytes + kQueueBytes + kPubBytes + kNselBytes + kBarBytes;
+};
+
 template <int KMAX, int KATOMS, int STAGES, int MODE, typename VT>
 __global__ void __launch_bounds__(kThreads, 1)
     topk_kernel(const __grid_constant__ CUtensorMap tm_rows, const __grid_constant__ CUtensorMap tm_cols,
                 Params p, uint32_t idesc) {
+  using L = Layout<KMAX, KATOMS, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kAtomBytes = kRows * 128;  // 128 rows x 64 (16-bit) elements
-  constexpr int kABytes = KATOMS * kAtomBytes;
-  constexpr int kBBytes = KATOMS * kAtomBytes;
   uint8_t* a_tile = smem;
-  uint8_t* b_ring = smem + kABytes;
-  uint8_t* tail = b_ring + STAGES * kBBytes;
-  Smem s;
-  s.hv = reinterpret_cast<float*>(tail);
-  s.hi = reinterpret_cast<int*>(s.hv + KMAX * kRows);
-  s.qv = reinterpret_cast<float*>(s.hi + KMAX * kRows);
-  s.qi = reinterpret_cast<int*>(s.qv + kQueue * kRows);
-  s.aux = reinterpret_cast<float*>(s.qi + kQueue * kRows);
-  s.nsel = reinterpret_cast<int*>(s.aux + KMAX * kRows);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s.nsel + kRows);
+  uint8_t* b_ring = smem + L::kABytes;
+  float* fv = reinterpret_cast<float*>(smem);  // final lists (after streaming)
+  int* fi = reinterpret_cast<int*>(fv + KMAX * kRows);
+  float* hv = reinterpret_cast<float*>(smem + L::kRegion0);  // [2][KMAX][kRows]
+  int* hi = reinterpret_cast<int*>(hv + 2 * KMAX * kRows);
+  float* qv = reinterpret_cast<float*>(hi + 2 * KMAX * kRows);  // [2][kQueue][kRows]
+  int* qi = reinterpret_cast<int*>(qv + 2 * kQueue * kRows);
+  volatile float* pub = reinterpret_cast<volatile float*>(qi + 2 * kQueue * kRows);  // [2][kRows]
+  int* nsel = reinterpret_cast<int*>(const_cast<float*>(pub) + 2 * kRows);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(nsel + kRows);
   uint64_t* bar_a = bars;
   uint64_t* full = bars + 1;
   uint64_t* empty = full + STAGES;
@@ -417,9 +462,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (p.window >= 0) {
     const int64_t lo = t0 - p.window;
     j_lo = lo > 0 ? lo / kCols : 0;
-    int64_t hi = t0 + kRows - 1;
-    if (hi > p.n_cols - 1) hi = p.n_cols - 1;
-    j_hi = hi < 0 ? -1 : hi / kCols;
+    int64_t hi_col = t0 + kRows - 1;
+    if (hi_col > p.n_cols - 1) hi_col = p.n_cols - 1;
+    j_hi = hi_col < 0 ? -1 : hi_col / kCols;
   }
   const int ntiles = j_hi >= j_lo ? static_cast<int>(j_hi - j_lo + 1) : 0;
 
@@ -431,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], kSelWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -442,23 +487,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kSelWarps) {
     // ------------------------------------------------------------ producer / MMA issuer
     if (lane == 0 && ntiles > 0) {
       prefetch_tmap(&tm_rows);
       prefetch_tmap(&tm_cols);
       bool ok = true;
-      mbar_arrive_expect_tx(bar_a, kABytes);
+      mbar_arrive_expect_tx(bar_a, L::kABytes);
 #pragma unroll
       for (int a = 0; a < KATOMS; ++a)
-        tma_load_3d(a_tile + a * kAtomBytes, &tm_rows, bar_a, a * 64, static_cast<int>(t0), static_cast<int>(b));
+        tma_load_3d(a_tile + a * L::kAtomBytes, &tm_rows, bar_a, a * 64, static_cast<int>(t0), static_cast<int>(b));
       const int pre = ntiles < STAGES ? ntiles : STAGES;
       for (int it = 0; it < pre; ++it) {
-        mbar_arrive_expect_tx(&full[it], kBBytes);
+        mbar_arrive_expect_tx(&full[it], L::kBBytes);
         const int col0 = static_cast<int>((j_lo + it) * kCols);
 #pragma unroll
         for (int a = 0; a < KATOMS; ++a)
-          tma_load_3d(b_ring + it * kBBytes + a * kAtomBytes, &tm_cols, &full[it], a * 64, col0, static_cast<int>(b));
+          tma_load_3d(b_ring + it * L::kBBytes + a * L::kAtomBytes, &tm_cols, &full[it], a * 64, col0,
+                      static_cast<int>(b));
       }
       ok = mbar_wait(bar_a, 0);
       for (int it = 0; it < ntiles && ok; ++it) {
@@ -469,24 +515,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (*abort_flag) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_addr = smem_u32(a_tile);
-        const uint32_t b_addr = smem_u32(b_ring + st * kBBytes);
+        const uint32_t b_addr = smem_u32(b_ring + st * L::kBBytes);
 #pragma unroll
         for (int kk = 0; kk < 4 * KATOMS; ++kk) {
-          const uint32_t off = (kk >> 2) * kAtomBytes + (kk & 3) * 32;
-          mma_f16_ss(tmem + buf * kCols, sdesc_kmajor_sw128(a_addr + off), sdesc_kmajor_sw128(b_addr + off),
-                     idesc, kk > 0 ? 1u : 0u);
+          const uint32_t off = (kk >> 2) * L::kAtomBytes + (kk & 3) * 32;
+          mma_f16_ss(tmem + buf * kCols, sdesc_kmajor_sw128(a_addr + off), sdesc_kmajor_sw128(b_addr + off), idesc,
+                     kk > 0 ? 1u : 0u);
         }
         mma_commit(&empty[st]);
         mma_commit(&tfull[buf]);
-        const int ip = it - 1;
+        // Refill the stage the previous tile used (its MMA has most likely retired); with a
+        // single stage, the stage of this tile once its own MMA retires.
+        const int ip = STAGES == 1 ? it : it - 1;
         if (ip >= 0 && ip + STAGES < ntiles) {
           const int sp = ip % STAGES;
           if (!mbar_wait(&empty[sp], (ip / STAGES) & 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[sp], kBBytes);
+          mbar_arrive_expect_tx(&full[sp], L::kBBytes);
           const int col0 = static_cast<int>((j_lo + ip + STAGES) * kCols);
 #pragma unroll
           for (int a = 0; a < KATOMS; ++a)
-            tma_load_3d(b_ring + sp * kBBytes + a * kAtomBytes, &tm_cols, &full[sp], a * 64, col0, static_cast<int>(b));
+            tma_load_3d(b_ring + sp * L::kBBytes + a * L::kAtomBytes, &tm_cols, &full[sp], a * 64, col0,
+                        static_cast<int>(b));
         }
       }
       // The MMA-retire arrivals on the ring barriers must land before the CTA exits.
@@ -500,9 +549,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue warps
-    const int tid = threadIdx.x;  // 0..127 == TMEM lane == row in tile
-    const int64_t t = t0 + tid;
+    // ------------------------------------------------------------ selection warps
+    const int quad = warp & 3;
+    const int half = warp >> 2;
+    const int row = quad * 32 + lane;  // TMEM lane == row in tile
+    const int64_t t = t0 + row;
     const bool row_ok = t < p.n_rows;
     // Visible columns of this row: [lo_t, hi_t] (32-bit; sizes are capped at 2^30).
     int lo_t = 0, hi_t = static_cast<int>(p.n_cols - 1);
@@ -511,20 +562,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       lo_t = lo < 0 ? 0 : static_cast<int>(lo);
       hi_t = t < hi_t ? static_cast<int>(t) : hi_t;
     }
-    if (!row_ok || hi_t < lo_t) {
-      // Nothing visible: an unreachable single-column range.
+    if (!row_ok || hi_t < lo_t) {  // nothing visible: an unreachable single-column range
       lo_t = INT_MAX / 2;
       hi_t = INT_MAX / 2;
     }
     const uint32_t span = static_cast<uint32_t>(hi_t - lo_t);
-    for (int i = 0; i < k; ++i) {
-      s.hv[i * kRows + tid] = -INFINITY;
-      s.hi[i * kRows + tid] = kSentinel;
+    const Lane heap{hv + half * KMAX * kRows + row, hi + half * KMAX * kRows + row};
+    const Lane queue{qv + half * kQueue * kRows + row, qi + half * kQueue * kRows + row};
+    for (int e = 0; e < k; ++e) {
+      heap.val(e) = -INFINITY;
+      heap.idx(e) = kSentinel;
     }
-    float thr = -INFINITY;
+    pub[half * kRows + row] = -INFINITY;
+    float thr_own = -INFINITY, thr_part = -INFINITY;
     int qn = 0;
     bool ok = true;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tbase = (static_cast<uint32_t>(quad * 32) << 16) + half * kHalfCols;
+#ifdef JK_PHASE_PROFILE
+    long long t_prev = clock64();
+#endif
+    sel_barrier();  // heaps and published roots initialised
     for (int it = 0; it < ntiles; ++it) {
       const int buf = it & 1;
       if (!mbar_wait(&tfull[buf], (it >> 1) & 1) || *abort_flag) {
@@ -532,70 +589,123 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t v[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_base + buf * kCols + c * 32, v[c]);
+      uint32_t v[2][32];
+      tmem_ld_32x32b_x32(tmem + tbase + buf * kCols, v[0]);
+      tmem_ld_32x32b_x32(tmem + tbase + buf * kCols + 32, v[1]);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
-      const int col0 = static_cast<int>((j_lo + it) * kCols);
+      const int col0 = static_cast<int>((j_lo + it) * kCols) + half * kHalfCols;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int col = col0 + c * 32 + e + u;
             const float x = __uint_as_float(v[c][e + u]);
-            const bool vis = static_cast<uint32_t>(col - lo_t) <= span;
-            if (vis && x > thr) {
-              s.qv[qn * kRows + tid] = x;
-              s.qi[qn * kRows + tid] = col;
+            const bool pass = static_cast<uint32_t>(col - lo_t) <= span && x > thr_own && x >= thr_part;
+            if (pass) {
+              queue.val(qn) = x;
+              queue.idx(qn) = col;
               ++qn;
             }
           }
-          if (__any_sync(0xffffffffu, qn > kQueue - 4)) thr = flush_queue(s, tid, k, qn);
+          if (__any_sync(0xffffffffu, qn > kQueue - 4)) {
+            thr_own = flush_queue(heap, queue, k, qn);
+            pub[half * kRows + row] = thr_own;
+            thr_part = pub[(half ^ 1) * kRows + row];
+          }
         }
       }
     }
     if (ok) {
-      thr = flush_queue(s, tid, k, qn);
-      heap_sort(s, tid, k);
-      int n = 0;
-      while (n < k && s.hi[n * kRows + tid] != kSentinel) ++n;
-      // Scores (bias added after selection; constant per op so the selection is unchanged).
-      const float bias = p.bias + (p.bias_dev ? __ldg(p.bias_dev) : 0.f);
-      for (int i = 0; i < n; ++i) s.hv[i * kRows + tid] += bias;
-      if (MODE == kGather && row_ok && (p.out_scores || p.out_index)) {
-        const int64_t o = (b * p.n_rows + t) * k;
-        for (int i = 0; i < k; ++i) {
-          if (p.out_scores) p.out_scores[o + i] = i < n ? s.hv[i * kRows + tid] : -INFINITY;
-          if (p.out_index) p.out_index[o + i] = i < n ? static_cast<int64_t>(s.hi[i * kRows + tid]) : -1;
-        }
-      }
-      compress_row(s, tid, n, p.compress);
-      s.nsel[tid] = row_ok ? n : 0;
-    } else {
-      s.nsel[tid] = 0;
+      flush_queue(heap, queue, k, qn);
+      JK_PHASE_MARK(0, t_prev);
+      heap_sort(heap, k);
+    }
+    sel_barrier();  // both halves sorted; MMA operand region is free
+    JK_PHASE_MARK(1, t_prev);
+    if (!ok) {
       atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
       *abort_flag = 1;
     }
-    __syncwarp();
-    if (ok) {
-      // Aggregate: warp w handles rows 32w .. 32w+31.
-      for (int r = 0; r < 32; ++r) {
-        const int rt = warp * 32 + r;
-        const int64_t row = t0 + rt;
-        if (row >= p.n_rows) break;
-        const int n = s.nsel[rt];
-        if (MODE == kGather) {
-          gather_row<VT>(s, rt, n, b, b * p.n_rows + row, p, lane);
-        } else {
-          scatter_row<VT>(s, rt, n, b, b * p.n_rows + row, p, lane);
+    sel_barrier();
+    const bool good = !*abort_flag;
+    if (half == 0) {
+      // Merge the two sorted halves (best first, ties to the lower column) into the
+      // final list, compress it, fold in the sender strength and form the state output.
+      const Lane A{hv + row, hi + row};
+      const Lane Bh{hv + KMAX * kRows + row, hi + KMAX * kRows + row};
+      const Lane F{fv + row, fi + row};
+      int ia = 0, ib = 0, n = 0;
+      if (good && row_ok) {
+        while (n < k) {
+          const float av = ia < k ? A.val(ia) : -INFINITY;
+          const float bv = ib < k ? Bh.val(ib) : -INFINITY;
+          const int ai = ia < k ? A.idx(ia) : kSentinel;
+          const int bi = ib < k ? Bh.idx(ib) : kSentinel;
+          const bool take_a = worse(bv, bi, av, ai);
+          const int id = take_a ? ai : bi;
+          if (id == kSentinel) break;
+          F.val(n) = take_a ? av : bv;
+          F.idx(n) = id;
+          ++n;
+          if (take_a) ++ia; else ++ib;
+        }
+      }
+      const float bias = p.bias + (p.bias_dev ? __ldg(p.bias_dev) : 0.f);
+      for (int e = 0; e < n; ++e) F.val(e) += bias;
+      if (MODE == kGather && row_ok && good && (p.out_scores || p.out_index)) {
+        const int64_t o = (b * p.n_rows + t) * k;
+        for (int e = 0; e < k; ++e) {
+          if (p.out_scores) p.out_scores[o + e] = e < n ? F.val(e) : -INFINITY;
+          if (p.out_index) p.out_index[o + e] = e < n ? static_cast<int64_t>(F.idx(e)) : -1;
+        }
+      }
+      compress_row(F, n, p.compress);
+      if (MODE == kGather && row_ok && good) {
+        const int64_t cb = b * p.n_cols;
+        float acc = 0.f;
+        for (int e0 = 0; e0 < n; e0 += 8) {
+          float st[8], sn[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const bool on = e0 + u < n;
+            const int j = on ? F.idx(e0 + u) : 0;
+            st[u] = on ? ld_elem(p.col_state, cb + j, p.state_dtype) : 0.f;
+            sn[u] = (on && p.col_sender) ? ld_elem(p.col_sender, cb + j, p.state_dtype) : 1.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            if (e0 + u < n) {
+              const float w = F.val(e0 + u) * sn[u];
+              F.val(e0 + u) = w;
+              acc = fmaf(w, st[u], acc);
+            }
+          }
+        }
+        st_elem(p.out_state, b * p.n_rows + t, p.out_dtype, acc);
+      }
+      nsel[row] = n;
+    }
+    sel_barrier();  // final lists ready
+    JK_PHASE_MARK(2, t_prev);
+    if (good) {
+      // Aggregate: warp w handles rows 16w .. 16w+15.
+      const int rt0 = warp * (kRows / kSelWarps);
+      if (MODE == kGather) {
+        gather_warp<VT>(fv, fi, nsel, rt0, kRows / kSelWarps, t0, b, p, lane);
+      } else {
+        for (int r = 0; r < kRows / kSelWarps; ++r) {
+          const int rt = rt0 + r;
+          if (t0 + rt >= p.n_rows) break;
+          scatter_row<VT>(Lane{fv + rt, fi + rt}, nsel[rt], b, b * p.n_rows + t0 + rt, p, lane);
         }
       }
     }
+    JK_PHASE_MARK(3, t_prev);
     tc_fence_before();
   }
   __syncthreads();
@@ -605,15 +715,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int KMAX, int KATOMS, int STAGES>
-constexpr int smem_bytes() {
-  return 1024 + (1 + STAGES) * KATOMS * kRows * 128 + (2 * KMAX + 2 * kQueue + KMAX) * kRows * 4 + kRows * 4 +
-         256;
-}
-
 // Converts the f32 destination accumulators of the scatter mode into the outputs.
-__global__ void finalize_scatter(const float* acc_state, const float* acc_val, int64_t n_state,
-                                 int64_t n_val, void* out_state, void* out_val, int out_dtype) {
+__global__ void finalize_scatter(const float* acc_state, const float* acc_val, int64_t n_state, int64_t n_val,
+                                 void* out_state, void* out_val, int out_dtype) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t j = i; j < n_val; j += stride) st_elem(out_val, j, out_dtype, acc_val[j]);
@@ -621,21 +725,24 @@ __global__ void finalize_scatter(const float* acc_state, const float* acc_val, i
 }
 
 template <int KMAX, int KATOMS, int MODE, typename VT>
-int launch_vt(const CUtensorMap& tr, const CUtensorMap& tc, const Params& p, int64_t batch,
-              uint32_t idesc, cudaStream_t st) {
-  constexpr int STAGES = KATOMS == 1 ? 4 : 2;
-  constexpr int sm = smem_bytes<KMAX, KATOMS, STAGES>();
+int launch_vt(const CUtensorMap& tr, const CUtensorMap& tc, const Params& p, int64_t batch, uint32_t idesc,
+              cudaStream_t st) {
+  constexpr int STAGES = KATOMS == 1 ? (KMAX > 32 ? 3 : 4) : (KMAX > 32 ? 1 : 2);
+  constexpr int sm = Layout<KMAX, KATOMS, STAGES>::kTotal;
+  static_assert(sm <= 232448, "shared memory budget");
   auto kern = topk_kernel<KMAX, KATOMS, STAGES, MODE, VT>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess)
-    return launch_status() == JK_OK ? JK_ERR_LAUNCH : JK_ERR_LAUNCH;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) {
+    cudaGetLastError();
+    return JK_ERR_LAUNCH;
+  }
   const dim3 grid(static_cast<unsigned>((p.n_rows + kRows - 1) / kRows), static_cast<unsigned>(batch));
   kern<<<grid, kThreads, sm, st>>>(tr, tc, p, idesc);
   return launch_status();
 }
 
 template <int KMAX, int KATOMS, int MODE>
-int launch_k(const CUtensorMap& tr, const CUtensorMap& tc, const Params& p, int64_t batch,
-             uint32_t idesc, cudaStream_t st) {
+int launch_k(const CUtensorMap& tr, const CUtensorMap& tc, const Params& p, int64_t batch, uint32_t idesc,
+             cudaStream_t st) {
   switch (p.val_dtype) {
     case JK_F32: return launch_vt<KMAX, KATOMS, MODE, float>(tr, tc, p, batch, idesc, st);
     case JK_BF16: return launch_vt<KMAX, KATOMS, MODE, __nv_bfloat16>(tr, tc, p, batch, idesc, st);
@@ -644,8 +751,8 @@ int launch_k(const CUtensorMap& tr, const CUtensorMap& tc, const Params& p, int6
 }
 
 template <int MODE>
-int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols,
-           int64_t rp, int proj_dtype, Params& p, cudaStream_t st) {
+int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols, int64_t rp,
+           int proj_dtype, Params& p, cudaStream_t st) {
   CUtensorMap tr, tc;
   const bool bf16 = proj_dtype == JK_BF16;
   int status = make_tmap_3d_16bit(&tr, row_proj, rp, n_rows, batch, 64, kRows, bf16);
@@ -662,13 +769,13 @@ int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_
                  : launch_k<64, 2, MODE>(tr, tc, p, batch, idesc, st);
 }
 
-int validate_common(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows,
-                    int64_t n_cols, int64_t rp, int proj_dtype, const void* state, int state_dtype,
-                    const void* val, int64_t dim, int val_dtype, int64_t k, int compress, int out_dtype) {
+int validate_common(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols,
+                    int64_t rp, int proj_dtype, const void* state, int state_dtype, const void* val, int64_t dim,
+                    int val_dtype, int64_t k, int compress, int out_dtype) {
   if (row_proj == nullptr || col_proj == nullptr || state == nullptr || val == nullptr) return JK_ERR_BAD_ARG;
   if (proj_dtype != JK_BF16 && proj_dtype != JK_F16) return JK_ERR_BAD_DTYPE;
-  if (val_dtype < JK_F32 || val_dtype > JK_F16 || out_dtype < JK_F32 || out_dtype > JK_F16 ||
-      state_dtype < JK_F32 || state_dtype > JK_F16)
+  if (val_dtype < JK_F32 || val_dtype > JK_F16 || out_dtype < JK_F32 || out_dtype > JK_F16 || state_dtype < JK_F32 ||
+      state_dtype > JK_F16)
     return JK_ERR_BAD_DTYPE;
   if (compress < JK_SOFTSIGN || compress > JK_SOFTMAX) return JK_ERR_UNSUPPORTED_KIND;
   if (k < 1 || k > 64) return JK_ERR_BAD_ARG;
@@ -683,16 +790,15 @@ int validate_common(const void* row_proj, const void* col_proj, int64_t batch, i
 }  // namespace topk
 }  // namespace jk
 
-extern "C" int jk_propagation_topk_forward(const void* row_proj, const void* col_proj, int64_t batch,
-                                           int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
-                                           const void* col_state, const void* col_sender, int state_dtype,
-                                           const void* col_val, int64_t dim, int val_dtype, int64_t k,
-                                           int64_t window, float score_bias, const float* bias_dev, int compress,
-                                           void* out_state, void* out_val, int out_dtype, float* out_scores,
-                                           int64_t* out_index, jk_stream_t stream) {
+extern "C" int jk_propagation_topk_forward(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows,
+                                           int64_t n_cols, int64_t rp, int proj_dtype, const void* col_state,
+                                           const void* col_sender, int state_dtype, const void* col_val, int64_t dim,
+                                           int val_dtype, int64_t k, int64_t window, float score_bias,
+                                           const float* bias_dev, int compress, void* out_state, void* out_val,
+                                           int out_dtype, float* out_scores, int64_t* out_index, jk_stream_t stream) {
   using namespace jk;
-  int st = topk::validate_common(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state,
-                                 state_dtype, col_val, dim, val_dtype, k, compress, out_dtype);
+  int st = topk::validate_common(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype,
+                                 col_val, dim, val_dtype, k, compress, out_dtype);
   if (st != JK_OK) return st;
   if (out_state == nullptr || out_val == nullptr) return JK_ERR_BAD_ARG;
   if (dim % 8 == 0 && !aligned16(out_val)) return JK_ERR_ALIGNMENT;
@@ -725,29 +831,26 @@ extern "C" int jk_propagation_topk_forward(const void* row_proj, const void* col
 
 extern "C" int jk_transition_query_topk_forward(const void* query_proj, const void* source_proj, int64_t batch,
                                                 int64_t n_query, int64_t n_source, int64_t rp, int proj_dtype,
-                                                const void* source_state, const void* source_sender,
-                                                int state_dtype, const void* source_val, int64_t dim,
-                                                int val_dtype, int64_t k, float score_bias,
-                                                const float* bias_dev, int compress, void* out_state,
-                                                void* out_val, int out_dtype, float* out_scores,
+                                                const void* source_state, const void* source_sender, int state_dtype,
+                                                const void* source_val, int64_t dim, int val_dtype, int64_t k,
+                                                float score_bias, const float* bias_dev, int compress,
+                                                void* out_state, void* out_val, int out_dtype, float* out_scores,
                                                 int64_t* out_index, jk_stream_t stream) {
-  return jk_propagation_topk_forward(query_proj, source_proj, batch, n_query, n_source, rp, proj_dtype,
-                                     source_state, source_sender, state_dtype, source_val, dim, val_dtype, k,
-                                     -1, score_bias, bias_dev, compress, out_state, out_val, out_dtype,
-                                     out_scores, out_index, stream);
+  return jk_propagation_topk_forward(query_proj, source_proj, batch, n_query, n_source, rp, proj_dtype, source_state,
+                                     source_sender, state_dtype, source_val, dim, val_dtype, k, -1, score_bias,
+                                     bias_dev, compress, out_state, out_val, out_dtype, out_scores, out_index, stream);
 }
 
 extern "C" int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_proj, int64_t batch,
                                                    int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
-                                                   const void* src_state, const void* src_sender,
-                                                   int state_dtype, const void* src_val, int64_t dim,
-                                                   int val_dtype, int64_t k, float score_bias,
-                                                   const float* bias_dev, int compress, float* accum,
-                                                   void* out_state, void* out_val, int out_dtype,
+                                                   const void* src_state, const void* src_sender, int state_dtype,
+                                                   const void* src_val, int64_t dim, int val_dtype, int64_t k,
+                                                   float score_bias, const float* bias_dev, int compress,
+                                                   float* accum, void* out_state, void* out_val, int out_dtype,
                                                    jk_stream_t stream) {
   using namespace jk;
-  int st = topk::validate_common(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_state,
-                                 state_dtype, src_val, dim, val_dtype, k, compress, out_dtype);
+  int st = topk::validate_common(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_state, state_dtype,
+                                 src_val, dim, val_dtype, k, compress, out_dtype);
   if (st != JK_OK) return st;
   if (accum == nullptr || out_state == nullptr || out_val == nullptr) return JK_ERR_BAD_ARG;
   if (!aligned16(accum)) return JK_ERR_ALIGNMENT;
@@ -787,3 +890,15 @@ extern "C" int jk_transition_pairwise_topk_forward(const void* src_proj, const v
   topk::finalize_scatter<<<blocks, 256, 0, cs>>>(acc_state, acc_val, n_state, n_val, out_state, out_val, out_dtype);
   return launch_status();
 }
+
+#ifdef JK_PHASE_PROFILE
+extern "C" int jk_debug_phase(unsigned long long* out, int reset) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out, jk::topk::g_phase, sizeof(unsigned long long) * 8);
+  if (reset) {
+    unsigned long long z[8] = {0};
+    cudaMemcpyToSymbol(jk::topk::g_phase, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
