@@ -51,7 +51,7 @@ int launch_status() {
 }
 
 int make_tmap_3d_16bit(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
-                       uint32_t box0, uint32_t box1, bool bf16) {
+                       uint32_t box0, uint32_t box1, bool bf16, bool swizzle128) {
   auto encode = get_encode_fn();
   if (encode == nullptr) return JK_ERR_UNSUPPORTED_DEVICE;
   if (!aligned16(base)) return JK_ERR_ALIGNMENT;
@@ -61,7 +61,8 @@ int make_tmap_3d_16bit(CUtensorMap* map, const void* base, uint64_t d0, uint64_t
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                       3, const_cast<void*>(base), dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? JK_OK : JK_ERR_BAD_SHAPE;
 }

@@ -23,9 +23,9 @@ int check_device();
 int launch_status();
 
 // Encodes a 3-D tiled tensor map over a contiguous [d2][d1][d0] array of 16-bit elements
-// with a {box0, box1, 1} box and 128-byte swizzle. Returns JK_OK or an error status.
+// with a {box0, box1, 1} box, 128-byte swizzled (MMA operands) or plain row-major. Returns JK_OK or an error status.
 int make_tmap_3d_16bit(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
-                       uint32_t box0, uint32_t box1, bool bf16);
+                       uint32_t box0, uint32_t box1, bool bf16, bool swizzle128 = true);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

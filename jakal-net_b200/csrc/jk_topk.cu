@@ -1,4 +1,4 @@
-// Fused low-rank score -> streaming top-k -> edge compress -> aggregate kernel.
+// Fused low-rank score -> top-k -> edge compress -> aggregate kernel.
 //
 // Covers three reference operators that share one structure ("every row picks its k best
 // columns by a low-rank bilinear score"):
@@ -11,20 +11,27 @@
 //                              softmax over the k picked destinations, scatter-add).
 //
 // Per CTA: 128 rows of one batch item, 9 warps.
-//   warp 8  (producer): TMA-loads the row-side projection tile once and streams the
-//           column-side tiles (128 columns x rp) through a multi-stage smem ring; issues
-//           tcgen05.mma (M=128 rows, N=128 columns, K=rp) into one of two TMEM
-//           accumulators, so the MMA of tile j+1 overlaps the selection of tile j.
-//   warps 0-7 (selection): two threads per row (warps w and w+4 read the same TMEM lanes);
-//           each owns 64 of the 128 columns of every tile. A thread keeps a k-entry
-//           min-heap (root = its current k-th best) in shared memory laid out
-//           [slot][row] so every access is bank-conflict free. Candidates are filtered
-//           against max(own root, partner's published root) -- a valid lower bound of the
-//           row's k-th best -- queued per thread and merged into the heap in warp-wide
-//           flushes, so lanes do not diverge per candidate. After the last tile both heaps
-//           are sorted and merged, compressed into edges, and all 8 warps aggregate the
-//           128 rows with 16-byte vector loads of the picked value rows (gather) or vector
-//           atomics into the destination rows (scatter).
+//   warp 8 (producer): TMA-loads the row-side projection tile once and streams the
+//          column-side tiles (128 columns x rp) through a smem ring; issues tcgen05.mma
+//          (M=128 rows, N=128 columns, K=rp) into one of two TMEM accumulators, so the MMA
+//          of one tile overlaps the selection work on the previous one. The column tiles
+//          are streamed once per selection pass (scores are recomputed, never stored).
+//   warps 0-7 (selection): two threads per row (warps w and w+4 read the same TMEM lanes),
+//          each owning 64 of the 128 columns of every tile.
+//     pass A (only when a row sees more than kCap columns): per-row mean and variance of
+//          the visible scores -> a threshold tau expected to pass about k + 3 sqrt(k) + 8
+//          columns (normal quantile).
+//     pass B: every visible column with score >= tau is appended to the row's candidate
+//          buffer (kCap slots in shared memory).
+//     pass C (only if some row of the CTA got fewer than min(k, visible) or more than kCap
+//          candidates -- a row far from normal): those rows redo an exact streaming
+//          selection, each thread keeping a k-entry min-heap in the row's buffer.
+//     select: one warp per row sorts the row's buffer (bitonic, 128 keys ordered by score
+//          then lower column) and keeps the best k.
+//   Then the k survivors are compressed into edges, and all 8 warps aggregate: a windowed
+//   CTA stages its whole source range in shared memory 64 value columns at a time (TMA)
+//   and gathers from there; otherwise 16-byte vector gathers from global memory; the
+//   per-source transition scatters with vector atomics instead.
 #include "jk_host.h"
 #include "jk_sm100.cuh"
 
@@ -49,15 +56,22 @@ __device__ unsigned long long g_phase[8];
   } while (0)
 #endif
 
-constexpr int kRows = 128;       // rows per CTA (MMA M)
-constexpr int kCols = 128;       // columns per tile (MMA N)
-constexpr int kHalfCols = 64;    // columns per selection thread per tile
-constexpr int kQueue = 8;        // per-thread candidate queue depth
-constexpr int kSelWarps = 8;     // selection / aggregation warps
+constexpr int kRows = 128;      // rows per CTA (MMA M)
+constexpr int kCols = 128;      // columns per tile (MMA N)
+constexpr int kHalfCols = 64;   // columns per selection thread per tile
+constexpr int kCap = 128;       // candidate slots per row
+constexpr int kQueue = 4;       // fallback queue slots per thread
+constexpr int kStride = 137;    // row stride of the candidate buffer (odd: conflict-free)
+constexpr int kSelWarps = 8;    // selection / aggregation warps
 constexpr int kThreads = (kSelWarps + 1) * 32;
 constexpr int kSentinel = INT_MAX;
+static_assert(kStride >= kCap + 2 * kQueue, "buffer row holds candidates and both fallback queues");
 
 enum Mode { kGather = 0, kScatter = 1 };
+
+// Start (in floats, 16-byte aligned) of a row's packed gather table: (weight, column) pairs
+// written over the row's candidate values once the edges are final.
+__device__ __forceinline__ int gtab_off(int row) { return (row * kStride + 3) & ~3; }
 
 struct Params {
   int64_t n_rows, n_cols, rp, dim;
@@ -67,6 +81,7 @@ struct Params {
   const float* bias_dev;
   int compress;
   int state_dtype, val_dtype, out_dtype;
+  int slab_ok;  // tm_val is valid (windowed gather of 16-bit values, dim % 64 == 0)
   const void* col_state;
   const void* col_val;
   const void* col_sender;
@@ -85,12 +100,12 @@ __device__ __forceinline__ bool worse(float av, int ai, float bv, int bi) {
   return av < bv || (av == bv && ai > bi);
 }
 
-// One thread's slice of a [slot][row] array pair (stride kRows).
+// A run of (value, index) slots of one row in the candidate buffer.
 struct Lane {
   float* v;
   int* i;
-  __device__ __forceinline__ float& val(int slot) const { return v[slot * kRows]; }
-  __device__ __forceinline__ int& idx(int slot) const { return i[slot * kRows]; }
+  __device__ __forceinline__ float& val(int slot) const { return v[slot]; }
+  __device__ __forceinline__ int& idx(int slot) const { return i[slot]; }
 };
 
 // Sift (x, id) down from the root of a min-heap of size n ("min" = worst).
@@ -134,17 +149,6 @@ __device__ __forceinline__ float flush_queue(const Lane& h, const Lane& q, int k
   }
   qn = 0;
   return root_v;
-}
-
-// In-place heapsort of a min-heap -> entries sorted best first.
-__device__ __forceinline__ void heap_sort(const Lane& h, int k) {
-  for (int end = k - 1; end > 0; --end) {
-    const float x = h.val(end);
-    const int id = h.idx(end);
-    h.val(end) = h.val(0);
-    h.idx(end) = h.idx(0);
-    heap_sift_root(h, end, x, id);
-  }
 }
 
 __device__ __forceinline__ float sgn(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
@@ -246,6 +250,24 @@ __device__ __forceinline__ void widen8<float>(const uint4&, float (&f)[8]) {
   for (int i = 0; i < 8; ++i) f[i] = 0.f;  // f32 values take the generic path
 }
 
+template <typename VT>
+__device__ __forceinline__ float2 widen2(uint32_t u);
+
+template <>
+__device__ __forceinline__ float2 widen2<__nv_bfloat16>(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+
+template <>
+__device__ __forceinline__ float2 widen2<__half>(uint32_t u) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+
+template <>
+__device__ __forceinline__ float2 widen2<float>(uint32_t) {
+  return make_float2(0.f, 0.f);
+}
+
 __device__ __forceinline__ void store8(void* base, int64_t elem, int dtype, const float (&f)[8]) {
   if (dtype == JK_F32) {
     float4* q = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + elem);
@@ -266,30 +288,41 @@ __device__ __forceinline__ void store8(void* base, int64_t elem, int dtype, cons
   }
 }
 
+__device__ __forceinline__ void store2(void* base, int64_t elem, int dtype, float a, float b) {
+  if (dtype == JK_F32) {
+    *reinterpret_cast<float2*>(reinterpret_cast<float*>(base) + elem) = make_float2(a, b);
+  } else if (dtype == JK_BF16) {
+    *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(base) + elem) = __floats2bfloat162_rn(a, b);
+  } else {
+    *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(base) + elem) = __floats2half2_rn(a, b);
+  }
+}
+
+// ---------------------------------------------------------------- aggregation
 // Generic aggregation of one row by one warp (any dim / f32 values): lanes stride the
 // value dimension; the final weights already include the sender strength.
-__device__ void gather_row_generic(const Lane& f, int n, int64_t col_base, int64_t row, const Params& p, int lane) {
+__device__ void gather_row_generic(const float* tab, int n, int64_t col_base, int64_t row, const Params& p, int lane) {
   const int64_t D = p.dim;
   for (int64_t d0 = 0; d0 < D; d0 += 32) {
     const int64_t d = d0 + lane;
     float acc = 0.f;
     for (int e = 0; e < n; ++e) {
-      const int j = f.idx(e);
-      if (d < D) acc = fmaf(f.val(e), ld_elem(p.col_val, (col_base + j) * D + d, p.val_dtype), acc);
+      const int j = __float_as_int(tab[2 * e + 1]);
+      if (d < D) acc = fmaf(tab[2 * e], ld_elem(p.col_val, (col_base + j) * D + d, p.val_dtype), acc);
     }
     if (d < D) st_elem(p.out_val, row * D + d, p.out_dtype, acc);
   }
 }
 
-// Aggregation of `nrows` rows (tile rows rt0 ..) by one warp for 16-bit values.
+// Aggregation of `nrows` rows (tile rows rt0 ..) by one warp from global memory.
 //
 // Work items are (row, 8-element chunk) pairs of a group of rows spread over the 32
 // lanes, so every lane keeps up to 16 independent 16-byte loads in flight per step (8
-// items x 2 neighbours) whatever the value width, which hides the L2 / HBM latency of the
-// random gathers. Accumulation is f32; each item is stored once.
+// items x 2 neighbours) whatever the value width, hiding the L2 / HBM latency of random
+// gathers. Accumulation is f32; each item is stored once.
 template <typename VT>
-__device__ void gather_warp(float* fv, int* fi, int* nsel, int rt0, int nrows, int64_t t0, int64_t b,
-                            const Params& p, int lane) {
+__device__ void gather_global(const float* bv, const int* nsel, int rt0, int nrows, int64_t t0, int64_t b,
+                              const Params& p, int lane) {
   constexpr int kItems = 8;
   const int64_t D = p.dim;
   const int64_t col_base = b * p.n_cols;
@@ -298,7 +331,7 @@ __device__ void gather_warp(float* fv, int* fi, int* nsel, int rt0, int nrows, i
       const int rt = rt0 + r;
       const int64_t row = t0 + rt;
       if (row >= p.n_rows) break;
-      gather_row_generic(Lane{fv + rt, fi + rt}, nsel[rt], col_base, b * p.n_rows + row, p, lane);
+      gather_row_generic(bv + gtab_off(rt), nsel[rt], col_base, b * p.n_rows + row, p, lane);
     }
     return;
   }
@@ -331,9 +364,9 @@ __device__ void gather_warp(float* fv, int* fi, int* nsel, int rt0, int nrows, i
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const bool on = i + u < nq[m];
-          const int slot = (on ? i + u : 0) * kRows + rq[m];
-          const int j = fi[slot];
-          w[m][u] = on ? fv[slot] : 0.f;
+          const float2 wj = *reinterpret_cast<const float2*>(bv + gtab_off(rq[m]) + 2 * (on ? i + u : 0));
+          const int j = __float_as_int(wj.y);
+          w[m][u] = on ? wj.x : 0.f;
           raw[m][u] = on ? __ldg(reinterpret_cast<const uint4*>(vbase + static_cast<int64_t>(j) * D + off[m]))
                          : make_uint4(0, 0, 0, 0);
         }
@@ -358,6 +391,49 @@ __device__ void gather_warp(float* fv, int* fi, int* nsel, int rt0, int nrows, i
         store8(p.out_val, row * D + off[m], p.out_dtype, acc[m]);
       }
     }
+  }
+}
+
+// Aggregation of `nrows` rows from a staged slab: 64 value columns of the source rows
+// s_lo .. s_lo + nslab - 1, row-major (128 B per source row). The warp works on 4 rows at a
+// time: lanes 8q .. 8q+7 own row q, 8 columns each, so a slab read of the warp is four
+// 128-byte rows (the minimum four wavefronts) and each lane does 8 FMAs per read.
+template <typename VT>
+__device__ void gather_slab_chunk(const uint8_t* slab, const float* bv, const int* nsel, int rt0, int nrows,
+                                  int64_t t0, int64_t b, int s_lo, int chunk, const Params& p, int lane) {
+  constexpr int kNb = 4;  // neighbours per step
+  const int64_t D = p.dim;
+  const int q = lane >> 3;     // row of the group this lane works on
+  const int piece = lane & 7;  // 16-byte piece (8 columns) of the 64-column chunk
+  for (int r0 = 0; r0 < nrows; r0 += 4) {
+    const int rt = rt0 + r0 + q;
+    const bool ok = r0 + q < nrows && t0 + rt < p.n_rows;
+    const int n = ok ? nsel[rt] : 0;
+    const int nmax = __reduce_max_sync(0xffffffffu, n);
+    const float* tab = bv + gtab_off(ok ? rt : rt0);
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int e0 = 0; e0 < nmax; e0 += kNb) {
+      uint4 u[kNb];
+      float w[kNb];
+#pragma unroll
+      for (int m = 0; m < kNb; ++m) {
+        const bool on = e0 + m < n;
+        const float2 wj = *reinterpret_cast<const float2*>(tab + 2 * (on ? e0 + m : 0));
+        w[m] = on ? wj.x : 0.f;
+        const int j = on ? __float_as_int(wj.y) - s_lo : 0;
+        u[m] = *reinterpret_cast<const uint4*>(slab + j * 128 + piece * 16);
+      }
+#pragma unroll
+      for (int m = 0; m < kNb; ++m) {
+        float x[8];
+        widen8<VT>(u[m], x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(w[m], x[e], acc[e]);
+      }
+    }
+    if (ok) store8(p.out_val, (b * p.n_rows + t0 + rt) * D + chunk * 64 + piece * 8, p.out_dtype, acc);
   }
 }
 
@@ -405,51 +481,131 @@ __device__ void scatter_row(const Lane& f, int n, int64_t b, int64_t src, const 
   }
 }
 
+// ---------------------------------------------------------------- warp bitonic selection
+// Orderable 64-bit key: larger = better (higher score, then lower column).
+__device__ __forceinline__ unsigned long long make_key(float v, int idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(idx));
+}
+
+__device__ __forceinline__ float key_val(unsigned long long key) {
+  uint32_t u = static_cast<uint32_t>(key >> 32);
+  u = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
+  return __uint_as_float(u);
+}
+
+__device__ __forceinline__ int key_idx(unsigned long long key) {
+  return static_cast<int>(~static_cast<uint32_t>(key & 0xFFFFFFFFull));
+}
+
+// Sorts the first n (<= NQ * 32) candidates of a row into descending key order with one
+// warp (element e = q * 32 + lane, NQ per lane) and writes the best min(k, valid) back to
+// slots 0 ..; returns that count.
+template <int NQ>
+__device__ int warp_select_row(float* rv, int* ri, int n, int k, int lane) {
+  constexpr int kN = NQ * 32;
+  const unsigned long long kNone = make_key(-INFINITY, kSentinel);
+  unsigned long long x[NQ];
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int e = q * 32 + lane;
+    x[q] = e < n ? make_key(rv[e], ri[e]) : kNone;
+  }
+  // Bitonic sort, descending, over kN elements indexed e = q*32 + lane.
+#pragma unroll
+  for (int size = 2; size <= kN; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        const int e = q * 32 + lane;
+        const bool desc = (e & size) == 0;  // direction of this block
+        if (stride >= 32) {
+          const int qs = stride >> 5;
+          if ((q & qs) == 0) {
+            const int q2 = q | qs;
+            const unsigned long long a = x[q], c = x[q2];
+            const bool swap = desc ? (a < c) : (a > c);
+            x[q] = swap ? c : a;
+            x[q2] = swap ? a : c;
+          }
+        } else {
+          const unsigned long long other = __shfl_xor_sync(0xffffffffu, x[q], stride);
+          const bool lower = (lane & stride) == 0;
+          const bool take_max = (lower == desc);  // the lower element keeps the larger key
+          const unsigned long long mx = x[q] > other ? x[q] : other;
+          const unsigned long long mn = x[q] > other ? other : x[q];
+          x[q] = take_max ? mx : mn;
+        }
+      }
+    }
+  }
+  int valid = 0;
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int e = q * 32 + lane;
+    valid += __popc(__ballot_sync(0xffffffffu, x[q] != kNone && e < k));
+  }
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int e = q * 32 + lane;
+    if (e < valid) {
+      rv[e] = key_val(x[q]);
+      ri[e] = key_idx(x[q]);
+    }
+  }
+  __syncwarp();
+  return valid;
+}
+
 __device__ __forceinline__ void sel_barrier() {
   asm volatile("bar.sync 1, %0;" ::"r"(kSelWarps * 32) : "memory");
 }
 
-template <int KMAX, int KATOMS, int STAGES>
+// ---------------------------------------------------------------- shared-memory layout
+template <int KATOMS, int STAGES>
 struct Layout {
   static constexpr int kAtomBytes = kRows * 128;  // 128 rows x 64 (16-bit) elements
   static constexpr int kABytes = KATOMS * kAtomBytes;
   static constexpr int kBBytes = KATOMS * kAtomBytes;
-  static constexpr int kRegion0 = kABytes + STAGES * kBBytes;  // A + ring; reused for the final lists
-  static constexpr int kFinalBytes = 2 * KMAX * kRows * 4;
-  static_assert(kFinalBytes <= kRegion0, "final lists must fit in the MMA operand region");
-  static constexpr int kHeapBytes = 2 * 2 * KMAX * kRows * 4;  // 2 halves x (value, index)
-  static constexpr int kQueueBytes = 2 * 2 * kQueue * kRows * 4;
-  static constexpr int kPubBytes = 2 * kRows * 4;
-  static constexpr int kNselBytes = kRows * 4;
+  static constexpr int kRegion0 = kABytes + STAGES * kBBytes;  // A + ring; reused as the value slab
+  static constexpr int kBufBytes = 2 * kRows * kStride * 4;    // candidate values + indices
+  static constexpr int kRowArrays = 10 * kRows * 4;            // per-row scalars
   static constexpr int kBarBytes = 256;
-  static constexpr int kTotal = 1024 + kRegion0 + kHeapBytes + kQueueBytes + kPubBytes + kNselBytes + kBarBytes;
+  static constexpr int kTotal = 1024 + kRegion0 + kBufBytes + kRowArrays + kBarBytes;
 };
 
-template <int KMAX, int KATOMS, int STAGES, int MODE, typename VT>
+template <int KATOMS, int STAGES, int MODE, typename VT>
 __global__ void __launch_bounds__(kThreads, 1)
     topk_kernel(const __grid_constant__ CUtensorMap tm_rows, const __grid_constant__ CUtensorMap tm_cols,
-                Params p, uint32_t idesc) {
-  using L = Layout<KMAX, KATOMS, STAGES>;
+                const __grid_constant__ CUtensorMap tm_val, Params p, uint32_t idesc) {
+  using L = Layout<KATOMS, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_tile = smem;
   uint8_t* b_ring = smem + L::kABytes;
-  float* fv = reinterpret_cast<float*>(smem);  // final lists (after streaming)
-  int* fi = reinterpret_cast<int*>(fv + KMAX * kRows);
-  float* hv = reinterpret_cast<float*>(smem + L::kRegion0);  // [2][KMAX][kRows]
-  int* hi = reinterpret_cast<int*>(hv + 2 * KMAX * kRows);
-  float* qv = reinterpret_cast<float*>(hi + 2 * KMAX * kRows);  // [2][kQueue][kRows]
-  int* qi = reinterpret_cast<int*>(qv + 2 * kQueue * kRows);
-  volatile float* pub = reinterpret_cast<volatile float*>(qi + 2 * kQueue * kRows);  // [2][kRows]
-  int* nsel = reinterpret_cast<int*>(const_cast<float*>(pub) + 2 * kRows);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(nsel + kRows);
+  float* bufv = reinterpret_cast<float*>(smem + L::kRegion0);  // [kRows][kStride]
+  int* bufi = reinterpret_cast<int*>(bufv + kRows * kStride);
+  int* cnt = bufi + kRows * kStride;                           // [kRows]
+  int* nsel = cnt + kRows;                                     // [kRows]
+  int* failrow = nsel + kRows;                                 // [kRows]
+  float* tau = reinterpret_cast<float*>(failrow + kRows);      // [kRows]
+  float* s1 = tau + kRows;                                     // [2][kRows]
+  float* s2 = s1 + 2 * kRows;                                  // [2][kRows]
+  volatile float* pub = s2 + 2 * kRows;                        // [2][kRows]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(const_cast<float*>(pub) + 2 * kRows);
   uint64_t* bar_a = bars;
-  uint64_t* full = bars + 1;
+  uint64_t* decide = bars + 1;
+  uint64_t* slab_bar = bars + 2;
+  uint64_t* full = bars + 3;
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* any_fail = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -457,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRows;
   const int k = p.k;
 
-  // Column-tile range.
+  // Column-tile range (identical in every thread).
   int64_t j_lo = 0, j_hi = (p.n_cols + kCols - 1) / kCols - 1;
   if (p.window >= 0) {
     const int64_t lo = t0 - p.window;
@@ -467,9 +623,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     j_hi = hi_col < 0 ? -1 : hi_col / kCols;
   }
   const int ntiles = j_hi >= j_lo ? static_cast<int>(j_hi - j_lo + 1) : 0;
+  // Pass A is needed when some row can see more columns than its buffer holds.
+  const int64_t max_visible = p.window >= 0 ? (p.window + 1 < p.n_cols ? p.window + 1 : p.n_cols) : p.n_cols;
+  const bool has_a = max_visible > kCap;
+  const int pre_passes = has_a ? 2 : 1;
 
   if (threadIdx.x == 0) {
     mbar_init(bar_a, 1);
+    mbar_init(decide, 1);
+    mbar_init(slab_bar, 1);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
@@ -479,6 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[i], kSelWarps);
     }
     *abort_flag = 0;
+    *any_fail = 0;
     fence_barrier_init();
   }
   if (warp == 0) tmem_alloc(tmem_slot, 256);
@@ -497,21 +660,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int a = 0; a < KATOMS; ++a)
         tma_load_3d(a_tile + a * L::kAtomBytes, &tm_rows, bar_a, a * 64, static_cast<int>(t0), static_cast<int>(b));
-      const int pre = ntiles < STAGES ? ntiles : STAGES;
-      for (int it = 0; it < pre; ++it) {
-        mbar_arrive_expect_tx(&full[it], L::kBBytes);
-        const int col0 = static_cast<int>((j_lo + it) * kCols);
+      int total = pre_passes * ntiles;  // grows by one pass if the fallback pass is needed
+      const int decide_at = total - 1;
+      int issued = 0;  // column-tile loads issued, in global iteration order
+      auto issue_loads = [&](int upto) -> bool {
+        while (issued <= upto && issued < total) {
+          const int s = issued % STAGES;
+          if (issued >= STAGES) {
+            const int prev = issued - STAGES;  // the MMA that last read stage s
+            if (!mbar_wait(&empty[s], (prev / STAGES) & 1)) return false;
+          }
+          mbar_arrive_expect_tx(&full[s], L::kBBytes);
+          const int col0 = static_cast<int>((j_lo + issued % ntiles) * kCols);
 #pragma unroll
-        for (int a = 0; a < KATOMS; ++a)
-          tma_load_3d(b_ring + it * L::kBBytes + a * L::kAtomBytes, &tm_cols, &full[it], a * 64, col0,
-                      static_cast<int>(b));
-      }
-      ok = mbar_wait(bar_a, 0);
-      for (int it = 0; it < ntiles && ok; ++it) {
-        const int st = it % STAGES;
-        const int buf = it & 1;
-        if (!mbar_wait(&full[st], (it / STAGES) & 1)) { ok = false; break; }
-        if (it >= 2 && !mbar_wait(&tempty[buf], ((it >> 1) - 1) & 1)) { ok = false; break; }
+          for (int a = 0; a < KATOMS; ++a)
+            tma_load_3d(b_ring + s * L::kBBytes + a * L::kAtomBytes, &tm_cols, &full[s], a * 64, col0,
+                        static_cast<int>(b));
+          ++issued;
+        }
+        return true;
+      };
+      ok = issue_loads(STAGES - 1) && mbar_wait(bar_a, 0);
+      for (int g = 0; g < total && ok; ++g) {
+        const int st = g % STAGES;
+        const int buf = g & 1;
+        if (!mbar_wait(&full[st], (g / STAGES) & 1)) { ok = false; break; }
+        if (g >= 2 && !mbar_wait(&tempty[buf], ((g >> 1) - 1) & 1)) { ok = false; break; }
         if (*abort_flag) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_addr = smem_u32(a_tile);
@@ -524,23 +698,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&empty[st]);
         mma_commit(&tfull[buf]);
-        // Refill the stage the previous tile used (its MMA has most likely retired); with a
-        // single stage, the stage of this tile once its own MMA retires.
-        const int ip = STAGES == 1 ? it : it - 1;
-        if (ip >= 0 && ip + STAGES < ntiles) {
-          const int sp = ip % STAGES;
-          if (!mbar_wait(&empty[sp], (ip / STAGES) & 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[sp], L::kBBytes);
-          const int col0 = static_cast<int>((j_lo + ip + STAGES) * kCols);
-#pragma unroll
-          for (int a = 0; a < KATOMS; ++a)
-            tma_load_3d(b_ring + sp * L::kBBytes + a * L::kAtomBytes, &tm_cols, &full[sp], a * 64, col0,
-                        static_cast<int>(b));
+        if (g == decide_at) {
+          // The selection warps report whether any row needs the exact fallback pass.
+          if (!mbar_wait(decide, 0)) { ok = false; break; }
+          if (*any_fail) total += ntiles;
         }
+        // Stage reuse: with >= 2 stages load ahead behind the previous MMA, with one stage
+        // behind this MMA.
+        if (!issue_loads(STAGES == 1 ? g + 1 : g - 1 + STAGES)) { ok = false; break; }
       }
       // The MMA-retire arrivals on the ring barriers must land before the CTA exits.
       if (ok) {
-        const int last = ntiles - 1;
+        const int last = total - 1;
         ok = mbar_wait(&empty[last % STAGES], (last / STAGES) & 1);
       }
       if (!ok) {
@@ -562,99 +731,188 @@ __global__ void __launch_bounds__(kThreads, 1)
       lo_t = lo < 0 ? 0 : static_cast<int>(lo);
       hi_t = t < hi_t ? static_cast<int>(t) : hi_t;
     }
+    int visible = hi_t - lo_t + 1;
     if (!row_ok || hi_t < lo_t) {  // nothing visible: an unreachable single-column range
       lo_t = INT_MAX / 2;
       hi_t = INT_MAX / 2;
+      visible = 0;
     }
     const uint32_t span = static_cast<uint32_t>(hi_t - lo_t);
-    const Lane heap{hv + half * KMAX * kRows + row, hi + half * KMAX * kRows + row};
-    const Lane queue{qv + half * kQueue * kRows + row, qi + half * kQueue * kRows + row};
-    for (int e = 0; e < k; ++e) {
-      heap.val(e) = -INFINITY;
-      heap.idx(e) = kSentinel;
-    }
-    pub[half * kRows + row] = -INFINITY;
-    float thr_own = -INFINITY, thr_part = -INFINITY;
-    int qn = 0;
-    bool ok = true;
     const uint32_t tbase = (static_cast<uint32_t>(quad * 32) << 16) + half * kHalfCols;
+    float* rv = bufv + row * kStride;
+    int* ri = bufi + row * kStride;
+    int g = 0;  // global iteration (tile x pass)
+    bool ok = true;
 #ifdef JK_PHASE_PROFILE
     long long t_prev = clock64();
 #endif
-    sel_barrier();  // heaps and published roots initialised
-    for (int it = 0; it < ntiles; ++it) {
-      const int buf = it & 1;
-      if (!mbar_wait(&tfull[buf], (it >> 1) & 1) || *abort_flag) {
-        ok = false;
-        break;
-      }
+
+    // Loads this thread's 64 scores of iteration g into v; false on timeout / abort.
+    auto load_tile = [&](uint32_t (&v)[2][32]) -> bool {
+      const int buf = g & 1;
+      if (!mbar_wait(&tfull[buf], (g >> 1) & 1) || *abort_flag) return false;
       tc_fence_after();
-      uint32_t v[2][32];
       tmem_ld_32x32b_x32(tmem + tbase + buf * kCols, v[0]);
       tmem_ld_32x32b_x32(tmem + tbase + buf * kCols + 32, v[1]);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
-      const int col0 = static_cast<int>((j_lo + it) * kCols) + half * kHalfCols;
+      ++g;
+      return true;
+    };
+
+    // ---- pass A: row statistics -> threshold
+    if (half == 0) cnt[row] = 0;
+    if (has_a) {
+      float a1 = 0.f, a2 = 0.f;
+      for (int it = 0; it < ntiles && ok; ++it) {
+        uint32_t v[2][32];
+        if (!load_tile(v)) { ok = false; break; }
+        const int col0 = static_cast<int>((j_lo + it) * kCols) + half * kHalfCols;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
+          for (int e = 0; e < 32; ++e) {
+            const float x = __uint_as_float(v[c][e]);
+            const bool vis = static_cast<uint32_t>(col0 + c * 32 + e - lo_t) <= span;
+            a1 += vis ? x : 0.f;
+            a2 = vis ? fmaf(x, x, a2) : a2;
+          }
+      }
+      s1[half * kRows + row] = a1;
+      s2[half * kRows + row] = a2;
+      sel_barrier();
+      if (half == 0) {
+        float th = -INFINITY;
+        if (visible > kCap) {
+          const float n = static_cast<float>(visible);
+          const float mean = (s1[row] + s1[kRows + row]) / n;
+          const float var = fmaxf((s2[row] + s2[kRows + row]) / n - mean * mean, 0.f);
+          // Expected survivors: k plus ~3 standard deviations of the count, so that too few
+          // is rare (the exact fallback pass covers it) and most rows fit a 64-key sort.
+          const float target = fminf(static_cast<float>(k) + 3.f * sqrtf(static_cast<float>(k)) + 8.f, 0.75f * kCap);
+          const float z = 1.41421356f * erfinvf(1.f - 2.f * target / n);
+          th = mean + z * sqrtf(var);
+        }
+        tau[row] = th;
+      }
+    } else if (half == 0) {
+      tau[row] = -INFINITY;
+    }
+    sel_barrier();
+    JK_PHASE_MARK(0, t_prev);
+
+    // ---- pass B: collect the columns at or above the threshold
+    {
+      const float th = tau[row];
+      for (int it = 0; it < ntiles && ok; ++it) {
+        uint32_t v[2][32];
+        if (!load_tile(v)) { ok = false; break; }
+        const int col0 = static_cast<int>((j_lo + it) * kCols) + half * kHalfCols;
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int col = col0 + c * 32 + e + u;
-            const float x = __uint_as_float(v[c][e + u]);
-            const bool pass = static_cast<uint32_t>(col - lo_t) <= span && x > thr_own && x >= thr_part;
-            if (pass) {
-              queue.val(qn) = x;
-              queue.idx(qn) = col;
-              ++qn;
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int col = col0 + c * 32 + e;
+            const float x = __uint_as_float(v[c][e]);
+            if (static_cast<uint32_t>(col - lo_t) <= span && x >= th) {
+              const int pos = atomicAdd(&cnt[row], 1);
+              if (pos < kCap) {
+                rv[pos] = x;
+                ri[pos] = col;
+              }
             }
           }
-          if (__any_sync(0xffffffffu, qn > kQueue - 4)) {
-            thr_own = flush_queue(heap, queue, k, qn);
-            pub[half * kRows + row] = thr_own;
-            thr_part = pub[(half ^ 1) * kRows + row];
-          }
-        }
       }
     }
-    if (ok) {
-      flush_queue(heap, queue, k, qn);
-      JK_PHASE_MARK(0, t_prev);
-      heap_sort(heap, k);
-    }
-    sel_barrier();  // both halves sorted; MMA operand region is free
-    JK_PHASE_MARK(1, t_prev);
     if (!ok) {
       atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
       *abort_flag = 1;
     }
     sel_barrier();
-    const bool good = !*abort_flag;
     if (half == 0) {
-      // Merge the two sorted halves (best first, ties to the lower column) into the
-      // final list, compress it, fold in the sender strength and form the state output.
-      const Lane A{hv + row, hi + row};
-      const Lane Bh{hv + KMAX * kRows + row, hi + KMAX * kRows + row};
-      const Lane F{fv + row, fi + row};
-      int ia = 0, ib = 0, n = 0;
-      if (good && row_ok) {
-        while (n < k) {
-          const float av = ia < k ? A.val(ia) : -INFINITY;
-          const float bv = ib < k ? Bh.val(ib) : -INFINITY;
-          const int ai = ia < k ? A.idx(ia) : kSentinel;
-          const int bi = ib < k ? Bh.idx(ib) : kSentinel;
-          const bool take_a = worse(bv, bi, av, ai);
-          const int id = take_a ? ai : bi;
-          if (id == kSentinel) break;
-          F.val(n) = take_a ? av : bv;
-          F.idx(n) = id;
-          ++n;
-          if (take_a) ++ia; else ++ib;
+      const int c = cnt[row];
+      const int need = k < visible ? k : visible;
+      const bool fail = row_ok && (c > kCap || c < need);
+      failrow[row] = fail ? 1 : 0;
+      if (fail) *any_fail = 1;
+    }
+    sel_barrier();
+    if (threadIdx.x == 0) mbar_arrive(decide);
+    JK_PHASE_MARK(1, t_prev);
+
+    // ---- pass C (rare): exact streaming selection for the rows the threshold missed
+    if (*any_fail && !*abort_flag && ntiles > 0) {
+      const bool mine = failrow[row] != 0;
+      const Lane heap{rv + half * 64, ri + half * 64};
+      const Lane queue{rv + kCap + half * kQueue, ri + kCap + half * kQueue};
+      if (mine) {
+        for (int e = 0; e < 64; ++e) {
+          heap.val(e) = -INFINITY;
+          heap.idx(e) = kSentinel;
         }
       }
+      pub[half * kRows + row] = -INFINITY;
+      sel_barrier();
+      float thr_own = -INFINITY, thr_part = -INFINITY;
+      int qn = 0;
+      for (int it = 0; it < ntiles && ok; ++it) {
+        uint32_t v[2][32];
+        if (!load_tile(v)) { ok = false; break; }
+        const int col0 = static_cast<int>((j_lo + it) * kCols) + half * kHalfCols;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int col = col0 + c * 32 + e + u;
+              const float x = __uint_as_float(v[c][e + u]);
+              if (mine && static_cast<uint32_t>(col - lo_t) <= span && x > thr_own && x >= thr_part) {
+                queue.val(qn) = x;
+                queue.idx(qn) = col;
+                ++qn;
+              }
+            }
+            if (__any_sync(0xffffffffu, qn > 0)) {
+              thr_own = flush_queue(heap, queue, k, qn);
+              pub[half * kRows + row] = thr_own;
+              thr_part = pub[(half ^ 1) * kRows + row];
+            }
+          }
+        }
+      }
+      if (!ok) {
+        atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
+        *abort_flag = 1;
+      }
+      sel_barrier();
+      if (half == 0 && mine) cnt[row] = kCap;  // both heaps (sentinel padded) are the candidates
+    }
+    sel_barrier();
+    JK_PHASE_MARK(2, t_prev);
+    const bool good = !*abort_flag;
+
+    // ---- select: one warp per row sorts the candidates and keeps the best k
+    const int rt0 = warp * (kRows / kSelWarps);
+    for (int r = 0; r < kRows / kSelWarps; ++r) {
+      const int rt = rt0 + r;
+      int n = 0;
+      if (good && t0 + rt < p.n_rows) {
+        const int c = cnt[rt] < kCap ? cnt[rt] : kCap;
+        n = c <= 64 ? warp_select_row<2>(bufv + rt * kStride, bufi + rt * kStride, c, k, lane)
+                    : warp_select_row<4>(bufv + rt * kStride, bufi + rt * kStride, c, k, lane);
+      }
+      if (lane == 0) nsel[rt] = n;
+    }
+    sel_barrier();
+    JK_PHASE_MARK(3, t_prev);
+
+    // ---- compress (thread per row), fold the sender strength, form the state output
+    if (half == 0) {
+      const Lane F{rv, ri};
+      const int n = nsel[row];
       const float bias = p.bias + (p.bias_dev ? __ldg(p.bias_dev) : 0.f);
       for (int e = 0; e < n; ++e) F.val(e) += bias;
       if (MODE == kGather && row_ok && good && (p.out_scores || p.out_index)) {
@@ -688,24 +946,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         st_elem(p.out_state, b * p.n_rows + t, p.out_dtype, acc);
       }
-      nsel[row] = n;
-    }
-    sel_barrier();  // final lists ready
-    JK_PHASE_MARK(2, t_prev);
-    if (good) {
-      // Aggregate: warp w handles rows 16w .. 16w+15.
-      const int rt0 = warp * (kRows / kSelWarps);
       if (MODE == kGather) {
-        gather_warp<VT>(fv, fi, nsel, rt0, kRows / kSelWarps, t0, b, p, lane);
-      } else {
-        for (int r = 0; r < kRows / kSelWarps; ++r) {
-          const int rt = rt0 + r;
-          if (t0 + rt >= p.n_rows) break;
-          scatter_row<VT>(Lane{fv + rt, fi + rt}, nsel[rt], b, b * p.n_rows + t0 + rt, p, lane);
+        // Pack (weight, column) pairs for the gather, back to front so that every write
+        // lands on an already consumed candidate slot of the same row.
+        float* tab = bufv + gtab_off(row);
+        for (int e = n - 1; e >= 0; --e) {
+          const float w = F.val(e);
+          const int j = F.idx(e);
+          tab[2 * e] = w;
+          tab[2 * e + 1] = __int_as_float(j);
         }
       }
     }
-    JK_PHASE_MARK(3, t_prev);
+    sel_barrier();
+    JK_PHASE_MARK(4, t_prev);
+
+    // ---- aggregate
+    if (good) {
+      const int nrows = kRows / kSelWarps;
+      if (MODE == kGather) {
+        int s_lo = 0, nslab = 0;
+        bool slab = false;
+        if (p.slab_ok && p.window >= 0 && sizeof(VT) == 2 && (p.dim % 64) == 0) {
+          const int64_t lo = t0 - p.window;
+          s_lo = lo > 0 ? static_cast<int>(lo) : 0;
+          int64_t hi_col = t0 + kRows - 1;
+          if (hi_col > p.n_cols - 1) hi_col = p.n_cols - 1;
+          nslab = static_cast<int>(hi_col - s_lo + 1);
+          slab = nslab > 0 && ((nslab + 127) / 128) * 128 * 128 <= L::kRegion0;
+        }
+        if (slab) {
+          const int nbox = (nslab + 127) / 128;
+          const int nchunk = static_cast<int>(p.dim / 64);
+          const uint8_t* slab_smem = smem;
+          for (int c = 0; c < nchunk && good; ++c) {
+            if (threadIdx.x == 0) {
+              fence_proxy_async_smem();  // prior generic reads of the slab region
+              mbar_arrive_expect_tx(slab_bar, nbox * 128 * 128);
+              for (int bx = 0; bx < nbox; ++bx)
+                tma_load_3d(smem + bx * 128 * 128, &tm_val, slab_bar, c * 64, s_lo + bx * 128, static_cast<int>(b));
+            }
+            if (!mbar_wait(slab_bar, c & 1)) {
+              atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
+              *abort_flag = 1;
+            } else {
+              gather_slab_chunk<VT>(slab_smem, bufv, nsel, rt0, nrows, t0, b, s_lo, c, p, lane);
+            }
+            sel_barrier();
+            if (*abort_flag) break;
+          }
+        } else {
+          gather_global<VT>(bufv, nsel, rt0, nrows, t0, b, p, lane);
+        }
+      } else {
+        for (int r = 0; r < nrows; ++r) {
+          const int rt = rt0 + r;
+          if (t0 + rt >= p.n_rows) break;
+          scatter_row<VT>(Lane{bufv + rt * kStride, bufi + rt * kStride}, nsel[rt], b, b * p.n_rows + t0 + rt, p,
+                          lane);
+        }
+      }
+    }
+    JK_PHASE_MARK(5, t_prev);
     tc_fence_before();
   }
   __syncthreads();
@@ -724,49 +1026,50 @@ __global__ void finalize_scatter(const float* acc_state, const float* acc_val, i
   for (int64_t j = i; j < n_state; j += stride) st_elem(out_state, j, out_dtype, acc_state[j]);
 }
 
-template <int KMAX, int KATOMS, int MODE, typename VT>
-int launch_vt(const CUtensorMap& tr, const CUtensorMap& tc, const Params& p, int64_t batch, uint32_t idesc,
-              cudaStream_t st) {
-  constexpr int STAGES = KATOMS == 1 ? (KMAX > 32 ? 3 : 4) : (KMAX > 32 ? 1 : 2);
-  constexpr int sm = Layout<KMAX, KATOMS, STAGES>::kTotal;
+template <int KATOMS, int MODE, typename VT>
+int launch_vt(const CUtensorMap& tr, const CUtensorMap& tc, const CUtensorMap& tv, const Params& p, int64_t batch,
+              uint32_t idesc, cudaStream_t st) {
+  constexpr int STAGES = KATOMS == 1 ? 4 : 1;
+  constexpr int sm = Layout<KATOMS, STAGES>::kTotal;
   static_assert(sm <= 232448, "shared memory budget");
-  auto kern = topk_kernel<KMAX, KATOMS, STAGES, MODE, VT>;
+  auto kern = topk_kernel<KATOMS, STAGES, MODE, VT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) {
     cudaGetLastError();
     return JK_ERR_LAUNCH;
   }
   const dim3 grid(static_cast<unsigned>((p.n_rows + kRows - 1) / kRows), static_cast<unsigned>(batch));
-  kern<<<grid, kThreads, sm, st>>>(tr, tc, p, idesc);
+  kern<<<grid, kThreads, sm, st>>>(tr, tc, tv, p, idesc);
   return launch_status();
 }
 
-template <int KMAX, int KATOMS, int MODE>
-int launch_k(const CUtensorMap& tr, const CUtensorMap& tc, const Params& p, int64_t batch, uint32_t idesc,
-             cudaStream_t st) {
+template <int KATOMS, int MODE>
+int launch_k(const CUtensorMap& tr, const CUtensorMap& tc, const CUtensorMap& tv, const Params& p, int64_t batch,
+             uint32_t idesc, cudaStream_t st) {
   switch (p.val_dtype) {
-    case JK_F32: return launch_vt<KMAX, KATOMS, MODE, float>(tr, tc, p, batch, idesc, st);
-    case JK_BF16: return launch_vt<KMAX, KATOMS, MODE, __nv_bfloat16>(tr, tc, p, batch, idesc, st);
-    default: return launch_vt<KMAX, KATOMS, MODE, __half>(tr, tc, p, batch, idesc, st);
+    case JK_F32: return launch_vt<KATOMS, MODE, float>(tr, tc, tv, p, batch, idesc, st);
+    case JK_BF16: return launch_vt<KATOMS, MODE, __nv_bfloat16>(tr, tc, tv, p, batch, idesc, st);
+    default: return launch_vt<KATOMS, MODE, __half>(tr, tc, tv, p, batch, idesc, st);
   }
 }
 
 template <int MODE>
 int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols, int64_t rp,
            int proj_dtype, Params& p, cudaStream_t st) {
-  CUtensorMap tr, tc;
+  CUtensorMap tr, tc, tv;
   const bool bf16 = proj_dtype == JK_BF16;
   int status = make_tmap_3d_16bit(&tr, row_proj, rp, n_rows, batch, 64, kRows, bf16);
   if (status != JK_OK) return status;
   status = make_tmap_3d_16bit(&tc, col_proj, rp, n_cols, batch, 64, kCols, bf16);
   if (status != JK_OK) return status;
-  const uint32_t idesc = idesc_f16(kRows, kCols, bf16 ? 1u : 0u);
-  const bool small_k = p.k <= 32;
-  if (rp == 64) {
-    return small_k ? launch_k<32, 1, MODE>(tr, tc, p, batch, idesc, st)
-                   : launch_k<64, 1, MODE>(tr, tc, p, batch, idesc, st);
+  tv = tc;  // placeholder when the slab path is off
+  p.slab_ok = 0;
+  if (MODE == kGather && p.window >= 0 && p.val_dtype != JK_F32 && p.dim % 64 == 0 && aligned16(p.col_val)) {
+    if (make_tmap_3d_16bit(&tv, p.col_val, p.dim, n_cols, batch, 64, 128, p.val_dtype == JK_BF16, false) == JK_OK)
+      p.slab_ok = 1;
   }
-  return small_k ? launch_k<32, 2, MODE>(tr, tc, p, batch, idesc, st)
-                 : launch_k<64, 2, MODE>(tr, tc, p, batch, idesc, st);
+  const uint32_t idesc = idesc_f16(kRows, kCols, bf16 ? 1u : 0u);
+  if (rp == 64) return launch_k<1, MODE>(tr, tc, tv, p, batch, idesc, st);
+  return launch_k<2, MODE>(tr, tc, tv, p, batch, idesc, st);
 }
 
 int validate_common(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols,

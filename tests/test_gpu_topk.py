@@ -62,11 +62,13 @@ def test_projection_matches_oracle(dev, rows, dim, rank):
         # f32 accumulation order differs from the float64 oracle: allow rare 1-ulp flips.
         diff = got[:, :rank] != ref
         assert diff.mean() < 2e-3, f"{diff.mean():.2e} of projections differ"
-        # A flip is one rounding step of the (near-identical) f32 sum: within 2^-7 relative,
+        # A flip is one rounding step of the (near-identical) f32 sum, which the later
+        # multiply / divide roundings can carry into up to a few final ulps (2^-6 relative),
         # or tiny in absolute terms where the dot product cancels to ~0.
         err = np.abs(got[:, :rank] - ref)
         scale = 1.0 if c is None else np.abs(_np(c))[None, :] / temp
-        assert np.all(err <= 2 ** -7 * np.abs(ref) + 2e-5 * scale)
+        bad = err > 2 ** -6 * np.abs(ref) + 2e-5 * scale
+        assert not bad.any(), (err[bad][:5], ref[bad][:5], got[:, :rank][bad][:5])
 
 
 def _check_topk(dev, B, N, D, R, k, window, compress_name, seed, n_cols=None, sender=False):
@@ -117,3 +119,49 @@ def test_topk_config2_reduced(dev):
 
 def test_topk_rank_128(dev):
     _check_topk(dev, B=1, N=400, D=64, R=100, k=16, window=-1, compress_name="softsign", seed=5)
+
+
+def _check_given(dev, val_rows, k, window, compress_name="softsign", seed=0):
+    """Parity on caller-shaped inputs (exercises the threshold fallback path)."""
+    jk = _jk()
+    g = np.random.default_rng(seed)
+    B, N, D = val_rows.shape
+    R = 64
+    val = _bf16(val_rows, dev)
+    state = _bf16(g.standard_normal((B, N)), dev)
+    wt = _bf16(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    ws = _bf16(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    core = _bf16(np.full(R, 1.0 / np.sqrt(R)), dev)
+    row_proj = jk.lowrank_project(val, wt)
+    col_proj = jk.lowrank_project(val, ws, core=core)
+    code = {"softsign": 0, "signed_abs_softmax": 1, "signed_entmax15": 2, "softmax": 3}[compress_name]
+    st, vv, sc, ix = jk.topk_aggregate(row_proj, col_proj, state, val, k, window=window, compress=code,
+                                       out_dtype=torch.float32, return_selection=True)
+    torch.cuda.synchronize()
+    rp_, cp_ = _np(row_proj), _np(col_proj)
+    o_st, o_val, o_sc, o_ix = oracle.propagation_topk(rp_, cp_, _np(state), _np(val), k,
+                                                      window=None if window < 0 else window,
+                                                      compress_name=compress_name)
+    parity.set_full_scores(oracle.lowrank_scores(rp_, cp_, 0.0))
+    ties = parity.tie_rows(_np(ix).astype(np.int64), o_ix, o_sc)
+    parity.assert_rows_close(_np(vv), o_val, ties, what="val")
+    parity.assert_rows_close(_np(st), o_st, ties, what="state")
+    return ties
+
+
+def test_topk_all_equal_scores_fallback(dev):
+    # Every row identical -> every score equal: the threshold pass overflows, the exact
+    # fallback keeps the k lowest columns (ties to the lower index).
+    row = np.random.default_rng(7).standard_normal((1, 1, 64))
+    val = np.repeat(row, 600, axis=1)
+    _check_given(dev, val, k=16, window=-1)
+    _check_given(dev, val, k=32, window=300)
+
+
+def test_topk_bimodal_scores(dev):
+    # Two clusters of rows far apart: strongly non-normal score rows.
+    g = np.random.default_rng(8)
+    val = g.standard_normal((2, 700, 64))
+    val[:, ::7] *= 12.0
+    ties = _check_given(dev, val, k=32, window=-1)
+    assert ties.mean() < 0.05
