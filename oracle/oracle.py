@@ -26,6 +26,10 @@ __all__ = [
     "compress",
     "entmax15",
     "signed_entmax15",
+    "topk_from_scores",
+    "masked_dense_from_scores",
+    "sparse_transition_from_logits",
+    "dense_transition_from_logits",
     "propagation_topk",
     "propagation_masked_dense",
     "transition_pairwise_topk",
@@ -160,9 +164,10 @@ def compress(sel_scores: np.ndarray, name: str) -> np.ndarray:
 
 
 # ----------------------------------------------------------------------------- operators
-def propagation_topk(row_proj, col_proj, col_state, col_val, k: int, *, window: int | None = None,
-                     bias: float = 0.0, compress_name: str = "softsign", col_sender=None):
-    """Per-row top-k propagation / per-query transition.
+def topk_from_scores(scores, col_state, col_val, k: int, *, window: int | None = None, bias: float = 0.0,
+                     compress_name: str = "softsign", col_sender=None):
+    """Top-k propagation / per-query transition on a given score tensor [B, T, S] (bias
+    not included; added after selection, which leaves the selection unchanged).
 
     window None: reference SparsePropagation(sparse_type="topk") -- top-k over every source
     (propagation.py:453-480, no causal mask; native kernel jakal_net_native_cuda.cu:1029-1183).
@@ -172,7 +177,7 @@ def propagation_topk(row_proj, col_proj, col_state, col_val, k: int, *, window: 
     multiplied by the sender strength of the picked source.
     Returns (state [B,T], val [B,T,D], sel_scores [B,T,k] (-inf pad), sel_index [B,T,k] (-1 pad)).
     """
-    sc = lowrank_scores(row_proj, col_proj, 0.0)
+    sc = np.asarray(scores, np.float64)
     B, T, S = sc.shape
     vis = causal_window_visible(T, S, window)
     st = np.asarray(col_state, np.float64)
@@ -198,14 +203,19 @@ def propagation_topk(row_proj, col_proj, col_state, col_val, k: int, *, window: 
     return out_state, out_val, sel_scores, sel_index
 
 
-def propagation_masked_dense(row_proj, col_proj, col_state, col_val, *, window: int | None,
-                             bias: float = 0.0, compress_name: str = "softsign"):
-    """Dense (window None) or causal-window propagation without top-k.
+def propagation_topk(row_proj, col_proj, col_state, col_val, k: int, *, window: int | None = None,
+                     bias: float = 0.0, compress_name: str = "softsign", col_sender=None):
+    """topk_from_scores on the low-rank scores row_proj . col_proj (modules.py:93-100)."""
+    return topk_from_scores(lowrank_scores(row_proj, col_proj, 0.0), col_state, col_val, k, window=window,
+                            bias=bias, compress_name=compress_name, col_sender=col_sender)
 
-    propagation.py:207-220 (dense) and :453-480 with the window mask; edges are compressed
-    over each row's visible sources (propagation.py:67-88), masked entries contribute 0.
-    """
-    sc = lowrank_scores(row_proj, col_proj, bias)
+
+def masked_dense_from_scores(scores, col_state, col_val, *, window: int | None, compress_name: str = "softsign"):
+    """Dense (window None) or causal-window propagation without top-k on a score tensor
+    (bias included): propagation.py:207-220 (dense) and :453-480 with the window mask; edges
+    are compressed over each row's visible sources (propagation.py:67-88), masked entries
+    contribute 0."""
+    sc = np.asarray(scores, np.float64)
     B, T, S = sc.shape
     vis = causal_window_visible(T, S, window)
     st = np.asarray(col_state, np.float64)
@@ -223,13 +233,19 @@ def propagation_masked_dense(row_proj, col_proj, col_state, col_val, *, window: 
     return out_state, out_val
 
 
-def transition_pairwise_topk(src_proj, dst_proj, src_state, src_val, src_sender, k: int, *,
-                             bias: float = 0.0, compress_name: str = "softmax"):
-    """Per-source sparse transition (SparseTransition, transition.py:431-452 / 483-590;
-    native jakal_net_native.cpp:6916-7087): every source picks its top-k destinations by
-    route logit, routes are compressed over those k, weighted by the sender strength and
-    scatter-added into the destinations."""
-    lg = lowrank_scores(src_proj, dst_proj, 0.0)
+def propagation_masked_dense(row_proj, col_proj, col_state, col_val, *, window: int | None,
+                             bias: float = 0.0, compress_name: str = "softsign"):
+    """masked_dense_from_scores on the low-rank scores."""
+    return masked_dense_from_scores(lowrank_scores(row_proj, col_proj, bias), col_state, col_val, window=window,
+                                    compress_name=compress_name)
+
+
+def sparse_transition_from_logits(logits, src_state, src_val, src_sender, k: int, *, compress_name: str = "softmax"):
+    """Per-source sparse transition on route logits [B, S, Dn] (bias included)
+    (SparseTransition, transition.py:431-452 / 483-590; native jakal_net_native.cpp:6916-7087):
+    every source picks its top-k destinations, routes are compressed over those k, weighted
+    by the sender strength and scatter-added into the destinations."""
+    lg = np.asarray(logits, np.float64)
     B, S, Dn = lg.shape
     st = np.asarray(src_state, np.float64)
     val = np.asarray(src_val, np.float64)
@@ -240,10 +256,17 @@ def transition_pairwise_topk(src_proj, dst_proj, src_state, src_val, src_sender,
     for b in range(B):
         for i in range(S):
             idx = select_topk(lg[b, i], allv, k)
-            r = compress(lg[b, i, idx] + bias, compress_name) * snd[b, i]
+            r = compress(lg[b, i, idx], compress_name) * snd[b, i]
             np.add.at(out_state[b], idx, r * st[b, i])
             out_val[b, idx] += r[:, None] * val[b, i][None, :]
     return out_state, out_val
+
+
+def transition_pairwise_topk(src_proj, dst_proj, src_state, src_val, src_sender, k: int, *,
+                             bias: float = 0.0, compress_name: str = "softmax"):
+    """sparse_transition_from_logits on the low-rank route logits."""
+    return sparse_transition_from_logits(lowrank_scores(src_proj, dst_proj, bias), src_state, src_val, src_sender, k,
+                                         compress_name=compress_name)
 
 
 def transition_query_topk(query_proj, source_proj, src_state, src_val, src_sender, k: int, *,
@@ -255,11 +278,10 @@ def transition_query_topk(query_proj, source_proj, src_state, src_val, src_sende
                             compress_name="softmax", col_sender=src_sender)
 
 
-def transition_dense(src_proj, dst_proj, src_state, src_val, src_sender, *, bias: float = 0.0,
-                     compress_name: str = "softmax"):
-    """Dense transition (transition.py:238-254): routes compressed over all destinations
-    per source, weighted by the sender strength, summed into every destination."""
-    lg = lowrank_scores(src_proj, dst_proj, bias)
+def dense_transition_from_logits(logits, src_state, src_val, src_sender, *, compress_name: str = "softmax"):
+    """Dense transition (transition.py:238-254) on route logits: routes compressed over all
+    destinations per source, weighted by the sender strength, summed into every destination."""
+    lg = np.asarray(logits, np.float64)
     B, S, Dn = lg.shape
     st = np.asarray(src_state, np.float64)
     val = np.asarray(src_val, np.float64)
@@ -269,3 +291,10 @@ def transition_dense(src_proj, dst_proj, src_state, src_val, src_sender, *, bias
         for i in range(S):
             routes[b, i] = compress(lg[b, i], compress_name) * snd[b, i]
     return np.einsum("bsd,bs->bd", routes, st), np.einsum("bsd,bsv->bdv", routes, val)
+
+
+def transition_dense(src_proj, dst_proj, src_state, src_val, src_sender, *, bias: float = 0.0,
+                     compress_name: str = "softmax"):
+    """dense_transition_from_logits on the low-rank route logits."""
+    return dense_transition_from_logits(lowrank_scores(src_proj, dst_proj, bias), src_state, src_val, src_sender,
+                                        compress_name=compress_name)

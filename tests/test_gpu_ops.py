@@ -1,0 +1,136 @@
+"""GPU parity of the reference-facing ops (the native-module contract of jakal_net_b200)
+against the CPU oracle, through the C ABI, on seeded bf16 inputs.
+
+The oracle is evaluated on the same bf16 projections the library produced
+(jk.lowrank_project), so the comparison isolates the fused kernels; outputs are bf16 like
+the reference op returns them, hence the bf16 rounding step in the tolerance."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import parity
+
+pytestmark = pytest.mark.gpu
+OUT_RTOL = parity.VAL_RTOL + 2 ** -8  # kernel tolerance + one bf16 rounding of the output
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return torch.device("cuda", 0)
+
+
+def _t(a, dev, dtype=torch.bfloat16):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev).to(dtype)
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+@pytest.mark.parametrize("compress", ["softsign", "signed_abs_softmax", "signed_entmax15"])
+@pytest.mark.parametrize("k", [3, 32])
+def test_propagation_topk_op(dev, compress, k):
+    import jakal_net_b200 as jk
+
+    g = np.random.default_rng(11 + k)
+    B, N, D, R = 2, 333, 96, 64
+    val = _t(g.standard_normal((B, N, D)), dev)
+    state = _t(g.standard_normal((B, N)), dev)
+    w_s = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    w_t = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    core = _t(np.full(R, R ** -0.5), dev, torch.float32)
+    bias = torch.tensor(0.05, device=dev)
+    st, vv = jk.propagation_topk("low_rank_bilinear", core, bias, w_s, None, w_t, None, compress, val, state, val,
+                                 k, 128, 128)
+    assert st.dtype == torch.bfloat16 and vv.shape == val.shape
+    pt = _np(jk.lowrank_project(val, w_t))
+    ps = _np(jk.lowrank_project(val, w_s, core=core))
+    o_st, o_val, _, _ = oracle.propagation_topk(pt, ps, _np(state), _np(val), k, bias=0.05, compress_name=compress)
+    parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
+    parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")
+
+
+def test_propagation_window_topk_op_state_weighted(dev):
+    # state_weight_edges folds softplus(state) into the projected inputs (propagation.py:165-174)
+    import jakal_net_b200 as jk
+
+    g = np.random.default_rng(5)
+    B, N, D, R, W, k = 3, 700, 128, 64, 200, 16
+    val = _t(g.standard_normal((B, N, D)), dev)
+    state = _t(g.standard_normal((B, N)), dev)
+    w_s = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    w_t = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    core = _t(np.linspace(0.05, 0.2, R), dev)
+    strength = torch.nn.functional.softplus(state.float())
+    pstate = strength.to(torch.bfloat16)
+    pval = (val.float() * strength[..., None]).to(torch.bfloat16)
+    st, vv = jk.propagation_window_topk("low_rank_bilinear", core, None, w_s, None, w_t, None, "softsign", val,
+                                        pstate, pval, W, k)
+    pt = _np(jk.lowrank_project(val, w_t))
+    ps = _np(jk.lowrank_project(val, w_s, core=core))
+    o_st, o_val, _, _ = oracle.propagation_topk(pt, ps, _np(pstate), _np(pval), k, window=W)
+    parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
+    parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")
+
+
+@pytest.mark.parametrize("temperature", [1.0, 0.5])
+def test_transition_query_topk_op(dev, temperature):
+    import jakal_net_b200 as jk
+
+    g = np.random.default_rng(21)
+    B, S, Q, D, R, k = 2, 1500, 200, 64, 64, 16
+    src = _t(g.standard_normal((B, S, D)), dev)
+    qv = _t(0.02 * g.standard_normal((B, Q, D)), dev)
+    sstate = _t(g.standard_normal((B, S)), dev)
+    w_s = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    w_t = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    core = _t(np.ones(R), dev)
+    bias = torch.tensor(0.3, device=dev)
+    sender = torch.nn.functional.softplus(sstate.float()).to(torch.bfloat16)
+    st, vv = jk.transition_query_topk("low_rank_bilinear_route", w_s, None, w_t, None, core, bias, None, None, None,
+                                      None, temperature, sender, src, qv, sstate, src, k, 128, 128, True)
+    sp = _np(jk.lowrank_project(src, w_s, core=core, temperature=temperature))
+    qp = _np(jk.lowrank_project(qv, w_t))
+    o_st, o_val, _, _ = oracle.transition_query_topk(qp, sp, _np(sstate), _np(src), _np(sender), k,
+                                                     bias=0.3 / temperature)
+    parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
+    parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")
+
+
+@pytest.mark.parametrize("compress", ["softmax", "signed_abs_softmax", "signed_entmax15"])
+def test_transition_pairwise_topk_op(dev, compress):
+    import jakal_net_b200 as jk
+
+    g = np.random.default_rng(31)
+    B, S, Dn, D, R, k = 2, 700, 150, 64, 64, 8
+    src = _t(g.standard_normal((B, S, D)), dev)
+    dst = _t(g.standard_normal((B, Dn, D)), dev)
+    sstate = _t(g.standard_normal((B, S)), dev)
+    w_s = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    w_t = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    core = _t(np.ones(R), dev)
+    sender = torch.nn.functional.softplus(sstate.float()).to(torch.bfloat16)
+    st, vv = jk.transition_pairwise_topk("low_rank_bilinear_route", w_s, None, w_t, None, core, None, None, None,
+                                         None, None, 1.0, sender, src, dst, sstate, src, k, 128, 128,
+                                         route_compress_name=compress)
+    sp = _np(jk.lowrank_project(src, w_s, core=core))
+    dp = _np(jk.lowrank_project(dst, w_t))
+    o_st, o_val = oracle.transition_pairwise_topk(sp, dp, _np(sstate), _np(src), _np(sender), k,
+                                                  compress_name=compress)
+    parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
+    parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")
+
+
+def test_device_status_is_clean_after_the_ops(dev):
+    import ctypes
+
+    import jakal_net_b200 as jk
+
+    status = ctypes.c_int(-99)
+    assert jk._LIBRARY.jk_device_status(None, ctypes.byref(status)) == 0
+    assert status.value == 0
