@@ -150,6 +150,30 @@ int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_pr
                                         int compress, float* accum, void* out_state,
                                         void* out_val, int out_dtype, jk_stream_t stream);
 
+/*
+ * Allocation-free per-source sparse transition. No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory at call time -- plain-C / FFI hosts with no
+ * device allocator of their own, and latency-critical loops that must not call cudaMalloc /
+ * cudaFree because those can synchronise the device. Same contract as
+ * jk_transition_pairwise_topk_forward without the `accum` argument: the f32 scratch is a
+ * fixed 16 MiB device array inside the library (held on every GPU that loads it until exit),
+ * so B * n_dst * (dim + 1) must not exceed jk_transition_pairwise_topk_noalloc_capacity()
+ * floats, else JK_ERR_BAD_SHAPE. The first call on a device resolves the array's address
+ * (make it before any stream capture). Calls share the array: calls that overlap on the GPU
+ * race; serialise them on one stream. The scratch is zeroed on the stream by every call.
+ */
+int jk_transition_pairwise_topk_forward_noalloc(const void* src_proj, const void* dst_proj,
+                                                int64_t batch, int64_t n_src, int64_t n_dst,
+                                                int64_t rp, int proj_dtype, const void* src_state,
+                                                const void* src_sender, int state_dtype,
+                                                const void* src_val, int64_t dim, int val_dtype,
+                                                int64_t k, float score_bias, const float* bias_dev,
+                                                int compress, void* out_state, void* out_val,
+                                                int out_dtype, jk_stream_t stream);
+
+/* Scratch capacity (in f32 elements) of the allocation-free entry point above. */
+int64_t jk_transition_pairwise_topk_noalloc_capacity(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -3,3 +3,4 @@
 #include "jk_host.cu"
 #include "jk_project.cu"
 #include "jk_topk.cu"
+#include "jk_noalloc.cu"

@@ -62,6 +62,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _i64, _f32, _p, _i32,
          _p, _p, _p, _i32, _p],
     ),
+    "jk_transition_pairwise_topk_forward_noalloc": (
+        _i32,
+        [_p, _p, _i64, _i64, _i64, _i64, _i32,
+         _p, _p, _i32,
+         _p, _i64, _i32,
+         _i64, _f32, _p, _i32,
+         _p, _p, _i32, _p],
+    ),
+    "jk_transition_pairwise_topk_noalloc_capacity": (_i64, []),
 }
 
 _LIB: ctypes.CDLL | None = None
