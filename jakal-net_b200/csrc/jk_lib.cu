@@ -3,4 +3,5 @@
 #include "jk_host.cu"
 #include "jk_project.cu"
 #include "jk_topk.cu"
+#include "jk_window.cu"
 #include "jk_noalloc.cu"

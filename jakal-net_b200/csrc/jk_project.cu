@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* done = empty + kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ float core_s[128];  // core weight widened once per CTA (1.0 when absent)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -59,6 +60,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
+  }
+  if (threadIdx.x < 128) {
+    float cw = 1.f;
+    if (p.core != nullptr && threadIdx.x < p.rank) {
+      cw = p.bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.core)[threadIdx.x])
+                  : __half2float(reinterpret_cast<const __half*>(p.core)[threadIdx.x]);
+    }
+    core_s[threadIdx.x] = cw;
   }
   if (warp == 0) tmem_alloc(tmem_slot, RP < 32 ? 32 : RP);
   tc_fence_before();
@@ -141,17 +150,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 x = 0.f;
               } else if (p.bf16) {
                 x = __bfloat162float(__float2bfloat16_rn(x));
-                if (p.core) {
-                  const float cw = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.core)[c]);
-                  x = __bfloat162float(__float2bfloat16_rn(x * cw));
-                }
+                if (p.core) x = __bfloat162float(__float2bfloat16_rn(x * core_s[c]));
                 if (p.temperature != 1.f) x = __bfloat162float(__float2bfloat16_rn(x / p.temperature));
               } else {
                 x = __half2float(__float2half_rn(x));
-                if (p.core) {
-                  const float cw = __half2float(reinterpret_cast<const __half*>(p.core)[c]);
-                  x = __half2float(__float2half_rn(x * cw));
-                }
+                if (p.core) x = __half2float(__float2half_rn(x * core_s[c]));
                 if (p.temperature != 1.f) x = __half2float(__float2half_rn(x / p.temperature));
               }
               f[h] = x;

@@ -163,6 +163,20 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand in the 128-byte-swizzle layout a
+// TMA box of {64 elements along MN, rows along K} writes: each K row is 128 B (64 MN
+// elements), 8 K rows form a 1024 B atom (stride byte offset), and the next 64 MN elements
+// live `mn_atom_bytes` further (leading byte offset, one TMA box per 64 MN elements).
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t smem_addr, uint32_t mn_atom_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((mn_atom_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with f32 accumulation, both operands K-major.
 // ab_format: 0 = f16, 1 = bf16.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, uint32_t ab_format) {

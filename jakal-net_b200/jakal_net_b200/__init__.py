@@ -25,8 +25,12 @@ __all__ = [
     "supported_ops",
     "supported_devices",
     "backend_name",
+    "propagation_dense",
+    "propagation_window",
+    "propagation_query_dense",
     "propagation_topk",
     "propagation_window_topk",
+    "masked_aggregate",
     "transition_query_topk",
     "transition_pairwise_topk",
     "lowrank_project",
@@ -50,6 +54,9 @@ _ROUTE_CODE = {
 _MAX_K = 64
 
 _SUPPORTED_OPS = (
+    "propagation_dense",
+    "propagation_window",
+    "propagation_query_dense",
     "propagation_topk",
     "transition_pairwise_topk",
     "transition_query_topk",
@@ -349,3 +356,98 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
         )
     return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
             out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))
+
+
+def masked_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, *, window: int = -1,
+                     compress: int = _lib.JK_SOFTSIGN, bias: Optional[Tensor] = None, score_bias: float = 0.0,
+                     out_dtype: Optional[torch.dtype] = None):
+    """Raw fused window / dense aggregate over already-projected inputs
+    (jk_propagation_window_forward). row_proj [B, T, rp], col_proj [B, S, rp], col_state [B, S],
+    col_val [B, S, D] in the projections' dtype, D a multiple of 64. window -1 = dense."""
+    for name, t in (("row_proj", row_proj), ("col_proj", col_proj), ("col_state", col_state), ("col_val", col_val)):
+        _require_cuda(name, t)
+    B, T, rp = row_proj.shape
+    S = col_proj.shape[1]
+    D = col_val.shape[-1]
+    dev = col_val.device
+    out_dtype = out_dtype or col_val.dtype
+    out_state = torch.empty((B, T), device=dev, dtype=out_dtype)
+    out_val = torch.empty((B, T, D), device=dev, dtype=out_dtype)
+    with torch.cuda.device(dev):
+        check(
+            _LIBRARY.jk_propagation_window_forward(
+                row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj),
+                col_state.data_ptr(), _dtype_code("state", col_state), col_val.data_ptr(), D,
+                int(window), float(score_bias), _ptr(bias), compress,
+                out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state), _stream(dev)),
+            "jk_propagation_window_forward",
+        )
+    return out_state, out_val
+
+
+def _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, target_val,
+                 source_val, projected_state, projected_val, window: int, source_state=None):
+    if edge_compress_name not in _EDGE_CODE:
+        raise RuntimeError(
+            "Only edge_compress_name in {softsign, signed_abs_softmax, signed_entmax15} is supported by the native backend."
+        )
+    for name, t in (("target_val", target_val), ("source_val", source_val), ("projected_state", projected_state),
+                    ("projected_val", projected_val)):
+        _require_cuda(name, t)
+    if kind != "low_rank_bilinear":
+        raise RuntimeError(f"Unsupported pairwise kernel kind for b200_sm100a: {kind}")
+    if in_weight is None or out_weight is None:
+        raise RuntimeError("Low-rank bilinear pairwise kernel is missing projection weights.")
+    batch_shape = target_val.shape[:-2]
+    n_t = target_val.shape[-2]
+    out_dim = projected_val.shape[-1]
+    tv = _flatten_val(target_val)
+    sv = _flatten_val(source_val)
+    pstate = _flatten_state(projected_state)
+    pval = _flatten_val(projected_val)
+    if source_state is not None and source_state.numel() != 0:
+        # edges weighted by the source state (jakal_net_native.cpp:6010-6013) == folding the
+        # weight into the aggregated inputs
+        ss = _flatten_state(source_state).float()
+        pstate = (pstate.float() * ss).to(pstate.dtype)
+        pval = (pval.float() * ss[..., None]).to(pval.dtype)
+    if pval.dtype != tv.dtype:
+        pval = pval.to(tv.dtype)
+    if out_dim % 64 != 0:
+        raise RuntimeError(f"b200_sm100a window/dense propagation needs a value width that is a multiple of 64 (got {out_dim}).")
+    row_proj = lowrank_project(tv, out_weight)
+    col_proj = lowrank_project(sv, in_weight, core=weight)
+    same = projected_state.dtype == projected_val.dtype
+    out_dtype = projected_val.dtype if same else torch.float32
+    st, out = masked_aggregate(row_proj, col_proj, pstate, pval, window=window,
+                               compress=_EDGE_CODE[edge_compress_name], bias=_bias_tensor(bias, tv.device),
+                               out_dtype=out_dtype)
+    return (st.to(projected_state.dtype).reshape(*batch_shape, n_t),
+            out.to(projected_val.dtype).reshape(*batch_shape, n_t, out_dim))
+
+
+def propagation_window(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, layer_val,
+                       projected_state, projected_val, window, target_block_size, source_block_size):
+    """SparsePropagation(sparse_type="window") forward: causal window [t - window, t], edges
+    compressed over the visible sources, aggregate (jakal_net_native.cpp:6190-6303;
+    propagation.py:453-480)."""
+    if window < 0:
+        raise RuntimeError("window must be non-negative.")
+    return _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, layer_val,
+                        layer_val, projected_state, projected_val, int(window))
+
+
+def propagation_dense(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, layer_val,
+                      projected_state, projected_val, source_state, target_block_size, source_block_size):
+    """Dense Propagation forward: every (target, source) pair (jakal_net_native.cpp:5962-6076;
+    propagation.py:207-220)."""
+    return _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, layer_val,
+                        layer_val, projected_state, projected_val, -1, source_state)
+
+
+def propagation_query_dense(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
+                            query_val, source_val, projected_state, projected_val, query_block_size,
+                            source_block_size):
+    """Dense query propagation: query rows score every source row (jakal_net_native.cpp:6078-6188)."""
+    return _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, query_val,
+                        source_val, projected_state, projected_val, -1)

@@ -46,6 +46,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _i64, _i64, _f32, _p, _i32,            # k, window, score_bias, bias_dev, compress
          _p, _p, _i32, _p, _p, _p],             # out_state, out_val, out_dtype, out_scores, out_index, stream
     ),
+    "jk_propagation_window_forward": (
+        _i32,
+        [_p, _p, _i64, _i64, _i64, _i64, _i32,  # row_proj, col_proj, B, n_rows, n_cols, rp, proj_dtype
+         _p, _i32, _p, _i64,                    # col_state, state_dtype, col_val, dim
+         _i64, _f32, _p, _i32,                  # window, score_bias, bias_dev, compress
+         _p, _p, _i32, _p],                     # out_state, out_val, out_dtype, stream
+    ),
     "jk_transition_query_topk_forward": (
         _i32,
         [_p, _p, _i64, _i64, _i64, _i64, _i32,

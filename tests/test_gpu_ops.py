@@ -134,3 +134,52 @@ def test_device_status_is_clean_after_the_ops(dev):
     status = ctypes.c_int(-99)
     assert jk._LIBRARY.jk_device_status(None, ctypes.byref(status)) == 0
     assert status.value == 0
+
+
+@pytest.mark.parametrize("compress", ["softsign", "signed_abs_softmax", "signed_entmax15"])
+@pytest.mark.parametrize("shape", [(2, 300, 128, 40), (1, 700, 384, 512), (2, 256, 64, -1), (1, 1024, 512, 511)])
+def test_window_and_dense_propagation_op(dev, compress, shape):
+    import jakal_net_b200 as jk
+
+    B, N, D, W = shape
+    g = np.random.default_rng(N + D)
+    R = 64
+    val = _t(g.standard_normal((B, N, D)), dev)
+    state = _t(g.standard_normal((B, N)), dev)
+    w_s = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    w_t = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    core = _t(np.full(R, R ** -0.5), dev)
+    bias = torch.tensor(-0.1, device=dev)
+    if W >= 0:
+        st, vv = jk.propagation_window("low_rank_bilinear", core, bias, w_s, None, w_t, None, compress, val, state,
+                                       val, W, 128, 128)
+    else:
+        st, vv = jk.propagation_dense("low_rank_bilinear", core, bias, w_s, None, w_t, None, compress, val, state,
+                                      val, None, 128, 128)
+    pt = _np(jk.lowrank_project(val, w_t))
+    ps = _np(jk.lowrank_project(val, w_s, core=core))
+    o_st, o_val = oracle.propagation_masked_dense(pt, ps, _np(state), _np(val), window=None if W < 0 else W,
+                                                  bias=-0.1, compress_name=compress)
+    parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
+    parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")
+
+
+def test_query_dense_propagation_op(dev):
+    import jakal_net_b200 as jk
+
+    g = np.random.default_rng(77)
+    B, Q, S, D, R = 2, 130, 900, 192, 64
+    qv = _t(g.standard_normal((B, Q, D)), dev)
+    sv = _t(g.standard_normal((B, S, D)), dev)
+    state = _t(g.standard_normal((B, S)), dev)
+    w_s = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    w_t = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    core = _t(np.full(R, R ** -0.5), dev)
+    st, vv = jk.propagation_query_dense("low_rank_bilinear", core, None, w_s, None, w_t, None, "signed_abs_softmax",
+                                        qv, sv, state, sv, 128, 128)
+    pt = _np(jk.lowrank_project(qv, w_t))
+    ps = _np(jk.lowrank_project(sv, w_s, core=core))
+    o_st, o_val = oracle.propagation_masked_dense(pt, ps, _np(state), _np(sv), window=None,
+                                                  compress_name="signed_abs_softmax")
+    parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
+    parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")
