@@ -33,6 +33,10 @@ extern "C" {
 #define JK_F32 0
 #define JK_BF16 1
 #define JK_F16 2
+/* Projection planes only: f32 projections (rank <= 32) stored as three bf16 planes
+ * [h | m | l | 0] of 32 columns each (rp = 128), see jk_split3_bf16; the score tiles then
+ * sum the six cross products, which reproduces an f32 dot product. */
+#define JK_BF16X3 3
 
 /* ---- edge / route compressors --------------------------------------------------------- */
 #define JK_SOFTSIGN 0              /* s / (1 + |s|)                       propagation.py:85   */
@@ -89,7 +93,7 @@ int jk_lowrank_project(const void* x, int64_t rows, int64_t dim, const void* w, 
  * score_bias is added to every score; when bias_dev != NULL the f32 it points to (device
  * memory) is added as well, so a bias tensor needs no host synchronisation.
  * Shapes: row_proj [B, n_rows, rp], col_proj [B, n_cols, rp] (rp = jk_padded_rank, dtype
- * proj_dtype = JK_BF16 | JK_F16); col_state and col_sender [B, n_cols] in state_dtype;
+ * proj_dtype = JK_BF16 | JK_F16 | JK_BF16X3); col_state and col_sender [B, n_cols] in state_dtype;
  * col_val [B, n_cols, dim] in val_dtype; out_state [B, n_rows], out_val [B, n_rows, dim] in
  * out_dtype. Optional out_scores f32 [B, n_rows, k] (score + bias, sorted descending,
  * -inf in empty slots) and out_index int64 [B, n_rows, k] (-1 in empty slots).
@@ -106,6 +110,36 @@ int jk_propagation_topk_forward(const void* row_proj, const void* col_proj, int6
                                 int64_t window, float score_bias, const float* bias_dev,
                                 int compress, void* out_state, void* out_val, int out_dtype,
                                 float* out_scores, int64_t* out_index, jk_stream_t stream);
+
+/*
+ * Fused window / dense propagation without top-k (flash-style: tcgen05 score tile -> exact
+ * f32 edges -> bf16 hi + lo edge tiles -> tcgen05 value GEMM, TMEM accumulator):
+ *   visible(t,s) = s < n_cols and (window < 0 or t - window <= s <= t)
+ *   e[t,s]       = compress over the visible s of row t of (score + score_bias (+ *bias_dev))
+ *                  compress = JK_SOFTSIGN | JK_SIGNED_ABS_SOFTMAX | JK_SIGNED_ENTMAX15
+ *   out_state[b,t] = sum_s e * col_state[b,s],  out_val[b,t,:] = sum_s e * col_val[b,s,:]
+ * row_proj [B,n_rows,rp], col_proj [B,n_cols,rp] (JK_BF16 | JK_F16 | JK_BF16X3); col_val
+ * [B,n_cols,dim] in the projections' 16-bit type (bf16 for JK_BF16X3), dim % 64 == 0; for
+ * f32 values pass the bf16 hi plane as col_val and the lo plane as col_val_lo (see
+ * jk_split2_bf16), else col_val_lo = NULL. col_state in state_dtype; outputs in out_dtype.
+ * Replaces propagation_window / propagation_dense / propagation_query_dense
+ * (jakal_net_native.cpp:6190-6303, 5962-6076, 6078-6188) and the CUDA kernels
+ * jakal_net_native_cuda.cu:1579-1750, 2023-2109, 1388-1576.
+ */
+int jk_propagation_window_forward(const void* row_proj, const void* col_proj, int64_t batch,
+                                  int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
+                                  const void* col_state, int state_dtype, const void* col_val,
+                                  const void* col_val_lo, int64_t dim, int64_t window,
+                                  float score_bias, const float* bias_dev, int compress,
+                                  void* out_state, void* out_val, int out_dtype,
+                                  jk_stream_t stream);
+
+/* f32 -> three bf16 planes [h|m|l|0] of 32 columns (rank <= 32), out [rows, 128] bf16, for
+ * JK_BF16X3 projections. Replaces nothing: the reference computes these dots in f32. */
+int jk_split3_bf16(const float* x, int64_t rows, int64_t rank, void* out, jk_stream_t stream);
+
+/* f32 -> bf16 hi plane + bf16 lo plane (x - hi), n elements each, for f32 values. */
+int jk_split2_bf16(const float* x, int64_t n, void* hi, void* lo, jk_stream_t stream);
 
 /*
  * Per-query ("query top-k") transition: identical contract to

@@ -4,4 +4,5 @@
 #include "jk_project.cu"
 #include "jk_topk.cu"
 #include "jk_window.cu"
+#include "jk_split.cu"
 #include "jk_noalloc.cu"

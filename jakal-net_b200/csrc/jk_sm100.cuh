@@ -187,6 +187,34 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, uint32_t ab_forma
          | ((uint32_t)(M >> 4) << 24);  // M / 16
 }
 
+// Score tile MMAs: D = A . B^T over the padded rank. Plain 16-bit projections: K steps
+// 0 .. 4*KATOMS-1 pair with themselves. Three-plane bf16 split of f32 projections (rank
+// <= 32, planes h | m | l at K steps {0,1} {2,3} {4,5} of a 128-wide row): the six products
+// hh, hm, mh, hl, lh, mm reproduce an f32 dot product.
+template <int KATOMS>
+__device__ __forceinline__ void score_mmas(uint32_t tmem_d, uint32_t a_addr, uint32_t b_addr, uint32_t idesc,
+                                           bool split3) {
+  constexpr uint32_t kAtom = 128 * 128;
+  if (KATOMS == 2 && split3) {
+    const int pa[6] = {0, 0, 1, 0, 2, 1};
+    const int pb[6] = {0, 1, 0, 2, 0, 1};
+#pragma unroll
+    for (int q = 0; q < 12; ++q) {
+      const int sa = pa[q >> 1] * 2 + (q & 1);
+      const int sb = pb[q >> 1] * 2 + (q & 1);
+      const uint32_t oa = (sa >> 2) * kAtom + (sa & 3) * 32;
+      const uint32_t ob = (sb >> 2) * kAtom + (sb & 3) * 32;
+      mma_f16_ss(tmem_d, sdesc_kmajor_sw128(a_addr + oa), sdesc_kmajor_sw128(b_addr + ob), idesc, q > 0 ? 1u : 0u);
+    }
+  } else {
+#pragma unroll
+    for (int kk = 0; kk < 4 * KATOMS; ++kk) {
+      const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+      mma_f16_ss(tmem_d, sdesc_kmajor_sw128(a_addr + off), sdesc_kmajor_sw128(b_addr + off), idesc, kk > 0 ? 1u : 0u);
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t elect_lane0() {
   return (threadIdx.x & 31) == 0;
 }

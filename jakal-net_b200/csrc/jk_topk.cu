@@ -82,6 +82,7 @@ struct Params {
   int compress;
   int state_dtype, val_dtype, out_dtype;
   int slab_ok;  // tm_val is valid (windowed gather of 16-bit values, dim % 64 == 0)
+  int split3;   // projections are the three-plane bf16 split of f32 values
   const void* col_state;
   const void* col_val;
   const void* col_sender;
@@ -690,12 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a_addr = smem_u32(a_tile);
         const uint32_t b_addr = smem_u32(b_ring + st * L::kBBytes);
-#pragma unroll
-        for (int kk = 0; kk < 4 * KATOMS; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kAtomBytes + (kk & 3) * 32;
-          mma_f16_ss(tmem + buf * kCols, sdesc_kmajor_sw128(a_addr + off), sdesc_kmajor_sw128(b_addr + off), idesc,
-                     kk > 0 ? 1u : 0u);
-        }
+        score_mmas<KATOMS>(tmem + buf * kCols, a_addr, b_addr, idesc, p.split3 != 0);
         mma_commit(&empty[st]);
         mma_commit(&tfull[buf]);
         if (g == decide_at) {
@@ -1056,7 +1052,8 @@ template <int MODE>
 int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols, int64_t rp,
            int proj_dtype, Params& p, cudaStream_t st) {
   CUtensorMap tr, tc, tv;
-  const bool bf16 = proj_dtype == JK_BF16;
+  const bool bf16 = proj_dtype != JK_F16;
+  p.split3 = proj_dtype == JK_BF16X3 ? 1 : 0;
   int status = make_tmap_3d_16bit(&tr, row_proj, rp, n_rows, batch, 64, kRows, bf16);
   if (status != JK_OK) return status;
   status = make_tmap_3d_16bit(&tc, col_proj, rp, n_cols, batch, 64, kCols, bf16);
@@ -1076,7 +1073,8 @@ int validate_common(const void* row_proj, const void* col_proj, int64_t batch, i
                     int64_t rp, int proj_dtype, const void* state, int state_dtype, const void* val, int64_t dim,
                     int val_dtype, int64_t k, int compress, int out_dtype) {
   if (row_proj == nullptr || col_proj == nullptr || state == nullptr || val == nullptr) return JK_ERR_BAD_ARG;
-  if (proj_dtype != JK_BF16 && proj_dtype != JK_F16) return JK_ERR_BAD_DTYPE;
+  if (proj_dtype != JK_BF16 && proj_dtype != JK_F16 && proj_dtype != JK_BF16X3) return JK_ERR_BAD_DTYPE;
+  if (proj_dtype == JK_BF16X3 && rp != 128) return JK_ERR_BAD_SHAPE;
   if (val_dtype < JK_F32 || val_dtype > JK_F16 || out_dtype < JK_F32 || out_dtype > JK_F16 || state_dtype < JK_F32 ||
       state_dtype > JK_F16)
     return JK_ERR_BAD_DTYPE;

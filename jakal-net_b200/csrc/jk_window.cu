@@ -54,6 +54,8 @@ struct Params {
   const void* col_state;
   void* out_state;
   void* out_val;
+  int split3;      // projections are the three-plane bf16 split of f32 values
+  int vsplit;      // values come as bf16 hi / lo planes (f32 values)
   int d0;          // first value column of this launch's slice
   int slice_cols;  // value columns of the slice (multiple of 64, <= kMaxSlice)
 };
@@ -104,7 +106,8 @@ __device__ __forceinline__ void split8(const float (&e)[8], bool f16, uint4& hi,
 template <int KATOMS>
 __global__ void __launch_bounds__(kThreads, 1)
     window_kernel(const __grid_constant__ CUtensorMap tm_rows, const __grid_constant__ CUtensorMap tm_cols,
-                  const __grid_constant__ CUtensorMap tm_val, Params p, uint32_t idesc_s, uint32_t idesc_pv) {
+                  const __grid_constant__ CUtensorMap tm_val, const __grid_constant__ CUtensorMap tm_val_lo, Params p,
+                  uint32_t idesc_s, uint32_t idesc_pv) {
   using L = Layout<KATOMS>;
   constexpr int PS = L::kPsStages;
   constexpr int VS = L::kVStages;
@@ -224,11 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a_addr = smem_u32(a_tile);
         const uint32_t b_addr = smem_u32(ps_ring + st * KATOMS * L::kAtom);
-        for (int kk = 0; kk < 4 * KATOMS; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kAtom + (kk & 3) * 32;
-          mma_f16_ss(tmem + buf * kCols, sdesc_kmajor_sw128(a_addr + off), sdesc_kmajor_sw128(b_addr + off), idesc_s,
-                     kk > 0 ? 1u : 0u);
-        }
+        score_mmas<KATOMS>(tmem + buf * kCols, a_addr, b_addr, idesc_s, p.split3 != 0);
         mma_commit(&empty[st]);
         mma_commit(&tfull[buf]);
         ++g;
@@ -236,11 +235,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto issue_v = [&](int it) {  // value tile `it` of the final pass into stage it % VS
         const int s = it % VS;
-        mbar_arrive_expect_tx(&vfull[s], nbox * L::kAtom);
         const int col0 = static_cast<int>((j_lo + it) * kCols);
-        for (int a = 0; a < nbox; ++a)
-          tma_load_3d(v_ring + s * L::kVStage + a * L::kAtom, &tm_val, &vfull[s], d0 + a * 64, col0,
-                      static_cast<int>(b));
+        if (p.vsplit) {  // one 64-column slice: hi plane box, then lo plane box
+          mbar_arrive_expect_tx(&vfull[s], 2 * L::kAtom);
+          tma_load_3d(v_ring + s * L::kVStage, &tm_val, &vfull[s], d0, col0, static_cast<int>(b));
+          tma_load_3d(v_ring + s * L::kVStage + L::kAtom, &tm_val_lo, &vfull[s], d0, col0, static_cast<int>(b));
+        } else {
+          mbar_arrive_expect_tx(&vfull[s], nbox * L::kAtom);
+          for (int a = 0; a < nbox; ++a)
+            tma_load_3d(v_ring + s * L::kVStage + a * L::kAtom, &tm_val, &vfull[s], d0 + a * 64, col0,
+                        static_cast<int>(b));
+        }
       };
       ok = mbar_wait(bar_a, 0);
       int dp = 0;
@@ -263,13 +268,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&vfull[vs], (it / VS) & 1) || !mbar_wait(eready, it & 1)) { ok = false; break; }
           tc_fence_after();
           const uint32_t v_addr = smem_u32(v_ring + vs * L::kVStage);
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const uint32_t e_addr = smem_u32(half == 0 ? e_hi : e_lo);
+          // E_hi.V + E_lo.V (+ E_hi.V_lo for split f32 values)
+          const int nprod = p.vsplit ? 3 : 2;
+          for (int q = 0; q < nprod; ++q) {
+            const uint32_t e_addr = smem_u32(q == 1 ? e_lo : e_hi);
+            const uint32_t vb = v_addr + (q == 2 ? L::kAtom : 0u);
             for (int kk = 0; kk < 8; ++kk) {
               const uint32_t aoff = (kk >> 2) * L::kAtom + (kk & 3) * 32;
-              mma_f16_ss(tmem_o, sdesc_kmajor_sw128(e_addr + aoff), sdesc_mnmajor_sw128(v_addr + kk * 2048, L::kAtom),
-                         idesc_pv, (it > 0 || half > 0 || kk > 0) ? 1u : 0u);
+              mma_f16_ss(tmem_o, sdesc_kmajor_sw128(e_addr + aoff), sdesc_mnmajor_sw128(vb + kk * 2048, L::kAtom),
+                         idesc_pv, (it > 0 || q > 0 || kk > 0) ? 1u : 0u);
             }
           }
           mma_commit(efree);
@@ -539,17 +546,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int KATOMS>
-int launch(const void* row_proj, const void* col_proj, const void* col_val, int64_t batch, int64_t n_rows,
-           int64_t n_cols, int64_t rp, bool bf16, Params& p, cudaStream_t st) {
-  CUtensorMap tr, tc, tv;
+int launch(const void* row_proj, const void* col_proj, const void* col_val, const void* col_val_lo, int64_t batch,
+           int64_t n_rows, int64_t n_cols, int64_t rp, bool bf16, Params& p, cudaStream_t st) {
+  CUtensorMap tr, tc, tv, tvl;
   int status = make_tmap_3d_16bit(&tr, row_proj, rp, n_rows, batch, 64, kRows, bf16);
   if (status != JK_OK) return status;
   status = make_tmap_3d_16bit(&tc, col_proj, rp, n_cols, batch, 64, kCols, bf16);
   if (status != JK_OK) return status;
   status = make_tmap_3d_16bit(&tv, col_val, p.dim, n_cols, batch, 64, kCols, bf16);
   if (status != JK_OK) return status;
+  tvl = tv;
+  if (p.vsplit) {
+    status = make_tmap_3d_16bit(&tvl, col_val_lo, p.dim, n_cols, batch, 64, kCols, bf16);
+    if (status != JK_OK) return status;
+  }
   const int nslice = static_cast<int>((p.dim + kMaxSlice - 1) / kMaxSlice);
-  const int per = static_cast<int>(((p.dim / 64 + nslice - 1) / nslice) * 64);
+  const int per = p.vsplit ? 64 : static_cast<int>(((p.dim / 64 + nslice - 1) / nslice) * 64);
   const uint32_t fmt = bf16 ? 1u : 0u;
   const uint32_t idesc_s = idesc_f16(kRows, kCols, fmt);
   constexpr int sm = Layout<KATOMS>::kTotal;
@@ -568,7 +580,7 @@ int launch(const void* row_proj, const void* col_proj, const void* col_val, int6
     q.d0 = d0;
     q.slice_cols = width;
     const uint32_t idesc_pv = idesc_f16(kRows, width, fmt) | (1u << 16);  // B (values) MN-major
-    kern<<<grid, kThreads, sm, st>>>(tr, tc, tv, q, idesc_s, idesc_pv);
+    kern<<<grid, kThreads, sm, st>>>(tr, tc, tv, tvl, q, idesc_s, idesc_pv);
     const int status2 = launch_status();
     if (status2 != JK_OK) return status2;
   }
@@ -581,14 +593,16 @@ int launch(const void* row_proj, const void* col_proj, const void* col_val, int6
 extern "C" int jk_propagation_window_forward(const void* row_proj, const void* col_proj, int64_t batch,
                                              int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
                                              const void* col_state, int state_dtype, const void* col_val,
-                                             int64_t dim, int64_t window, float score_bias, const float* bias_dev,
-                                             int compress, void* out_state, void* out_val, int out_dtype,
-                                             jk_stream_t stream) {
+                                             const void* col_val_lo, int64_t dim, int64_t window, float score_bias,
+                                             const float* bias_dev, int compress, void* out_state, void* out_val,
+                                             int out_dtype, jk_stream_t stream) {
   using namespace jk;
   if (row_proj == nullptr || col_proj == nullptr || col_state == nullptr || col_val == nullptr ||
       out_state == nullptr || out_val == nullptr)
     return JK_ERR_BAD_ARG;
-  if (proj_dtype != JK_BF16 && proj_dtype != JK_F16) return JK_ERR_BAD_DTYPE;
+  if (proj_dtype != JK_BF16 && proj_dtype != JK_F16 && proj_dtype != JK_BF16X3) return JK_ERR_BAD_DTYPE;
+  if (proj_dtype == JK_BF16X3 && rp != 128) return JK_ERR_BAD_SHAPE;
+  if (col_val_lo != nullptr && proj_dtype == JK_F16) return JK_ERR_BAD_DTYPE;
   if (state_dtype < JK_F32 || state_dtype > JK_F16 || out_dtype < JK_F32 || out_dtype > JK_F16) return JK_ERR_BAD_DTYPE;
   if (compress != JK_SOFTSIGN && compress != JK_SIGNED_ABS_SOFTMAX && compress != JK_SIGNED_ENTMAX15)
     return JK_ERR_UNSUPPORTED_KIND;
@@ -596,7 +610,8 @@ extern "C" int jk_propagation_window_forward(const void* row_proj, const void* c
   if (batch > 65535 || n_rows > (int64_t(1) << 30) || n_cols > (int64_t(1) << 30)) return JK_ERR_BAD_SHAPE;
   if (rp != 64 && rp != 128) return JK_ERR_BAD_SHAPE;
   if (window < -1) return JK_ERR_BAD_ARG;
-  if (!aligned16(row_proj) || !aligned16(col_proj) || !aligned16(col_val) || !aligned16(out_val))
+  if (!aligned16(row_proj) || !aligned16(col_proj) || !aligned16(col_val) || !aligned16(out_val) ||
+      (col_val_lo != nullptr && !aligned16(col_val_lo)))
     return JK_ERR_ALIGNMENT;
   int st = check_device();
   if (st != JK_OK) return st;
@@ -611,11 +626,13 @@ extern "C" int jk_propagation_window_forward(const void* row_proj, const void* c
   p.state_dtype = state_dtype;
   p.out_dtype = out_dtype;
   p.f16 = proj_dtype == JK_F16 ? 1 : 0;
+  p.split3 = proj_dtype == JK_BF16X3 ? 1 : 0;
+  p.vsplit = col_val_lo != nullptr ? 1 : 0;
   p.col_state = col_state;
   p.out_state = out_state;
   p.out_val = out_val;
   auto cs = reinterpret_cast<cudaStream_t>(stream);
-  const bool bf16 = proj_dtype == JK_BF16;
-  if (rp == 64) return win::launch<1>(row_proj, col_proj, col_val, batch, n_rows, n_cols, rp, bf16, p, cs);
-  return win::launch<2>(row_proj, col_proj, col_val, batch, n_rows, n_cols, rp, bf16, p, cs);
+  const bool bf16 = proj_dtype != JK_F16;
+  if (rp == 64) return win::launch<1>(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, bf16, p, cs);
+  return win::launch<2>(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, bf16, p, cs);
 }

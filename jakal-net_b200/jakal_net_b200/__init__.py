@@ -102,11 +102,13 @@ def _dtype_code(name: str, t: Tensor) -> int:
     return code
 
 
-def _proj_dtype(val: Tensor) -> int:
+def _proj_dtype(val: Tensor, split3: bool = False) -> int:
+    if split3:
+        return _lib.JK_BF16X3
     if val.dtype not in (torch.bfloat16, torch.float16):
         raise RuntimeError(
-            "b200_sm100a scores low-rank projections on tcgen05 tensor cores in the input "
-            f"dtype; bfloat16 or float16 inputs are required (got {val.dtype})."
+            "b200_sm100a scores low-rank projections on tcgen05 tensor cores; projections must be bf16 / f16, "
+            f"or the three-plane split of f32 projections (got {val.dtype})."
         )
     return _DTYPE_CODE[val.dtype]
 
@@ -122,13 +124,31 @@ def _flatten_state(t: Tensor) -> Tensor:
 def lowrank_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None,
                     temperature: float = 1.0) -> Tensor:
     """round(x @ weight^T) [* core] [/ temperature] in x's dtype, padded to a multiple of
-    64 columns (jakal_net_native.cpp:6236-6239, 6977-6986). x [..., D] -> [..., rp]."""
+    64 columns (jakal_net_native.cpp:6236-6239, 6977-6986). x [..., D] -> [..., rp].
+
+    f32 inputs (rank <= 32): the f32 projection (a plain f32 GEMM, like the reference's
+    torch::matmul) is returned as three bf16 planes [h | m | l | 0] (rp = 128) whose six
+    cross products the fused kernels sum -- an f32-accurate score (JK_BF16X3)."""
     _require_cuda("x", x)
-    code = _proj_dtype(x)
     rank, dim = weight.shape
     if x.shape[-1] != dim:
         raise ValueError(f"projection weight expects dim {dim}, got {x.shape[-1]}")
     x2 = x.reshape(-1, dim).contiguous()
+    if x.dtype == torch.float32:
+        if rank > 32:
+            raise RuntimeError(f"b200_sm100a f32 scoring supports score rank <= 32 (got {rank}).")
+        proj = torch.matmul(x2, weight.detach().to(device=x.device, dtype=torch.float32).t())
+        if core is not None:
+            proj = proj * core.detach().reshape(-1).to(device=x.device, dtype=torch.float32)
+        if float(temperature) != 1.0:
+            proj = proj / float(temperature)
+        proj = proj.contiguous()
+        out = torch.empty((x2.shape[0], 128), device=x.device, dtype=torch.bfloat16)
+        with torch.cuda.device(x.device):
+            check(_LIBRARY.jk_split3_bf16(proj.data_ptr(), x2.shape[0], rank, out.data_ptr(), _stream(x.device)),
+                  "jk_split3_bf16")
+        return out.reshape(*x.shape[:-1], 128)
+    code = _proj_dtype(x)
     w = weight.detach().to(device=x.device, dtype=x.dtype).contiguous()
     c = None if core is None else core.detach().reshape(-1).to(device=x.device, dtype=x.dtype).contiguous()
     rp = int(_LIBRARY.jk_padded_rank(rank))
@@ -157,7 +177,7 @@ def _bias_tensor(bias: Optional[Tensor], device: torch.device, scale: float = 1.
 def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, k: int, *,
                    window: int = -1, compress: int = _lib.JK_SOFTSIGN, col_sender: Optional[Tensor] = None,
                    bias: Optional[Tensor] = None, score_bias: float = 0.0,
-                   out_dtype: Optional[torch.dtype] = None, return_selection: bool = False):
+                   out_dtype: Optional[torch.dtype] = None, return_selection: bool = False, split3: bool = False):
     """Raw fused top-k aggregate over already-projected inputs (jk_propagation_topk_forward).
 
     row_proj [B, T, rp], col_proj [B, S, rp], col_state [B, S], col_val [B, S, D].
@@ -179,7 +199,7 @@ def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_va
     with torch.cuda.device(dev):
         check(
             _LIBRARY.jk_propagation_topk_forward(
-                row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj),
+                row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj, split3),
                 col_state.data_ptr(), _ptr(sender), _dtype_code("state", col_state),
                 col_val.data_ptr(), D, _dtype_code("val", col_val),
                 k, window, float(score_bias), _ptr(bias), compress,
@@ -229,7 +249,8 @@ def _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, o
     out_dtype = projected_val.dtype if same else torch.float32
     bias_t = _bias_tensor(bias, val.device)
     state, out = topk_aggregate(row_proj, col_proj, pstate, pval, k, window=window,
-                                compress=_EDGE_CODE[edge_compress_name], bias=bias_t, out_dtype=out_dtype)
+                                compress=_EDGE_CODE[edge_compress_name], bias=bias_t, out_dtype=out_dtype,
+                                split3=val.dtype == torch.float32)
     state = state.to(projected_state.dtype).reshape(*batch_shape, n)
     out = out.to(projected_val.dtype).reshape(*batch_shape, n, out_dim)
     return state, out
@@ -303,7 +324,7 @@ def transition_query_topk(route_kind, source_weight, source_bias, target_weight,
     same = projected_state.dtype == projected_val.dtype
     out_dtype = projected_val.dtype if same else torch.float32
     state, out = topk_aggregate(q_proj, src_proj, pstate, pval, k, window=-1, compress=_lib.JK_SOFTMAX,
-                                col_sender=sender, bias=bias_t, out_dtype=out_dtype)
+                                col_sender=sender, bias=bias_t, out_dtype=out_dtype, split3=sv.dtype == torch.float32)
     return (state.to(projected_state.dtype).reshape(*batch_shape, n_query),
             out.to(projected_val.dtype).reshape(*batch_shape, n_query, out_dim))
 
@@ -347,7 +368,8 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
     with torch.cuda.device(dev):
         check(
             _LIBRARY.jk_transition_pairwise_topk_forward(
-                src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1], _proj_dtype(src_proj),
+                src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1],
+                _proj_dtype(src_proj, sv.dtype == torch.float32),
                 pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
                 pval.data_ptr(), out_dim, _dtype_code("val", pval),
                 k, 0.0, _ptr(bias_t), _ROUTE_CODE[route_compress_name], accum.data_ptr(),
@@ -360,7 +382,8 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
 
 def masked_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, *, window: int = -1,
                      compress: int = _lib.JK_SOFTSIGN, bias: Optional[Tensor] = None, score_bias: float = 0.0,
-                     out_dtype: Optional[torch.dtype] = None):
+                     out_dtype: Optional[torch.dtype] = None, split3: bool = False,
+                     col_val_lo: Optional[Tensor] = None):
     """Raw fused window / dense aggregate over already-projected inputs
     (jk_propagation_window_forward). row_proj [B, T, rp], col_proj [B, S, rp], col_state [B, S],
     col_val [B, S, D] in the projections' dtype, D a multiple of 64. window -1 = dense."""
@@ -376,8 +399,8 @@ def masked_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_
     with torch.cuda.device(dev):
         check(
             _LIBRARY.jk_propagation_window_forward(
-                row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj),
-                col_state.data_ptr(), _dtype_code("state", col_state), col_val.data_ptr(), D,
+                row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj, split3),
+                col_state.data_ptr(), _dtype_code("state", col_state), col_val.data_ptr(), _ptr(col_val_lo), D,
                 int(window), float(score_bias), _ptr(bias), compress,
                 out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state), _stream(dev)),
             "jk_propagation_window_forward",
@@ -411,17 +434,32 @@ def _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, e
         ss = _flatten_state(source_state).float()
         pstate = (pstate.float() * ss).to(pstate.dtype)
         pval = (pval.float() * ss[..., None]).to(pval.dtype)
-    if pval.dtype != tv.dtype:
+    f32 = tv.dtype == torch.float32
+    pad = (-out_dim) % 64  # the value GEMM works on 64-column boxes
+    if pad:
+        pval = torch.nn.functional.pad(pval, (0, pad))
+    pval_lo = None
+    if f32:
+        # f32 values: bf16 hi + lo planes, both multiplied by the hi + lo edge planes
+        pval = pval.float().contiguous()
+        hi = torch.empty(pval.shape, device=pval.device, dtype=torch.bfloat16)
+        pval_lo = torch.empty_like(hi)
+        with torch.cuda.device(pval.device):
+            check(_LIBRARY.jk_split2_bf16(pval.data_ptr(), pval.numel(), hi.data_ptr(), pval_lo.data_ptr(),
+                                          _stream(pval.device)), "jk_split2_bf16")
+        pval = hi
+    elif pval.dtype != tv.dtype:
         pval = pval.to(tv.dtype)
-    if out_dim % 64 != 0:
-        raise RuntimeError(f"b200_sm100a window/dense propagation needs a value width that is a multiple of 64 (got {out_dim}).")
+    pval = pval.contiguous()
     row_proj = lowrank_project(tv, out_weight)
     col_proj = lowrank_project(sv, in_weight, core=weight)
     same = projected_state.dtype == projected_val.dtype
     out_dtype = projected_val.dtype if same else torch.float32
     st, out = masked_aggregate(row_proj, col_proj, pstate, pval, window=window,
                                compress=_EDGE_CODE[edge_compress_name], bias=_bias_tensor(bias, tv.device),
-                               out_dtype=out_dtype)
+                               out_dtype=out_dtype, split3=f32, col_val_lo=pval_lo)
+    if pad:
+        out = out[..., :out_dim]
     return (st.to(projected_state.dtype).reshape(*batch_shape, n_t),
             out.to(projected_val.dtype).reshape(*batch_shape, n_t, out_dim))
 

@@ -23,7 +23,7 @@ JK_ERR_DEVICE_TIMEOUT = -6
 JK_ERR_BAD_ARG = -7
 JK_ERR_ALIGNMENT = -8
 
-JK_F32, JK_BF16, JK_F16 = 0, 1, 2
+JK_F32, JK_BF16, JK_F16, JK_BF16X3 = 0, 1, 2, 3
 JK_SOFTSIGN, JK_SIGNED_ABS_SOFTMAX, JK_SIGNED_ENTMAX15, JK_SOFTMAX = 0, 1, 2, 3
 
 _p = ctypes.c_void_p
@@ -49,10 +49,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "jk_propagation_window_forward": (
         _i32,
         [_p, _p, _i64, _i64, _i64, _i64, _i32,  # row_proj, col_proj, B, n_rows, n_cols, rp, proj_dtype
-         _p, _i32, _p, _i64,                    # col_state, state_dtype, col_val, dim
+         _p, _i32, _p, _p, _i64,                # col_state, state_dtype, col_val, col_val_lo, dim
          _i64, _f32, _p, _i32,                  # window, score_bias, bias_dev, compress
          _p, _p, _i32, _p],                     # out_state, out_val, out_dtype, stream
     ),
+    "jk_split3_bf16": (_i32, [_p, _i64, _i64, _p, _p]),
+    "jk_split2_bf16": (_i32, [_p, _i64, _p, _p, _p]),
     "jk_transition_query_topk_forward": (
         _i32,
         [_p, _p, _i64, _i64, _i64, _i64, _i32,
