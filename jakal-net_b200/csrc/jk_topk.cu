@@ -163,7 +163,8 @@ __device__ void compress_row(const Lane& f, int n, int compress) {
       f.val(e) = x / (1.f + fabsf(x));
     }
   } else if (compress == JK_SOFTMAX) {
-    const float m = f.val(0);  // sorted: first is the max
+    float m = f.val(0);
+    for (int e = 1; e < n; ++e) m = fmaxf(m, f.val(e));
     float z = 0.f;
     for (int e = 0; e < n; ++e) z += expf(f.val(e) - m);
     const float inv = 1.f / z;
@@ -500,20 +501,22 @@ __device__ __forceinline__ int key_idx(unsigned long long key) {
   return static_cast<int>(~static_cast<uint32_t>(key & 0xFFFFFFFFull));
 }
 
-// Sorts the first n (<= NQ * 32) candidates of a row into descending key order with one
-// warp (element e = q * 32 + lane, NQ per lane) and writes the best min(k, valid) back to
-// slots 0 ..; returns that count.
+
+// Sorts the valid candidates of a row into descending (score, lower column) order with one
+// warp (bitonic network over NQ*32 64-bit keys) and writes the best min(k, valid) back to
+// slots 0 ..; returns that count. Needs c0 + c1 <= NQ * 32.
 template <int NQ>
-__device__ int warp_select_row(float* rv, int* ri, int n, int k, int lane) {
+__device__ int warp_select_row(float* rv, int* ri, int c0, int c1, int k, int lane) {
   constexpr int kN = NQ * 32;
   const unsigned long long kNone = make_key(-INFINITY, kSentinel);
   unsigned long long x[NQ];
 #pragma unroll
   for (int q = 0; q < NQ; ++q) {
-    const int e = q * 32 + lane;
-    x[q] = e < n ? make_key(rv[e], ri[e]) : kNone;
+    // logical candidate i = q*32 + lane: the half-0 stack, then the half-1 stack
+    const int i = q * 32 + lane;
+    const int e = i < c0 ? i : kCap - 1 - (i - c0);
+    x[q] = (i < c0 + c1 && ri[e] != kSentinel) ? make_key(rv[e], ri[e]) : kNone;
   }
-  // Bitonic sort, descending, over kN elements indexed e = q*32 + lane.
 #pragma unroll
   for (int size = 2; size <= kN; size <<= 1) {
 #pragma unroll
@@ -799,9 +802,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     sel_barrier();
     JK_PHASE_MARK(0, t_prev);
 
-    // ---- pass B: collect the columns at or above the threshold
+    // ---- pass B: collect the columns at or above the threshold. Half 0 stacks its
+    // candidates from slot 0 upwards, half 1 from slot kCap-1 downwards, each with a
+    // register counter (no atomics); a row whose stacks meet takes the exact fallback pass.
     {
       const float th = tau[row];
+      int myc = 0;
       for (int it = 0; it < ntiles && ok; ++it) {
         uint32_t v[2][32];
         if (!load_tile(v)) { ok = false; break; }
@@ -813,14 +819,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int col = col0 + c * 32 + e;
             const float x = __uint_as_float(v[c][e]);
             if (static_cast<uint32_t>(col - lo_t) <= span && x >= th) {
-              const int pos = atomicAdd(&cnt[row], 1);
-              if (pos < kCap) {
-                rv[pos] = x;
-                ri[pos] = col;
+              if (myc < kCap) {
+                const int slot = half == 0 ? myc : kCap - 1 - myc;
+                rv[slot] = x;
+                ri[slot] = col;
               }
+              ++myc;
             }
           }
       }
+      (half == 0 ? cnt : nsel)[row] = myc;
     }
     if (!ok) {
       atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
@@ -828,9 +836,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     sel_barrier();
     if (half == 0) {
-      const int c = cnt[row];
+      const int c0 = cnt[row], c1 = nsel[row];
       const int need = k < visible ? k : visible;
-      const bool fail = row_ok && (c > kCap || c < need);
+      const bool fail = row_ok && (c0 + c1 > kCap || c0 + c1 < need);
       failrow[row] = fail ? 1 : 0;
       if (fail) *any_fail = 1;
     }
@@ -884,22 +892,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
       }
       sel_barrier();
-      if (half == 0 && mine) cnt[row] = kCap;  // both heaps (sentinel padded) are the candidates
+      if (half == 0 && mine) {  // both heaps (sentinel padded) are the candidates
+        cnt[row] = 64;
+        nsel[row] = 64;
+      }
     }
     sel_barrier();
     JK_PHASE_MARK(2, t_prev);
     const bool good = !*abort_flag;
 
-    // ---- select: one warp per row sorts the candidates and keeps the best k
+    // ---- select: one warp per row keeps the best k of the row's two candidate stacks
     const int rt0 = warp * (kRows / kSelWarps);
     for (int r = 0; r < kRows / kSelWarps; ++r) {
       const int rt = rt0 + r;
       int n = 0;
       if (good && t0 + rt < p.n_rows) {
-        const int c = cnt[rt] < kCap ? cnt[rt] : kCap;
-        n = c <= 64 ? warp_select_row<2>(bufv + rt * kStride, bufi + rt * kStride, c, k, lane)
-                    : warp_select_row<4>(bufv + rt * kStride, bufi + rt * kStride, c, k, lane);
+        float* wv = bufv + rt * kStride;
+        int* wi = bufi + rt * kStride;
+        const int c0 = cnt[rt];
+        const int c1 = nsel[rt];
+        n = c0 + c1 <= 64 ? warp_select_row<2>(wv, wi, c0, c1, k, lane)
+                          : warp_select_row<4>(wv, wi, c0, c1, k, lane);
       }
+      __syncwarp();
       if (lane == 0) nsel[rt] = n;
     }
     sel_barrier();
@@ -986,7 +1001,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
               *abort_flag = 1;
             } else {
+              JK_PHASE_MARK(6, t_prev);
               gather_slab_chunk<VT>(slab_smem, bufv, nsel, rt0, nrows, t0, b, s_lo, c, p, lane);
+              JK_PHASE_MARK(7, t_prev);
             }
             sel_barrier();
             if (*abort_flag) break;
