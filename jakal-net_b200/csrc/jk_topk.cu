@@ -37,6 +37,7 @@
 
 #include <cfloat>
 #include <climits>
+#include <type_traits>
 
 namespace jk {
 namespace topk {
@@ -396,49 +397,6 @@ __device__ void gather_global(const float* bv, const int* nsel, int rt0, int nro
   }
 }
 
-// Aggregation of `nrows` rows from a staged slab: 64 value columns of the source rows
-// s_lo .. s_lo + nslab - 1, row-major (128 B per source row). The warp works on 4 rows at a
-// time: lanes 8q .. 8q+7 own row q, 8 columns each, so a slab read of the warp is four
-// 128-byte rows (the minimum four wavefronts) and each lane does 8 FMAs per read.
-template <typename VT>
-__device__ void gather_slab_chunk(const uint8_t* slab, const float* bv, const int* nsel, int rt0, int nrows,
-                                  int64_t t0, int64_t b, int s_lo, int chunk, const Params& p, int lane) {
-  constexpr int kNb = 4;  // neighbours per step
-  const int64_t D = p.dim;
-  const int q = lane >> 3;     // row of the group this lane works on
-  const int piece = lane & 7;  // 16-byte piece (8 columns) of the 64-column chunk
-  for (int r0 = 0; r0 < nrows; r0 += 4) {
-    const int rt = rt0 + r0 + q;
-    const bool ok = r0 + q < nrows && t0 + rt < p.n_rows;
-    const int n = ok ? nsel[rt] : 0;
-    const int nmax = __reduce_max_sync(0xffffffffu, n);
-    const float* tab = bv + gtab_off(ok ? rt : rt0);
-    float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-    for (int e0 = 0; e0 < nmax; e0 += kNb) {
-      uint4 u[kNb];
-      float w[kNb];
-#pragma unroll
-      for (int m = 0; m < kNb; ++m) {
-        const bool on = e0 + m < n;
-        const float2 wj = *reinterpret_cast<const float2*>(tab + 2 * (on ? e0 + m : 0));
-        w[m] = on ? wj.x : 0.f;
-        const int j = on ? __float_as_int(wj.y) - s_lo : 0;
-        u[m] = *reinterpret_cast<const uint4*>(slab + j * 128 + piece * 16);
-      }
-#pragma unroll
-      for (int m = 0; m < kNb; ++m) {
-        float x[8];
-        widen8<VT>(u[m], x);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = fmaf(w[m], x[e], acc[e]);
-      }
-    }
-    if (ok) store8(p.out_val, (b * p.n_rows + t0 + rt) * D + chunk * 64 + piece * 8, p.out_dtype, acc);
-  }
-}
-
 // Scatter of one source row by one warp into the f32 destination accumulators.
 template <typename VT>
 __device__ void scatter_row(const Lane& f, int n, int64_t b, int64_t src, const Params& p, int lane) {
@@ -603,7 +561,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar_a = bars;
   uint64_t* decide = bars + 1;
   uint64_t* slab_bar = bars + 2;
-  uint64_t* full = bars + 3;
+  uint64_t* agg_bar = bars + 3;
+  uint64_t* vb_full = bars + 4;   // [2] value tiles of the tensor-core aggregate
+  uint64_t* vb_empty = bars + 6;  // [2]
+  uint64_t* full = bars + 8;
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -636,6 +597,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_a, 1);
     mbar_init(decide, 1);
     mbar_init(slab_bar, 1);
+    mbar_init(agg_bar, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&vb_full[i], 1);
+      mbar_init(&vb_empty[i], 1);
+    }
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
@@ -648,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *any_fail = 0;
     fence_barrier_init();
   }
-  if (warp == 0) tmem_alloc(tmem_slot, 256);
+  if (warp == 0) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -984,29 +950,125 @@ __global__ void __launch_bounds__(kThreads, 1)
           int64_t hi_col = t0 + kRows - 1;
           if (hi_col > p.n_cols - 1) hi_col = p.n_cols - 1;
           nslab = static_cast<int>(hi_col - s_lo + 1);
-          slab = nslab > 0 && ((nslab + 127) / 128) * 128 * 128 <= L::kRegion0;
+          slab = nslab > 0 && nslab <= 1024 && p.dim <= 512;  // dense enough; O fits TMEM
         }
         if (slab) {
-          const int nbox = (nslab + 127) / 128;
-          const int nchunk = static_cast<int>(p.dim / 64);
-          const uint8_t* slab_smem = smem;
-          for (int c = 0; c < nchunk && good; ++c) {
-            if (threadIdx.x == 0) {
-              fence_proxy_async_smem();  // prior generic reads of the slab region
-              mbar_arrive_expect_tx(slab_bar, nbox * 128 * 128);
-              for (int bx = 0; bx < nbox; ++bx)
-                tma_load_3d(smem + bx * 128 * 128, &tm_val, slab_bar, c * 64, s_lo + bx * 128, static_cast<int>(b));
+          // Tensor-core aggregate over the CTA's source window: for every 128-row source
+          // tile, the selected edges of the 128 target rows form a sparse 128 x 128 matrix
+          // E, written (bf16 / f16 hi + lo planes) into the MMA operand region; thread 0
+          // multiplies it with the tile's values 128 columns at a time (TMA, MN-major 128B
+          // swizzle, double-buffered) into a TMEM accumulator O[128 x dim]:
+          // O += E_hi.V + E_lo.V. The hi + lo planes keep the edge weights to ~16 bits.
+          constexpr bool kHalfV = std::is_same<VT, __half>::value;
+          const int ntile = (nslab + 127) / 128;
+          const int nsl = static_cast<int>((p.dim + 127) / 128);  // 128-column value slices
+          const int npair = ntile * nsl;
+          uint8_t* e_hi = smem;              // 2 K atoms (32 KB)
+          uint8_t* e_lo = smem + 2 * 16384;  // 2 K atoms (32 KB)
+          uint8_t* vbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bufi) + 1023) & ~uintptr_t(1023));
+          const int erow = row;  // this thread's target row
+          auto slice_w = [&](int sl) { return static_cast<int>(p.dim - sl * 128 < 128 ? p.dim - sl * 128 : 128); };
+          auto load_v = [&](int pi) {  // (tile, slice) pair pi -> buffer pi & 1
+            const int st = pi / nsl, sl = pi % nsl, nb = slice_w(sl) / 64;
+            mbar_arrive_expect_tx(&vb_full[pi & 1], nb * 16384);
+            for (int a = 0; a < nb; ++a)
+              tma_load_3d(vbuf + (pi & 1) * 32768 + a * 16384, &tm_val, &vb_full[pi & 1], sl * 128 + a * 64,
+                          s_lo + st * 128, static_cast<int>(b));
+          };
+          if (threadIdx.x == 0) {
+            fence_proxy_async_smem();  // the value buffers held generic candidate data before
+            load_v(0);
+            if (npair > 1) load_v(1);
+          }
+          for (int st = 0; st < ntile; ++st) {
+            const int src0 = s_lo + st * 128;
+            uint4* ez = reinterpret_cast<uint4*>(e_hi);
+            for (int i = threadIdx.x; i < 4096; i += kSelWarps * 32) ez[i] = make_uint4(0, 0, 0, 0);
+            sel_barrier();
+            if (t0 + erow < p.n_rows) {
+              const float* tab = bufv + gtab_off(erow);
+              const int n = nsel[erow];
+              for (int e = half; e < n; e += 2) {
+                const int kcol = __float_as_int(tab[2 * e + 1]) - src0;
+                if (static_cast<uint32_t>(kcol) < 128u) {
+                  const float w = tab[2 * e];
+                  const int kin = kcol & 63;
+                  const int off = (kcol >> 6) * 16384 + (erow >> 3) * 1024 + (erow & 7) * 128 +
+                                  (((kin >> 3) ^ (erow & 7)) << 4) + (kin & 7) * 2;
+                  if (kHalfV) {
+                    const __half h = __float2half_rn(w);
+                    *reinterpret_cast<__half*>(e_hi + off) = h;
+                    *reinterpret_cast<__half*>(e_lo + off) = __float2half_rn(w - __half2float(h));
+                  } else {
+                    const __nv_bfloat16 h = __float2bfloat16_rn(w);
+                    *reinterpret_cast<__nv_bfloat16*>(e_hi + off) = h;
+                    *reinterpret_cast<__nv_bfloat16*>(e_lo + off) = __float2bfloat16_rn(w - __bfloat162float(h));
+                  }
+                }
+              }
             }
-            if (!mbar_wait(slab_bar, c & 1)) {
-              atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
-              *abort_flag = 1;
-            } else {
-              JK_PHASE_MARK(6, t_prev);
-              gather_slab_chunk<VT>(slab_smem, bufv, nsel, rt0, nrows, t0, b, s_lo, c, p, lane);
-              JK_PHASE_MARK(7, t_prev);
+            fence_proxy_async_smem();
+            sel_barrier();
+            if (threadIdx.x == 0) {
+              bool okm = true;
+              for (int sl = 0; sl < nsl && okm; ++sl) {
+                const int pi = st * nsl + sl;
+                if (!mbar_wait(&vb_full[pi & 1], (pi >> 1) & 1)) { okm = false; break; }
+                tc_fence_after();
+                const int w = slice_w(sl);
+                const uint32_t idesc_pv = idesc_f16(128, w, kHalfV ? 0u : 1u) | (1u << 16);
+                const uint32_t vaddr = smem_u32(vbuf + (pi & 1) * 32768);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                  const uint32_t eaddr = smem_u32(q == 0 ? e_hi : e_lo);
+#pragma unroll
+                  for (int kk = 0; kk < 8; ++kk) {
+                    mma_f16_ss(tmem + sl * 128, sdesc_kmajor_sw128(eaddr + (kk >> 2) * 16384 + (kk & 3) * 32),
+                               sdesc_mnmajor_sw128(vaddr + kk * 2048, 16384), idesc_pv,
+                               (st > 0 || q > 0 || kk > 0) ? 1u : 0u);
+                  }
+                }
+                mma_commit(&vb_empty[pi & 1]);
+                if (pi + 2 < npair) {  // refill this buffer once its MMAs retired
+                  if (!mbar_wait(&vb_empty[pi & 1], (pi >> 1) & 1)) { okm = false; break; }
+                  load_v(pi + 2);
+                }
+              }
+              if (okm) {
+                mma_commit(agg_bar);
+              } else {
+                atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
+                *abort_flag = 1;
+              }
             }
             sel_barrier();
             if (*abort_flag) break;
+            if (!mbar_wait(agg_bar, st & 1)) {  // E may be rewritten once its MMAs retired
+              atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
+              *abort_flag = 1;
+              break;
+            }
+            tc_fence_after();
+          }
+          sel_barrier();
+          if (!*abort_flag) {
+            // O -> outputs (thread = row; half = which half of the columns)
+            const int hcols = static_cast<int>(p.dim / 2);  // multiple of 32
+            for (int c0 = 0; c0 < hcols; c0 += 32) {
+              uint32_t v[32];
+              tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * hcols + c0, v);
+              tmem_ld_wait();
+              if (t0 + erow < p.n_rows) {
+                const int64_t base = (b * p.n_rows + t0 + erow) * p.dim + half * hcols + c0;
+#pragma unroll
+                for (int e = 0; e < 32; e += 8) {
+                  float f[8];
+#pragma unroll
+                  for (int u = 0; u < 8; ++u) f[u] = __uint_as_float(v[e + u]);
+                  store8(p.out_val, base + e, p.out_dtype, f);
+                }
+              }
+            }
           }
         } else {
           gather_global<VT>(bufv, nsel, rt0, nrows, t0, b, p, lane);
@@ -1026,7 +1088,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -1078,7 +1140,7 @@ int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_
   tv = tc;  // placeholder when the slab path is off
   p.slab_ok = 0;
   if (MODE == kGather && p.window >= 0 && p.val_dtype != JK_F32 && p.dim % 64 == 0 && aligned16(p.col_val)) {
-    if (make_tmap_3d_16bit(&tv, p.col_val, p.dim, n_cols, batch, 64, 128, p.val_dtype == JK_BF16, false) == JK_OK)
+    if (make_tmap_3d_16bit(&tv, p.col_val, p.dim, n_cols, batch, 64, 128, p.val_dtype == JK_BF16, true) == JK_OK)
       p.slab_ok = 1;
   }
   const uint32_t idesc = idesc_f16(kRows, kCols, bf16 ? 1u : 0u);
