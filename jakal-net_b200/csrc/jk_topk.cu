@@ -26,8 +26,9 @@
 //     pass C (only if some row of the CTA got fewer than min(k, visible) or more than kCap
 //          candidates -- a row far from normal): those rows redo an exact streaming
 //          selection, each thread keeping a k-entry min-heap in the row's buffer.
-//     select: one warp per row sorts the row's buffer (bitonic, 128 keys ordered by score
-//          then lower column) and keeps the best k.
+//     select: one warp per row ranks the row's candidates (64-bit keys ordered by score
+//          then lower column; each lane counts the keys that beat its own) and keeps the
+//          best k in descending order.
 //   Then the k survivors are compressed into edges, and all 8 warps aggregate: a windowed
 //   CTA stages its whole source range in shared memory 64 value columns at a time (TMA)
 //   and gathers from there; otherwise 16-byte vector gathers from global memory; the
@@ -44,14 +45,23 @@ namespace topk {
 
 #ifdef JK_PHASE_PROFILE
 // Debug-only phase timer (sum over selection warps of clock64 deltas per phase).
-__device__ unsigned long long g_phase[8];
+__device__ unsigned long long g_phase[16];
 #define JK_PHASE_MARK(i, t_prev)                                                                \
   do {                                                                                         \
     const long long _now = clock64();                                                          \
     if ((threadIdx.x & 31) == 0) atomicAdd(&g_phase[i], (unsigned long long)(_now - (t_prev))); \
     t_prev = _now;                                                                             \
   } while (0)
+// Adds the cycles spent in `expr` (one thread) to slot i.
+#define JK_PHASE_TIME(i, expr)                                   \
+  ([&]() {                                                       \
+    const long long _t0 = clock64();                             \
+    auto _r = (expr);                                            \
+    if ((threadIdx.x & 31) == 0) atomicAdd(&g_phase[i], (unsigned long long)(clock64() - _t0)); \
+    return _r;                                                   \
+  }())
 #else
+#define JK_PHASE_TIME(i, expr) (expr)
 #define JK_PHASE_MARK(i, t_prev) \
   do {                           \
   } while (0)
@@ -64,11 +74,23 @@ constexpr int kCap = 128;       // candidate slots per row
 constexpr int kQueue = 4;       // fallback queue slots per thread
 constexpr int kStride = 137;    // row stride of the candidate buffer (odd: conflict-free)
 constexpr int kSelWarps = 8;    // selection / aggregation warps
-constexpr int kThreads = (kSelWarps + 1) * 32;
+constexpr int kMmaWarp = kSelWarps;       // tcgen05.mma issuer
+constexpr int kLoadWarp = kSelWarps + 1;  // TMA loader
+constexpr int kThreads = (kSelWarps + 2) * 32;
 constexpr int kSentinel = INT_MAX;
 static_assert(kStride >= kCap + 2 * kQueue, "buffer row holds candidates and both fallback queues");
+static_assert(kCap / 2 >= 64, "the score-rank permutation sits behind k <= 64 selected slots");
 
 enum Mode { kGather = 0, kScatter = 1 };
+
+// Tensor-core aggregate: 64 source rows per edge tile, value slices of 128 columns.
+constexpr int kEK = 64;       // source rows per edge tile (MMA K)
+constexpr int kVSlice = 128;  // value columns per slice (MMA N)
+constexpr int kVBufs = 4;     // value-slice buffers (16 KB each)
+constexpr int kElStride = 65;  // 8-byte entries per row of the per-half edge lists (64 + pad)
+constexpr int kOCols = 384;   // TMEM columns of the aggregate's accumulator O (dim <= 384)
+// Edge tiles live in TMEM behind O: buffer e, plane q (hi / lo) at column
+// kOCols + e * 64 + q * 32; a row's 64 K elements are 32 columns of bf16 / f16 pairs.
 
 // Start (in floats, 16-byte aligned) of a row's packed gather table: (weight, column) pairs
 // written over the row's candidate values once the edges are final.
@@ -155,7 +177,7 @@ __device__ __forceinline__ float flush_queue(const Lane& h, const Lane& q, int k
 
 __device__ __forceinline__ float sgn(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
 
-// Replaces f.val(0..n) (sorted scores, bias included) by compressed edges.
+// Replaces f.val(0..n) (the selected scores, bias included, any order) by compressed edges.
 __device__ void compress_row(const Lane& f, int n, int compress) {
   if (n <= 0) return;
   if (compress == JK_SOFTSIGN) {
@@ -460,70 +482,124 @@ __device__ __forceinline__ int key_idx(unsigned long long key) {
 }
 
 
-// Sorts the valid candidates of a row into descending (score, lower column) order with one
-// warp (bitonic network over NQ*32 64-bit keys) and writes the best min(k, valid) back to
-// slots 0 ..; returns that count. Needs c0 + c1 <= NQ * 32.
+// Rank selection: the row's n candidates (logical order: half-0 stack, then half-1 stack)
+// become 64-bit keys in the warp's scratch ks; every lane counts, for its NQ keys, how many
+// keys of the row beat them (broadcast reads, independent compares: no shuffle chains).
+// Keys are unique (distinct columns), so the best min(k, real) keys have ranks 0 .. k-1.
+// The survivors are written back in column order, as two ascending runs: when the stacks
+// hold columns in ascending order (`runs`: the threshold pass appends them that way),
+// by a ballot prefix over the logical order, run 0 = survivors of stack 0 and run 1 =
+// those of stack 1; otherwise (heap fallback rows) by counting, for every survivor, the
+// survivors of lower column -- one run. m0 receives the length of run 0. ri[kCap / 2 + c]
+// keeps the score rank of slot c for the ordered score outputs.
+// Returns min(k, real candidates). Needs c0 + c1 <= NQ * 32 and k <= kCap / 2.
 template <int NQ>
-__device__ int warp_select_row(float* rv, int* ri, int c0, int c1, int k, int lane) {
-  constexpr int kN = NQ * 32;
+__device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int lane, unsigned long long* ks,
+                                bool runs, int& m0) {
+  const int n = c0 + c1;
   const unsigned long long kNone = make_key(-INFINITY, kSentinel);
   unsigned long long x[NQ];
+  int rank[NQ];
 #pragma unroll
   for (int q = 0; q < NQ; ++q) {
-    // logical candidate i = q*32 + lane: the half-0 stack, then the half-1 stack
     const int i = q * 32 + lane;
     const int e = i < c0 ? i : kCap - 1 - (i - c0);
-    x[q] = (i < c0 + c1 && ri[e] != kSentinel) ? make_key(rv[e], ri[e]) : kNone;
+    x[q] = (i < n && ri[e] != kSentinel) ? make_key(rv[e], ri[e]) : kNone;
+    if (i < n) ks[i] = x[q];
+    rank[q] = 0;
   }
+  __syncwarp();  // from here on rv / ri of the row are free: every lane holds its keys
+  int j = 0;
+  for (; j + 4 <= n; j += 4) {
+    const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(ks + j);
+    const ulonglong2 c = *reinterpret_cast<const ulonglong2*>(ks + j + 2);
 #pragma unroll
-  for (int size = 2; size <= kN; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-      for (int q = 0; q < NQ; ++q) {
-        const int e = q * 32 + lane;
-        const bool desc = (e & size) == 0;  // direction of this block
-        if (stride >= 32) {
-          const int qs = stride >> 5;
-          if ((q & qs) == 0) {
-            const int q2 = q | qs;
-            const unsigned long long a = x[q], c = x[q2];
-            const bool swap = desc ? (a < c) : (a > c);
-            x[q] = swap ? c : a;
-            x[q2] = swap ? a : c;
-          }
-        } else {
-          const unsigned long long other = __shfl_xor_sync(0xffffffffu, x[q], stride);
-          const bool lower = (lane & stride) == 0;
-          const bool take_max = (lower == desc);  // the lower element keeps the larger key
-          const unsigned long long mx = x[q] > other ? x[q] : other;
-          const unsigned long long mn = x[q] > other ? other : x[q];
-          x[q] = take_max ? mx : mn;
-        }
-      }
-    }
+    for (int q = 0; q < NQ; ++q)
+      rank[q] += (a.x > x[q]) + (a.y > x[q]) + (c.x > x[q]) + (c.y > x[q]);
   }
-  int valid = 0;
+  for (; j < n; ++j) {
+    const unsigned long long a = ks[j];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) rank[q] += a > x[q];
+  }
+  int real = 0;
+  bool keep[NQ];
+  int col[NQ], slot[NQ];
 #pragma unroll
   for (int q = 0; q < NQ; ++q) {
-    const int e = q * 32 + lane;
-    valid += __popc(__ballot_sync(0xffffffffu, x[q] != kNone && e < k));
+    real += __popc(__ballot_sync(0xffffffffu, x[q] != kNone));
+    keep[q] = x[q] != kNone && rank[q] < k;
+    col[q] = key_idx(x[q]);
   }
-  __syncwarp();
+  if (runs) {
+    const uint32_t lt = (1u << lane) - 1u;
+    int before = 0, in0 = 0;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, keep[q]);
+      slot[q] = before + __popc(bal & lt);
+      before += __popc(bal);
+      in0 += __popc(__ballot_sync(0xffffffffu, keep[q] && q * 32 + lane < c0));
+    }
+    m0 = in0;
+  } else {
+    __syncwarp();  // every lane has read the keys: the scratch now holds the kept columns
+    int* kc = reinterpret_cast<int*>(ks);
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int i = q * 32 + lane;
+      if (i < n) kc[i] = keep[q] ? col[q] : INT_MAX;
+      slot[q] = 0;
+    }
+    __syncwarp();
+    for (j = 0; j + 4 <= n; j += 4) {
+      const int4 a = *reinterpret_cast<const int4*>(kc + j);
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) slot[q] += (a.x < col[q]) + (a.y < col[q]) + (a.z < col[q]) + (a.w < col[q]);
+    }
+    for (; j < n; ++j) {
+      const int a = kc[j];
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) slot[q] += a < col[q];
+    }
+    m0 = real < k ? real : k;
+  }
 #pragma unroll
   for (int q = 0; q < NQ; ++q) {
-    const int e = q * 32 + lane;
-    if (e < valid) {
-      rv[e] = key_val(x[q]);
-      ri[e] = key_idx(x[q]);
+    if (keep[q]) {
+      rv[slot[q]] = key_val(x[q]);
+      ri[slot[q]] = col[q];
+      ri[kCap / 2 + slot[q]] = rank[q];
     }
   }
   __syncwarp();
-  return valid;
+  return real < k ? real : k;
 }
 
 __device__ __forceinline__ void sel_barrier() {
   asm volatile("bar.sync 1, %0;" ::"r"(kSelWarps * 32) : "memory");
+}
+
+// Source window of a CTA's tensor-core aggregate: rows [s_lo, s_lo + n) of the values.
+// Taken when the CTA's sources form a window of at most 1024 rows of 16-bit values whose
+// width fits the TMEM accumulator beside the edge tiles (identical in every thread).
+struct SlabRange {
+  int s_lo, n;
+  bool on;
+};
+
+template <typename VT>
+__device__ __forceinline__ SlabRange slab_range(const Params& p, int64_t t0) {
+  SlabRange r{0, 0, false};
+  if (p.slab_ok && p.window >= 0 && sizeof(VT) == 2 && (p.dim % 64) == 0) {
+    const int64_t lo = t0 - p.window;
+    r.s_lo = lo > 0 ? static_cast<int>(lo) : 0;
+    int64_t hi_col = t0 + kRows - 1;
+    if (hi_col > p.n_cols - 1) hi_col = p.n_cols - 1;
+    r.n = static_cast<int>(hi_col - r.s_lo + 1);
+    r.on = r.n > 0 && r.n <= 1024 && p.dim <= kOCols;
+  }
+  return r;
 }
 
 // ---------------------------------------------------------------- shared-memory layout
@@ -532,10 +608,12 @@ struct Layout {
   static constexpr int kAtomBytes = kRows * 128;  // 128 rows x 64 (16-bit) elements
   static constexpr int kABytes = KATOMS * kAtomBytes;
   static constexpr int kBBytes = KATOMS * kAtomBytes;
-  static constexpr int kRegion0 = kABytes + STAGES * kBBytes;  // A + ring; reused as the value slab
+  // A + ring; reused by the selection scratch and the aggregate's per-half edge lists
+  static constexpr int kRegion0 = kABytes + STAGES * kBBytes > kRows * kElStride * 8 ? kABytes + STAGES * kBBytes
+                                                                                     : kRows * kElStride * 8;
   static constexpr int kBufBytes = 2 * kRows * kStride * 4;    // candidate values + indices
   static constexpr int kRowArrays = 10 * kRows * 4;            // per-row scalars
-  static constexpr int kBarBytes = 256;
+  static constexpr int kBarBytes = 320;
   static constexpr int kTotal = 1024 + kRegion0 + kBufBytes + kRowArrays + kBarBytes;
 };
 
@@ -562,15 +640,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* decide = bars + 1;
   uint64_t* slab_bar = bars + 2;
   uint64_t* agg_bar = bars + 3;
-  uint64_t* vb_full = bars + 4;   // [2] value tiles of the tensor-core aggregate
-  uint64_t* vb_empty = bars + 6;  // [2]
-  uint64_t* full = bars + 8;
+  uint64_t* vb_full = bars + 4;    // [kVBufs] value slices of the tensor-core aggregate
+  uint64_t* vb_empty = bars + 8;   // [kVBufs]
+  uint64_t* e_full = bars + 12;    // [2] edge tiles written (one arrival per selection warp)
+  uint64_t* e_empty = bars + 14;   // [2] edge tiles retired by their MMAs
+  uint64_t* full = bars + 16;
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* any_fail = abort_flag + 1;
+  volatile int* agg_mode = any_fail + 1;  // 1: tensor-core aggregate (set before slab_bar)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -598,9 +679,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(decide, 1);
     mbar_init(slab_bar, 1);
     mbar_init(agg_bar, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kVBufs; ++i) {
       mbar_init(&vb_full[i], 1);
       mbar_init(&vb_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&e_full[i], kSelWarps);
+      mbar_init(&e_empty[i], 1);
     }
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 1);
@@ -620,11 +705,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kSelWarps) {
-    // ------------------------------------------------------------ producer / MMA issuer
+  if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ TMA loader
+    // Row tile once, then the column tiles of every pass through the STAGES ring, then
+    // (tensor-core aggregate) the value slices of the source window through kVBufs buffers.
     if (lane == 0 && ntiles > 0) {
       prefetch_tmap(&tm_rows);
       prefetch_tmap(&tm_cols);
+      if (p.slab_ok) prefetch_tmap(&tm_val);
       bool ok = true;
       mbar_arrive_expect_tx(bar_a, L::kABytes);
 #pragma unroll
@@ -632,25 +720,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(a_tile + a * L::kAtomBytes, &tm_rows, bar_a, a * 64, static_cast<int>(t0), static_cast<int>(b));
       int total = pre_passes * ntiles;  // grows by one pass if the fallback pass is needed
       const int decide_at = total - 1;
-      int issued = 0;  // column-tile loads issued, in global iteration order
-      auto issue_loads = [&](int upto) -> bool {
-        while (issued <= upto && issued < total) {
-          const int s = issued % STAGES;
-          if (issued >= STAGES) {
-            const int prev = issued - STAGES;  // the MMA that last read stage s
-            if (!mbar_wait(&empty[s], (prev / STAGES) & 1)) return false;
-          }
-          mbar_arrive_expect_tx(&full[s], L::kBBytes);
-          const int col0 = static_cast<int>((j_lo + issued % ntiles) * kCols);
+      for (int i = 0; i < total && ok; ++i) {
+        const int s = i % STAGES;
+        if (i >= STAGES && !mbar_wait(&empty[s], ((i - STAGES) / STAGES) & 1)) { ok = false; break; }
+        if (*abort_flag) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], L::kBBytes);
+        const int col0 = static_cast<int>((j_lo + i % ntiles) * kCols);
 #pragma unroll
-          for (int a = 0; a < KATOMS; ++a)
-            tma_load_3d(b_ring + s * L::kBBytes + a * L::kAtomBytes, &tm_cols, &full[s], a * 64, col0,
-                        static_cast<int>(b));
-          ++issued;
+        for (int a = 0; a < KATOMS; ++a)
+          tma_load_3d(b_ring + s * L::kBBytes + a * L::kAtomBytes, &tm_cols, &full[s], a * 64, col0,
+                      static_cast<int>(b));
+        if (i == decide_at) {
+          // The selection warps report whether any row needs the exact fallback pass.
+          if (!mbar_wait(decide, 0)) { ok = false; break; }
+          if (*any_fail) total += ntiles;
         }
-        return true;
-      };
-      ok = issue_loads(STAGES - 1) && mbar_wait(bar_a, 0);
+      }
+      if (ok) ok = mbar_wait(slab_bar, 0);
+      if (ok && *agg_mode) {
+        const SlabRange sr = slab_range<VT>(p, t0);
+        const int nkt = (sr.n + kEK - 1) / kEK;
+        const int nsl = static_cast<int>((p.dim + kVSlice - 1) / kVSlice);
+        uint8_t* vbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bufi) + 1023) & ~uintptr_t(1023));
+        for (int pi = 0; pi < nkt * nsl && ok; ++pi) {
+          const int vb = pi % kVBufs;
+          if (pi >= kVBufs && !JK_PHASE_TIME(10, mbar_wait(&vb_empty[vb], ((pi - kVBufs) / kVBufs) & 1))) {
+            ok = false;
+            break;
+          }
+          if (*abort_flag) { ok = false; break; }
+          const int kt = pi / nsl, sl = pi % nsl;
+          const int w = static_cast<int>(p.dim) - sl * kVSlice;
+          const int nb = (w < kVSlice ? w : kVSlice) / 64;
+          mbar_arrive_expect_tx(&vb_full[vb], nb * 8192);
+          for (int a = 0; a < nb; ++a)
+            tma_load_3d(vbuf + vb * 16384 + a * 8192, &tm_val, &vb_full[vb], sl * kVSlice + a * 64,
+                        sr.s_lo + kt * kEK, static_cast<int>(b));
+        }
+      }
+      if (!ok) {
+        atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
+        *abort_flag = 1;
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && ntiles > 0) {
+      bool ok = mbar_wait(bar_a, 0);
+      int total = pre_passes * ntiles;
+      const int decide_at = total - 1;
       for (int g = 0; g < total && ok; ++g) {
         const int st = g % STAGES;
         const int buf = g & 1;
@@ -664,18 +782,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&empty[st]);
         mma_commit(&tfull[buf]);
         if (g == decide_at) {
-          // The selection warps report whether any row needs the exact fallback pass.
           if (!mbar_wait(decide, 0)) { ok = false; break; }
           if (*any_fail) total += ntiles;
         }
-        // Stage reuse: with >= 2 stages load ahead behind the previous MMA, with one stage
-        // behind this MMA.
-        if (!issue_loads(STAGES == 1 ? g + 1 : g - 1 + STAGES)) { ok = false; break; }
       }
       // The MMA-retire arrivals on the ring barriers must land before the CTA exits.
       if (ok) {
         const int last = total - 1;
         ok = mbar_wait(&empty[last % STAGES], (last / STAGES) & 1);
+      }
+      // Aggregate MMAs: once the selection warps decided (slab_bar), every double-buffered
+      // edge tile (TMEM) is multiplied with the value slices the loader streams in.
+      if (ok) ok = mbar_wait(slab_bar, 0);
+      if (ok && *agg_mode) {
+        constexpr bool kHalfV = std::is_same<VT, __half>::value;
+        const SlabRange sr = slab_range<VT>(p, t0);
+        const int nkt = (sr.n + kEK - 1) / kEK;
+        const int nsl = static_cast<int>((p.dim + kVSlice - 1) / kVSlice);
+        uint8_t* vbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bufi) + 1023) & ~uintptr_t(1023));
+#ifdef JK_PHASE_PROFILE
+        const long long t_iss = clock64();
+#endif
+        for (int kt = 0; kt < nkt && ok; ++kt) {
+          const int buf = kt & 1;
+          if (!JK_PHASE_TIME(8, mbar_wait(&e_full[buf], (kt >> 1) & 1)) || *abort_flag) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t e_col = tmem + kOCols + buf * 64;
+          for (int sl = 0; sl < nsl; ++sl) {
+            const int pi = kt * nsl + sl, vb = pi % kVBufs;
+            if (!JK_PHASE_TIME(9, mbar_wait(&vb_full[vb], (pi / kVBufs) & 1))) { ok = false; break; }
+            const int w = static_cast<int>(p.dim) - sl * kVSlice;
+            const uint32_t idesc_pv = idesc_f16(kRows, w < kVSlice ? w : kVSlice, kHalfV ? 0u : 1u) | (1u << 16);
+            const uint32_t v_addr = smem_u32(vbuf + vb * 16384);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+#pragma unroll
+              for (int kk = 0; kk < kEK / 16; ++kk) {
+                mma_f16_ts(tmem + sl * kVSlice, e_col + q * 32 + kk * 8, sdesc_mnmajor_sw128(v_addr + kk * 2048, 8192),
+                           idesc_pv, (kt > 0 || q > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            mma_commit(&vb_empty[vb]);
+          }
+          if (ok) mma_commit(&e_empty[buf]);
+        }
+        if (ok) {
+          mma_commit(agg_bar);
+#ifdef JK_PHASE_PROFILE
+          atomicAdd(&g_phase[12], (unsigned long long)(clock64() - t_iss));
+#endif
+          ok = JK_PHASE_TIME(13, mbar_wait(agg_bar, 0));  // every MMA and commit retired before exit
+        }
       }
       if (!ok) {
         atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
@@ -869,24 +1026,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- select: one warp per row keeps the best k of the row's two candidate stacks
     const int rt0 = warp * (kRows / kSelWarps);
+    // Key scratch in the (now idle) operand region: 128 keys per warp.
+    unsigned long long* ks = reinterpret_cast<unsigned long long*>(smem) + warp * kCap;
     for (int r = 0; r < kRows / kSelWarps; ++r) {
       const int rt = rt0 + r;
-      int n = 0;
+      int n = 0, m0 = 0;
       if (good && t0 + rt < p.n_rows) {
         float* wv = bufv + rt * kStride;
         int* wi = bufi + rt * kStride;
         const int c0 = cnt[rt];
         const int c1 = nsel[rt];
-        n = c0 + c1 <= 64 ? warp_select_row<2>(wv, wi, c0, c1, k, lane)
-                          : warp_select_row<4>(wv, wi, c0, c1, k, lane);
+        const int m = c0 + c1;
+        const bool runs = failrow[rt] == 0;
+#if defined(JK_SEL_EXP) && JK_SEL_EXP == 1
+        n = m < k ? m : k; m0 = n; (void)runs; (void)wv; (void)wi; (void)ks;
+#else
+        n = m <= 32   ? warp_rank_select<1>(wv, wi, c0, c1, k, lane, ks, runs, m0)
+            : m <= 64 ? warp_rank_select<2>(wv, wi, c0, c1, k, lane, ks, runs, m0)
+            : m <= 96 ? warp_rank_select<3>(wv, wi, c0, c1, k, lane, ks, runs, m0)
+                      : warp_rank_select<4>(wv, wi, c0, c1, k, lane, ks, runs, m0);
+#endif
       }
       __syncwarp();
-      if (lane == 0) nsel[rt] = n;
+      if (lane == 0) {
+        nsel[rt] = n;
+        cnt[rt] = m0;  // length of the first ascending column run
+      }
     }
     sel_barrier();
     JK_PHASE_MARK(3, t_prev);
 
     // ---- compress (thread per row), fold the sender strength, form the state output
+    const SlabRange sr = slab_range<VT>(p, t0);
+    const bool tc_agg = MODE == kGather && good && sr.on && ntiles > 0;
     if (half == 0) {
       const Lane F{rv, ri};
       const int n = nsel[row];
@@ -894,9 +1066,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int e = 0; e < n; ++e) F.val(e) += bias;
       if (MODE == kGather && row_ok && good && (p.out_scores || p.out_index)) {
         const int64_t o = (b * p.n_rows + t) * k;
+        // column slot e holds score rank ri[kCap / 2 + e]; outputs go in score order
         for (int e = 0; e < k; ++e) {
-          if (p.out_scores) p.out_scores[o + e] = e < n ? F.val(e) : -INFINITY;
-          if (p.out_index) p.out_index[o + e] = e < n ? static_cast<int64_t>(F.idx(e)) : -1;
+          const int r = e < n ? F.idx(kCap / 2 + e) : e;
+          if (p.out_scores) p.out_scores[o + r] = e < n ? F.val(e) : -INFINITY;
+          if (p.out_index) p.out_index[o + r] = e < n ? static_cast<int64_t>(F.idx(e)) : -1;
         }
       }
       compress_row(F, n, p.compress);
@@ -923,7 +1097,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         st_elem(p.out_state, b * p.n_rows + t, p.out_dtype, acc);
       }
-      if (MODE == kGather) {
+      if (tc_agg) {
+        // Per-half edge lists of the tensor-core aggregate (region 0, kElStride entries
+        // per row): the two ascending column runs are merged, and every edge goes to the
+        // list of the source-tile half it falls in (bit 5 of its window-relative column):
+        // half 0 from entry 0 upwards, half 1 from entry 63 downwards, both ascending.
+        // Entry = (bf16 / f16 hi | lo << 16, window-relative column).
+        constexpr bool kHalfV = std::is_same<VT, __half>::value;
+        uint2* el = reinterpret_cast<uint2*>(smem) + row * kElStride;
+        const int m0 = cnt[row];
+        int a = 0, c = m0, l0 = 0, l1 = 0;
+        for (int e = 0; e < n; ++e) {
+          const bool from0 = a < m0 && (c >= n || F.idx(a) < F.idx(c));
+          const int s = from0 ? a++ : c++;
+          const float w = F.val(s);
+          const int rel = F.idx(s) - sr.s_lo;
+          uint32_t hb, lb;
+          if (kHalfV) {
+            const __half h = __float2half_rn(w);
+            hb = __half_as_ushort(h);
+            lb = __half_as_ushort(__float2half_rn(w - __half2float(h)));
+          } else {
+            const __nv_bfloat16 h = __float2bfloat16_rn(w);
+            hb = __bfloat16_as_ushort(h);
+            lb = __bfloat16_as_ushort(__float2bfloat16_rn(w - __bfloat162float(h)));
+          }
+          const uint2 ent = make_uint2(hb | (lb << 16), static_cast<uint32_t>(rel));
+          if (rel & 32) el[63 - l1++] = ent;
+          else el[l0++] = ent;
+        }
+        cnt[row] = l0;  // list 0 length; list 1 holds n - l0
+      } else if (MODE == kGather) {
         // Pack (weight, column) pairs for the gather, back to front so that every write
         // lands on an already consumed candidate slot of the same row.
         float* tab = bufv + gtab_off(row);
@@ -935,122 +1139,85 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    fence_proxy_async_smem();  // candidate slots are reused by TMA and the MMAs next
     sel_barrier();
     JK_PHASE_MARK(4, t_prev);
 
     // ---- aggregate
+    if (threadIdx.x == 0) {  // tell the MMA warp whether it issues the aggregate
+      *agg_mode = tc_agg ? 1 : 0;
+      mbar_arrive(slab_bar);
+    }
     if (good) {
       const int nrows = kRows / kSelWarps;
       if (MODE == kGather) {
-        int s_lo = 0, nslab = 0;
-        bool slab = false;
-        if (p.slab_ok && p.window >= 0 && sizeof(VT) == 2 && (p.dim % 64) == 0) {
-          const int64_t lo = t0 - p.window;
-          s_lo = lo > 0 ? static_cast<int>(lo) : 0;
-          int64_t hi_col = t0 + kRows - 1;
-          if (hi_col > p.n_cols - 1) hi_col = p.n_cols - 1;
-          nslab = static_cast<int>(hi_col - s_lo + 1);
-          slab = nslab > 0 && nslab <= 1024 && p.dim <= 512;  // dense enough; O fits TMEM
-        }
-        if (slab) {
-          // Tensor-core aggregate over the CTA's source window: for every 128-row source
-          // tile, the selected edges of the 128 target rows form a sparse 128 x 128 matrix
-          // E, written (bf16 / f16 hi + lo planes) into the MMA operand region; thread 0
-          // multiplies it with the tile's values 128 columns at a time (TMA, MN-major 128B
-          // swizzle, double-buffered) into a TMEM accumulator O[128 x dim]:
-          // O += E_hi.V + E_lo.V. The hi + lo planes keep the edge weights to ~16 bits.
+        if (tc_agg) {
+          // Tensor-core aggregate over the CTA's source window. For every 64-row source
+          // tile the selected edges of the 128 target rows form a sparse 128 x 64 matrix E
+          // (bf16 / f16 hi + lo planes), double-buffered in TMEM as the MMA's A operand:
+          // each thread packs its row's half (32 source rows) of the tile from the row's
+          // column-ordered edges in registers and stores it (tcgen05.st, thread = TMEM
+          // lane = row), then its warp signals e_full. The MMA warp forms
+          // O[128 x dim] += E_hi.V + E_lo.V in TMEM with V streamed through shared memory.
+          // The hi + lo planes keep the edge weights to ~16 bits.
           constexpr bool kHalfV = std::is_same<VT, __half>::value;
-          const int ntile = (nslab + 127) / 128;
-          const int nsl = static_cast<int>((p.dim + 127) / 128);  // 128-column value slices
-          const int npair = ntile * nsl;
-          uint8_t* e_hi = smem;              // 2 K atoms (32 KB)
-          uint8_t* e_lo = smem + 2 * 16384;  // 2 K atoms (32 KB)
-          uint8_t* vbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bufi) + 1023) & ~uintptr_t(1023));
-          const int erow = row;  // this thread's target row
-          auto slice_w = [&](int sl) { return static_cast<int>(p.dim - sl * 128 < 128 ? p.dim - sl * 128 : 128); };
-          auto load_v = [&](int pi) {  // (tile, slice) pair pi -> buffer pi & 1
-            const int st = pi / nsl, sl = pi % nsl, nb = slice_w(sl) / 64;
-            mbar_arrive_expect_tx(&vb_full[pi & 1], nb * 16384);
-            for (int a = 0; a < nb; ++a)
-              tma_load_3d(vbuf + (pi & 1) * 32768 + a * 16384, &tm_val, &vb_full[pi & 1], sl * 128 + a * 64,
-                          s_lo + st * 128, static_cast<int>(b));
-          };
-          if (threadIdx.x == 0) {
-            fence_proxy_async_smem();  // the value buffers held generic candidate data before
-            load_v(0);
-            if (npair > 1) load_v(1);
-          }
-          for (int st = 0; st < ntile; ++st) {
-            const int src0 = s_lo + st * 128;
-            uint4* ez = reinterpret_cast<uint4*>(e_hi);
-            for (int i = threadIdx.x; i < 4096; i += kSelWarps * 32) ez[i] = make_uint4(0, 0, 0, 0);
-            sel_barrier();
-            if (t0 + erow < p.n_rows) {
-              const float* tab = bufv + gtab_off(erow);
-              const int n = nsel[erow];
-              for (int e = half; e < n; e += 2) {
-                const int kcol = __float_as_int(tab[2 * e + 1]) - src0;
-                if (static_cast<uint32_t>(kcol) < 128u) {
-                  const float w = tab[2 * e];
-                  const int kin = kcol & 63;
-                  const int off = (kcol >> 6) * 16384 + (erow >> 3) * 1024 + (erow & 7) * 128 +
-                                  (((kin >> 3) ^ (erow & 7)) << 4) + (kin & 7) * 2;
-                  if (kHalfV) {
-                    const __half h = __float2half_rn(w);
-                    *reinterpret_cast<__half*>(e_hi + off) = h;
-                    *reinterpret_cast<__half*>(e_lo + off) = __float2half_rn(w - __half2float(h));
-                  } else {
-                    const __nv_bfloat16 h = __float2bfloat16_rn(w);
-                    *reinterpret_cast<__nv_bfloat16*>(e_hi + off) = h;
-                    *reinterpret_cast<__nv_bfloat16*>(e_lo + off) = __float2bfloat16_rn(w - __bfloat162float(h));
-                  }
-                }
-              }
-            }
-            fence_proxy_async_smem();
-            sel_barrier();
-            if (threadIdx.x == 0) {
-              bool okm = true;
-              for (int sl = 0; sl < nsl && okm; ++sl) {
-                const int pi = st * nsl + sl;
-                if (!mbar_wait(&vb_full[pi & 1], (pi >> 1) & 1)) { okm = false; break; }
-                tc_fence_after();
-                const int w = slice_w(sl);
-                const uint32_t idesc_pv = idesc_f16(128, w, kHalfV ? 0u : 1u) | (1u << 16);
-                const uint32_t vaddr = smem_u32(vbuf + (pi & 1) * 32768);
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                  const uint32_t eaddr = smem_u32(q == 0 ? e_hi : e_lo);
-#pragma unroll
-                  for (int kk = 0; kk < 8; ++kk) {
-                    mma_f16_ss(tmem + sl * 128, sdesc_kmajor_sw128(eaddr + (kk >> 2) * 16384 + (kk & 3) * 32),
-                               sdesc_mnmajor_sw128(vaddr + kk * 2048, 16384), idesc_pv,
-                               (st > 0 || q > 0 || kk > 0) ? 1u : 0u);
-                  }
-                }
-                mma_commit(&vb_empty[pi & 1]);
-                if (pi + 2 < npair) {  // refill this buffer once its MMAs retired
-                  if (!mbar_wait(&vb_empty[pi & 1], (pi >> 1) & 1)) { okm = false; break; }
-                  load_v(pi + 2);
-                }
-              }
-              if (okm) {
-                mma_commit(agg_bar);
-              } else {
-                atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
-                *abort_flag = 1;
-              }
-            }
-            sel_barrier();
-            if (*abort_flag) break;
-            if (!mbar_wait(agg_bar, st & 1)) {  // E may be rewritten once its MMAs retired
+          const int nkt = (sr.n + kEK - 1) / kEK;
+          // this thread's edge list (ascending window-relative columns)
+          const uint2* el = reinterpret_cast<const uint2*>(smem) + row * kElStride;
+          const int len = half == 0 ? cnt[row] : nsel[row] - cnt[row];
+          auto entry = [&](int i) { return el[half == 0 ? i : 63 - i]; };
+          int cur = 0;
+          uint2 nx = len > 0 ? entry(0) : make_uint2(0u, 0x7FFFFFFFu);
+          const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + kOCols + half * 16;
+          for (int kt = 0; kt < nkt; ++kt) {
+            const int buf = kt & 1;
+            if (kt >= 2 && !JK_PHASE_TIME(11, mbar_wait(&e_empty[buf], ((kt >> 1) - 1) & 1))) {
               atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
               *abort_flag = 1;
-              break;
             }
+            if (*abort_flag) break;
             tc_fence_after();
+            uint32_t ehi[16], elo[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ehi[i] = elo[i] = 0u;
+#ifdef JK_PHASE_PROFILE
+            long long t_take = clock64();
+#endif
+            while (static_cast<int>(nx.y >> 6) == kt) {
+              const uint2 e = nx;
+              ++cur;
+              nx = cur < len ? entry(cur) : make_uint2(0u, 0x7FFFFFFFu);  // prefetch the next
+              const int kin = static_cast<int>(e.y & 31);
+              const int sh = (kin & 1) * 16;
+              const int r = kin >> 1;
+              const uint32_t hb = (e.x & 0xFFFFu) << sh, lb = (e.x >> 16) << sh;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                ehi[i] |= (i == r) ? hb : 0u;
+                elo[i] |= (i == r) ? lb : 0u;
+              }
+            }
+#ifdef JK_PHASE_PROFILE
+            if (lane == 0) atomicAdd(&g_phase[14], (unsigned long long)(clock64() - t_take));
+            t_take = clock64();
+#endif
+            tmem_st_32x32b_x16(lane_base + buf * 64, ehi);
+            tmem_st_32x32b_x16(lane_base + buf * 64 + 32, elo);
+            tmem_st_wait();
+#ifdef JK_PHASE_PROFILE
+            if (lane == 0) atomicAdd(&g_phase[15], (unsigned long long)(clock64() - t_take));
+#endif
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&e_full[buf]);
           }
-          sel_barrier();
+          JK_PHASE_MARK(6, t_prev);
+          if (!*abort_flag && !mbar_wait(agg_bar, 0)) {
+            atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
+            *abort_flag = 1;
+          }
+          tc_fence_after();
+          JK_PHASE_MARK(7, t_prev);
           if (!*abort_flag) {
             // O -> outputs (thread = row; half = which half of the columns)
             const int hcols = static_cast<int>(p.dim / 2);  // multiple of 32
@@ -1058,8 +1225,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t v[32];
               tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * hcols + c0, v);
               tmem_ld_wait();
-              if (t0 + erow < p.n_rows) {
-                const int64_t base = (b * p.n_rows + t0 + erow) * p.dim + half * hcols + c0;
+              if (row_ok) {
+                const int64_t base = (b * p.n_rows + t) * p.dim + half * hcols + c0;
 #pragma unroll
                 for (int e = 0; e < 32; e += 8) {
                   float f[8];
@@ -1140,7 +1307,7 @@ int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_
   tv = tc;  // placeholder when the slab path is off
   p.slab_ok = 0;
   if (MODE == kGather && p.window >= 0 && p.val_dtype != JK_F32 && p.dim % 64 == 0 && aligned16(p.col_val)) {
-    if (make_tmap_3d_16bit(&tv, p.col_val, p.dim, n_cols, batch, 64, 128, p.val_dtype == JK_BF16, true) == JK_OK)
+    if (make_tmap_3d_16bit(&tv, p.col_val, p.dim, n_cols, batch, 64, kEK, p.val_dtype == JK_BF16, true) == JK_OK)
       p.slab_ok = 1;
   }
   const uint32_t idesc = idesc_f16(kRows, kCols, bf16 ? 1u : 0u);
@@ -1274,9 +1441,9 @@ extern "C" int jk_transition_pairwise_topk_forward(const void* src_proj, const v
 #ifdef JK_PHASE_PROFILE
 extern "C" int jk_debug_phase(unsigned long long* out, int reset) {
   cudaDeviceSynchronize();
-  cudaMemcpyFromSymbol(out, jk::topk::g_phase, sizeof(unsigned long long) * 8);
+  cudaMemcpyFromSymbol(out, jk::topk::g_phase, sizeof(unsigned long long) * 16);
   if (reset) {
-    unsigned long long z[8] = {0};
+    unsigned long long z[16] = {0};
     cudaMemcpyToSymbol(jk::topk::g_phase, z, sizeof(z));
   }
   return 0;
