@@ -45,7 +45,7 @@ namespace topk {
 
 #ifdef JK_PHASE_PROFILE
 // Debug-only phase timer (sum over selection warps of clock64 deltas per phase).
-__device__ unsigned long long g_phase[16];
+__device__ unsigned long long g_phase[24];
 #define JK_PHASE_MARK(i, t_prev)                                                                \
   do {                                                                                         \
     const long long _now = clock64();                                                          \
@@ -78,7 +78,8 @@ constexpr int kMmaWarp = kSelWarps;       // tcgen05.mma issuer
 constexpr int kLoadWarp = kSelWarps + 1;  // TMA loader
 constexpr int kThreads = (kSelWarps + 2) * 32;
 constexpr int kSentinel = INT_MAX;
-static_assert(kStride >= kCap + 2 * kQueue, "buffer row holds candidates and both fallback queues");
+constexpr int kJunk = kCap + 2 * kQueue;  // scratch slot of a row for branch-free appends
+static_assert(kStride > kJunk, "buffer row holds candidates, both fallback queues and the junk slot");
 static_assert(kCap / 2 >= 64, "the score-rank permutation sits behind k <= 64 selected slots");
 
 enum Mode { kGather = 0, kScatter = 1 };
@@ -509,6 +510,9 @@ __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int l
     rank[q] = 0;
   }
   __syncwarp();  // from here on rv / ri of the row are free: every lane holds its keys
+#ifdef JK_PHASE_PROFILE
+  long long t_sel = clock64();
+#endif
   int j = 0;
   for (; j + 4 <= n; j += 4) {
     const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(ks + j);
@@ -522,6 +526,10 @@ __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int l
 #pragma unroll
     for (int q = 0; q < NQ; ++q) rank[q] += a > x[q];
   }
+#ifdef JK_PHASE_PROFILE
+  if (lane == 0) atomicAdd(&g_phase[16], (unsigned long long)(clock64() - t_sel));
+  t_sel = clock64();
+#endif
   int real = 0;
   bool keep[NQ];
   int col[NQ], slot[NQ];
@@ -573,6 +581,9 @@ __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int l
     }
   }
   __syncwarp();
+#ifdef JK_PHASE_PROFILE
+  if (lane == 0) atomicAdd(&g_phase[17], (unsigned long long)(clock64() - t_sel));
+#endif
   return real < k ? real : k;
 }
 
@@ -872,7 +883,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Loads this thread's 64 scores of iteration g into v; false on timeout / abort.
     auto load_tile = [&](uint32_t (&v)[2][32]) -> bool {
       const int buf = g & 1;
-      if (!mbar_wait(&tfull[buf], (g >> 1) & 1) || *abort_flag) return false;
+      if (!JK_PHASE_TIME(18, mbar_wait(&tfull[buf], (g >> 1) & 1)) || *abort_flag) return false;
       tc_fence_after();
       tmem_ld_32x32b_x32(tmem + tbase + buf * kCols, v[0]);
       tmem_ld_32x32b_x32(tmem + tbase + buf * kCols + 32, v[1]);
@@ -939,16 +950,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
+            // branch-free append: a failing column (or an overflowing one) goes to the
+            // row's junk slot kJunk
             const int col = col0 + c * 32 + e;
             const float x = __uint_as_float(v[c][e]);
-            if (static_cast<uint32_t>(col - lo_t) <= span && x >= th) {
-              if (myc < kCap) {
-                const int slot = half == 0 ? myc : kCap - 1 - myc;
-                rv[slot] = x;
-                ri[slot] = col;
-              }
-              ++myc;
-            }
+            const bool pass = static_cast<uint32_t>(col - lo_t) <= span && x >= th;
+            const int slot = (pass && myc < kCap) ? (half == 0 ? myc : kCap - 1 - myc) : kJunk;
+            rv[slot] = x;
+            ri[slot] = col;
+            myc += pass ? 1 : 0;
           }
       }
       (half == 0 ? cnt : nsel)[row] = myc;
@@ -1038,14 +1048,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c1 = nsel[rt];
         const int m = c0 + c1;
         const bool runs = failrow[rt] == 0;
-#if defined(JK_SEL_EXP) && JK_SEL_EXP == 1
-        n = m < k ? m : k; m0 = n; (void)runs; (void)wv; (void)wi; (void)ks;
-#else
         n = m <= 32   ? warp_rank_select<1>(wv, wi, c0, c1, k, lane, ks, runs, m0)
             : m <= 64 ? warp_rank_select<2>(wv, wi, c0, c1, k, lane, ks, runs, m0)
             : m <= 96 ? warp_rank_select<3>(wv, wi, c0, c1, k, lane, ks, runs, m0)
                       : warp_rank_select<4>(wv, wi, c0, c1, k, lane, ks, runs, m0);
-#endif
       }
       __syncwarp();
       if (lane == 0) {
@@ -1441,9 +1447,9 @@ extern "C" int jk_transition_pairwise_topk_forward(const void* src_proj, const v
 #ifdef JK_PHASE_PROFILE
 extern "C" int jk_debug_phase(unsigned long long* out, int reset) {
   cudaDeviceSynchronize();
-  cudaMemcpyFromSymbol(out, jk::topk::g_phase, sizeof(unsigned long long) * 16);
+  cudaMemcpyFromSymbol(out, jk::topk::g_phase, sizeof(unsigned long long) * 24);
   if (reset) {
-    unsigned long long z[16] = {0};
+    unsigned long long z[24] = {0};
     cudaMemcpyToSymbol(jk::topk::g_phase, z, sizeof(z));
   }
   return 0;
