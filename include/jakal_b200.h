@@ -134,6 +134,27 @@ int jk_propagation_window_forward(const void* row_proj, const void* col_proj, in
                                   void* out_state, void* out_val, int out_dtype,
                                   jk_stream_t stream);
 
+/* Dense pairwise transition (Transition.forward with a dense route, transition.py:238-254):
+ * every source routes to every destination, routes compressed over the destinations of
+ * the source (JK_SOFTMAX | JK_SIGNED_ABS_SOFTMAX | JK_SIGNED_ENTMAX15), times the source's
+ * sender strength, accumulated into the destinations:
+ *   out_state[d] = sum_s r[s,d] * sender[s] * src_state[s],
+ *   out_val[d]   = sum_s r[s,d] * sender[s] * src_val[s].
+ * src_proj [B, n_src, rp] (route source projection divided by the temperature) and
+ * dst_proj [B, n_dst, rp]; logits = src_proj . dst_proj + score_bias (+ *bias_dev).
+ * stats: caller scratch of batch * n_src * 3 floats (per-source max, sender / normaliser,
+ * entmax threshold). dim % 64 == 0; f32 values as bf16 hi (src_val) + lo (src_val_lo)
+ * planes, like jk_propagation_window_forward.
+ * Replaces transition_pairwise_dense (jakal_net_native.cpp:6705-6914; native_backend.py
+ * :5801-5822). */
+int jk_transition_pairwise_dense_forward(const void* src_proj, const void* dst_proj, int64_t batch,
+                                         int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                         const void* src_state, const void* sender, int state_dtype,
+                                         const void* src_val, const void* src_val_lo, int64_t dim,
+                                         float score_bias, const float* bias_dev, int compress,
+                                         float* stats, void* out_state, void* out_val, int out_dtype,
+                                         jk_stream_t stream);
+
 /* f32 -> three bf16 planes [h|m|l|0] of 32 columns (rank <= 32), out [rows, 128] bf16, for
  * JK_BF16X3 projections. Replaces nothing: the reference computes these dots in f32. */
 int jk_split3_bf16(const float* x, int64_t rows, int64_t rank, void* out, jk_stream_t stream);

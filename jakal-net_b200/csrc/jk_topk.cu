@@ -1166,7 +1166,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           // lane = row), then its warp signals e_full. The MMA warp forms
           // O[128 x dim] += E_hi.V + E_lo.V in TMEM with V streamed through shared memory.
           // The hi + lo planes keep the edge weights to ~16 bits.
-          constexpr bool kHalfV = std::is_same<VT, __half>::value;
           const int nkt = (sr.n + kEK - 1) / kEK;
           // this thread's edge list (ascending window-relative columns)
           const uint2* el = reinterpret_cast<const uint2*>(smem) + row * kElStride;

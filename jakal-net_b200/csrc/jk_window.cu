@@ -58,7 +58,25 @@ struct Params {
   int vsplit;      // values come as bf16 hi / lo planes (f32 values)
   int d0;          // first value column of this launch's slice
   int slice_cols;  // value columns of the slice (multiple of 64, <= kMaxSlice)
+  // Statistics mode (stats_out != null): only the normalising passes run; every row writes
+  // (max, row_scale[row] / normaliser, entmax tau) as 3 floats and nothing is aggregated.
+  float* stats_out;
+  const void* row_scale;  // state dtype; null = 1
+  // Column-statistics mode (col_stats != null): a single final pass whose edges are
+  // normalised per COLUMN with the (max, scale / normaliser, tau) triples a statistics-mode
+  // launch wrote for the columns (the transposed route normalisation of a transition).
+  const float* col_stats;
 };
+
+// One edge from a score and the (max, scale / normaliser, tau) of its normalisation set.
+__device__ __forceinline__ float edge_of(float s, int compress, float m, float inv, float tau) {
+  if (compress == JK_SOFTSIGN) return s / (1.f + fabsf(s));
+  if (compress == JK_SOFTMAX) return expf(s - m) * inv;
+  const float sg = s > 0.f ? 1.f : (s < 0.f ? -1.f : 0.f);
+  if (compress == JK_SIGNED_ABS_SOFTMAX) return sg * expf(fabsf(s) - m) * inv;
+  const float pz = fmaxf((fabsf(s) - m) * 0.5f - tau, 0.f);
+  return sg * pz * pz * inv;
+}
 
 template <int KATOMS>
 struct Layout {
@@ -77,8 +95,6 @@ struct Layout {
 __device__ __forceinline__ void sel_barrier() {
   asm volatile("bar.sync 1, %0;" ::"r"(kSelWarps * 32) : "memory");
 }
-
-__device__ __forceinline__ float sgnf(float x) { return x > 0.f ? 1.f : (x < 0.f ? -1.f : 0.f); }
 
 // Packs 8 f32 edges into 8 16-bit hi parts and 8 lo parts (e - hi).
 __device__ __forceinline__ void split8(const float (&e)[8], bool f16, uint4& hi, uint4& lo) {
@@ -339,7 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     // First pass.
-    int pass = p.compress == JK_SOFTSIGN ? kFinal : kStatsMax;
+    const bool stats_mode = p.stats_out != nullptr;
+    const bool col_mode = p.col_stats != nullptr;
+    const bool plain = p.compress == JK_SOFTMAX;  // normalised over s, not |s|
+    int pass = (p.compress == JK_SOFTSIGN || col_mode) ? kFinal : kStatsMax;
     if (threadIdx.x == 0) {
       *next_pass = ntiles > 0 ? pass : kDone;
       mbar_arrive(decide);
@@ -356,12 +375,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           float tm = m;
 #pragma unroll
           for (int e = 0; e < 64; ++e)
-            if (static_cast<uint32_t>(col0 + e - lo_t) <= span) tm = fmaxf(tm, fabsf(x[e]));
-          if (p.compress == JK_SIGNED_ABS_SOFTMAX && tm > -INFINITY) {
+            if (static_cast<uint32_t>(col0 + e - lo_t) <= span) tm = fmaxf(tm, plain ? x[e] : fabsf(x[e]));
+          if ((p.compress == JK_SIGNED_ABS_SOFTMAX || plain) && tm > -INFINITY) {
             z = (m > -INFINITY) ? z * expf(m - tm) : 0.f;
 #pragma unroll
             for (int e = 0; e < 64; ++e)
-              if (static_cast<uint32_t>(col0 + e - lo_t) <= span) z += expf(fabsf(x[e]) - tm);
+              if (static_cast<uint32_t>(col0 + e - lo_t) <= span) z += expf((plain ? x[e] : fabsf(x[e])) - tm);
           }
           m = tm;
         }
@@ -382,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           rcount[row] = 0x7FFFFFFF;
           rconv[row] = 0;
         }
-        pass = p.compress == JK_SIGNED_ABS_SOFTMAX ? kFinal : kStatsEnt;
+        pass = (p.compress == JK_SIGNED_ABS_SOFTMAX || plain) ? kFinal : kStatsEnt;
       } else {  // kStatsEnt: support statistics for z > tau
         const float mrow = rmax[row], tau = rtau[row];
         float c = 0.f, s1 = 0.f, s2 = 0.f;
@@ -435,10 +454,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!*vote || iters >= kMaxEntIters) pass = kFinal;
       }
       if (threadIdx.x == 0) {
-        *next_pass = (ok && !*abort_flag) ? pass : kDone;
+        // a statistics-mode launch ends where the final pass would start
+        *next_pass = (ok && !*abort_flag && !(stats_mode && pass == kFinal)) ? pass : kDone;
         mbar_arrive(decide);
       }
       if (*abort_flag) ok = false;
+    }
+    if (stats_mode) {
+      if (ok && pass == kFinal && half == 0 && row_ok) {
+        const float norm = rnorm[row];
+        const float inv = (p.compress == JK_SIGNED_ENTMAX15) ? (norm > 0.f ? 1.f / fmaxf(norm, FLT_EPSILON) : 0.f)
+                                                              : (norm > 0.f ? 1.f / norm : 0.f);
+        const float scale = p.row_scale ? ld_elem(p.row_scale, b * p.n_rows + t, p.state_dtype) : 1.f;
+        float* o = p.stats_out + (b * p.n_rows + t) * 3;
+        o[0] = rmax[row];
+        o[1] = inv * scale;
+        o[2] = rtau[row];
+      }
+      pass = kDone;
     }
 
     // Final pass: exact edges -> hi / lo edge tiles -> producer multiplies with the values.
@@ -455,19 +488,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!load_tile(x)) { ok = false; break; }
         const int col0 = static_cast<int>((j_lo + it) * kCols) + half * kHalfCols;
         float ev[64];
-#pragma unroll
-        for (int e = 0; e < 64; ++e) {
-          const float s = x[e];
-          float w;
-          if (p.compress == JK_SOFTSIGN) {
-            w = s / (1.f + fabsf(s));
-          } else if (p.compress == JK_SIGNED_ABS_SOFTMAX) {
-            w = sgnf(s) * expf(fabsf(s) - mrow) * inv;
-          } else {
-            const float pz2 = fmaxf((fabsf(s) - mrow) * 0.5f - tau, 0.f);
-            w = sgnf(s) * pz2 * pz2 * inv;
+        if (col_mode) {
+          // per-column normalisation: the column's triple (broadcast loads, L1-resident)
+#pragma unroll 8
+          for (int e = 0; e < 64; ++e) {
+            const int col = col0 + e;
+            const float* cs = p.col_stats + (cb + (col < p.n_cols ? col : 0)) * 3;
+            const float w = edge_of(x[e], p.compress, __ldg(cs), __ldg(cs + 1), __ldg(cs + 2));
+            ev[e] = static_cast<uint32_t>(col - lo_t) <= span ? w : 0.f;
           }
-          ev[e] = static_cast<uint32_t>(col0 + e - lo_t) <= span ? w : 0.f;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const float w = edge_of(x[e], p.compress, mrow, inv, tau);
+            ev[e] = static_cast<uint32_t>(col0 + e - lo_t) <= span ? w : 0.f;
+          }
         }
         // state: sum_s e * state[s] over this thread's visible columns
         for (int e0 = 0; e0 < 64; e0 += 8) {
@@ -501,38 +536,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
       }
     }
-    // Epilogue: O from TMEM, state from the two halves.
-    pst[half * kRows + row] = state_acc;
-    const bool have_o = ok && pass == kFinal && !*abort_flag;
-    bool got_o = false;
-    if (have_o) got_o = mbar_wait(obar, 0);
-    if (have_o && !got_o) {
-      atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
-      *abort_flag = 1;
-    }
-    sel_barrier();
-    if (half == 0 && row_ok && d0 == 0) {
-      st_elem(p.out_state, b * p.n_rows + t, p.out_dtype, pst[row] + pst[kRows + row]);
-    }
-    tc_fence_after();
-    const int hcols = dc / 2;  // multiple of 32
-    for (int c0 = 0; c0 < hcols; c0 += 32) {
-      uint32_t v[32];
-      if (got_o) {
-        tmem_ld_32x32b_x32(tmem_o + (static_cast<uint32_t>(quad * 32) << 16) + half * hcols + c0, v);
-        tmem_ld_wait();
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = 0u;
+    // Epilogue: O from TMEM, state from the two halves (not in statistics mode).
+    if (!stats_mode) {
+      pst[half * kRows + row] = state_acc;
+      const bool have_o = ok && pass == kFinal && !*abort_flag;
+      bool got_o = false;
+      if (have_o) got_o = mbar_wait(obar, 0);
+      if (have_o && !got_o) {
+        atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
+        *abort_flag = 1;
       }
-      if (row_ok) {
-        const int64_t base = (b * p.n_rows + t) * p.dim + d0 + half * hcols + c0;
+      sel_barrier();
+      if (half == 0 && row_ok && d0 == 0) {
+        st_elem(p.out_state, b * p.n_rows + t, p.out_dtype, pst[row] + pst[kRows + row]);
+      }
+      tc_fence_after();
+      const int hcols = dc / 2;  // multiple of 32
+      for (int c0 = 0; c0 < hcols; c0 += 32) {
+        uint32_t v[32];
+        if (got_o) {
+          tmem_ld_32x32b_x32(tmem_o + (static_cast<uint32_t>(quad * 32) << 16) + half * hcols + c0, v);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-        for (int e = 0; e < 32; e += 8) {
-          float f[8];
+          for (int e = 0; e < 32; ++e) v[e] = 0u;
+        }
+        if (row_ok) {
+          const int64_t base = (b * p.n_rows + t) * p.dim + d0 + half * hcols + c0;
 #pragma unroll
-          for (int u = 0; u < 8; ++u) f[u] = __uint_as_float(v[e + u]);
-          topk::store8(p.out_val, base + e, p.out_dtype, f);
+          for (int e = 0; e < 32; e += 8) {
+            float f[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) f[u] = __uint_as_float(v[e + u]);
+            topk::store8(p.out_val, base + e, p.out_dtype, f);
+          }
         }
       }
     }
@@ -553,8 +590,11 @@ int launch(const void* row_proj, const void* col_proj, const void* col_val, cons
   if (status != JK_OK) return status;
   status = make_tmap_3d_16bit(&tc, col_proj, rp, n_cols, batch, 64, kCols, bf16);
   if (status != JK_OK) return status;
-  status = make_tmap_3d_16bit(&tv, col_val, p.dim, n_cols, batch, 64, kCols, bf16);
-  if (status != JK_OK) return status;
+  tv = tc;  // statistics mode reads no values
+  if (col_val != nullptr) {
+    status = make_tmap_3d_16bit(&tv, col_val, p.dim, n_cols, batch, 64, kCols, bf16);
+    if (status != JK_OK) return status;
+  }
   tvl = tv;
   if (p.vsplit) {
     status = make_tmap_3d_16bit(&tvl, col_val_lo, p.dim, n_cols, batch, 64, kCols, bf16);
@@ -574,6 +614,13 @@ int launch(const void* row_proj, const void* col_proj, const void* col_val, cons
   // One launch per value-column slice (the value MMA's N is the slice width; the last
   // slice may be narrower). Every slice recomputes the scores and edges.
   const dim3 grid(static_cast<unsigned>((n_rows + kRows - 1) / kRows), static_cast<unsigned>(batch), 1);
+  if (p.stats_out != nullptr) {  // one launch: the statistics do not depend on the values
+    Params q = p;
+    q.d0 = 0;
+    q.slice_cols = 64;
+    kern<<<grid, kThreads, sm, st>>>(tr, tc, tv, tvl, q, idesc_s, idesc_f16(kRows, 64, fmt) | (1u << 16));
+    return launch_status();
+  }
   for (int d0 = 0; d0 < p.dim; d0 += per) {
     const int width = static_cast<int>(p.dim - d0 < per ? p.dim - d0 : per);
     Params q = p;
@@ -590,13 +637,14 @@ int launch(const void* row_proj, const void* col_proj, const void* col_val, cons
 }  // namespace win
 }  // namespace jk
 
-extern "C" int jk_propagation_window_forward(const void* row_proj, const void* col_proj, int64_t batch,
-                                             int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
-                                             const void* col_state, int state_dtype, const void* col_val,
-                                             const void* col_val_lo, int64_t dim, int64_t window, float score_bias,
-                                             const float* bias_dev, int compress, void* out_state, void* out_val,
-                                             int out_dtype, jk_stream_t stream) {
-  using namespace jk;
+namespace jk {
+namespace win {
+
+// Checks shared by the window entry points; fills the common Params.
+int prepare(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols, int64_t rp,
+            int proj_dtype, const void* col_state, int state_dtype, const void* col_val, const void* col_val_lo,
+            int64_t dim, float score_bias, const float* bias_dev, int compress, void* out_state, void* out_val,
+            int out_dtype, Params& p) {
   if (row_proj == nullptr || col_proj == nullptr || col_state == nullptr || col_val == nullptr ||
       out_state == nullptr || out_val == nullptr)
     return JK_ERR_BAD_ARG;
@@ -604,22 +652,17 @@ extern "C" int jk_propagation_window_forward(const void* row_proj, const void* c
   if (proj_dtype == JK_BF16X3 && rp != 128) return JK_ERR_BAD_SHAPE;
   if (col_val_lo != nullptr && proj_dtype == JK_F16) return JK_ERR_BAD_DTYPE;
   if (state_dtype < JK_F32 || state_dtype > JK_F16 || out_dtype < JK_F32 || out_dtype > JK_F16) return JK_ERR_BAD_DTYPE;
-  if (compress != JK_SOFTSIGN && compress != JK_SIGNED_ABS_SOFTMAX && compress != JK_SIGNED_ENTMAX15)
-    return JK_ERR_UNSUPPORTED_KIND;
   if (batch <= 0 || n_rows <= 0 || n_cols <= 0 || dim <= 0 || dim % 64 != 0) return JK_ERR_BAD_SHAPE;
   if (batch > 65535 || n_rows > (int64_t(1) << 30) || n_cols > (int64_t(1) << 30)) return JK_ERR_BAD_SHAPE;
   if (rp != 64 && rp != 128) return JK_ERR_BAD_SHAPE;
-  if (window < -1) return JK_ERR_BAD_ARG;
   if (!aligned16(row_proj) || !aligned16(col_proj) || !aligned16(col_val) || !aligned16(out_val) ||
       (col_val_lo != nullptr && !aligned16(col_val_lo)))
     return JK_ERR_ALIGNMENT;
-  int st = check_device();
-  if (st != JK_OK) return st;
-  win::Params p{};
+  p = Params{};
   p.n_rows = n_rows;
   p.n_cols = n_cols;
   p.dim = dim;
-  p.window = window;
+  p.window = -1;
   p.bias = score_bias;
   p.bias_dev = bias_dev;
   p.compress = compress;
@@ -631,8 +674,66 @@ extern "C" int jk_propagation_window_forward(const void* row_proj, const void* c
   p.col_state = col_state;
   p.out_state = out_state;
   p.out_val = out_val;
+  return check_device();
+}
+
+int run(const void* row_proj, const void* col_proj, const void* col_val, const void* col_val_lo, int64_t batch,
+        int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype, Params& p, jk_stream_t stream) {
   auto cs = reinterpret_cast<cudaStream_t>(stream);
   const bool bf16 = proj_dtype != JK_F16;
-  if (rp == 64) return win::launch<1>(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, bf16, p, cs);
-  return win::launch<2>(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, bf16, p, cs);
+  if (rp == 64) return launch<1>(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, bf16, p, cs);
+  return launch<2>(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, bf16, p, cs);
+}
+
+}  // namespace win
+}  // namespace jk
+
+extern "C" int jk_propagation_window_forward(const void* row_proj, const void* col_proj, int64_t batch,
+                                             int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
+                                             const void* col_state, int state_dtype, const void* col_val,
+                                             const void* col_val_lo, int64_t dim, int64_t window, float score_bias,
+                                             const float* bias_dev, int compress, void* out_state, void* out_val,
+                                             int out_dtype, jk_stream_t stream) {
+  using namespace jk;
+  if (compress != JK_SOFTSIGN && compress != JK_SIGNED_ABS_SOFTMAX && compress != JK_SIGNED_ENTMAX15)
+    return JK_ERR_UNSUPPORTED_KIND;
+  if (window < -1) return JK_ERR_BAD_ARG;
+  win::Params p;
+  const int st = win::prepare(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype,
+                              col_val, col_val_lo, dim, score_bias, bias_dev, compress, out_state, out_val, out_dtype,
+                              p);
+  if (st != JK_OK) return st;
+  p.window = window;
+  return win::run(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, proj_dtype, p, stream);
+}
+
+extern "C" int jk_transition_pairwise_dense_forward(const void* src_proj, const void* dst_proj, int64_t batch,
+                                                    int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                                    const void* src_state, const void* sender, int state_dtype,
+                                                    const void* src_val, const void* src_val_lo, int64_t dim,
+                                                    float score_bias, const float* bias_dev, int compress,
+                                                    float* stats, void* out_state, void* out_val, int out_dtype,
+                                                    jk_stream_t stream) {
+  using namespace jk;
+  if (compress != JK_SOFTMAX && compress != JK_SIGNED_ABS_SOFTMAX && compress != JK_SIGNED_ENTMAX15)
+    return JK_ERR_UNSUPPORTED_KIND;
+  if (stats == nullptr) return JK_ERR_BAD_ARG;
+  // Aggregate launch: rows = destinations, columns = sources, per-column normalisation.
+  win::Params agg;
+  int st = win::prepare(dst_proj, src_proj, batch, n_dst, n_src, rp, proj_dtype, src_state, state_dtype, src_val,
+                        src_val_lo, dim, score_bias, bias_dev, compress, out_state, out_val, out_dtype, agg);
+  if (st != JK_OK) return st;
+  // Statistics launch: rows = sources, columns = destinations; the sender strength scales
+  // each source's normaliser.
+  win::Params sp = agg;
+  sp.n_rows = n_src;
+  sp.n_cols = n_dst;
+  sp.stats_out = stats;
+  sp.row_scale = sender;
+  sp.out_state = nullptr;
+  sp.out_val = nullptr;
+  st = win::run(src_proj, dst_proj, nullptr, nullptr, batch, n_src, n_dst, rp, proj_dtype, sp, stream);
+  if (st != JK_OK) return st;
+  agg.col_stats = stats;
+  return win::run(dst_proj, src_proj, src_val, src_val_lo, batch, n_dst, n_src, rp, proj_dtype, agg, stream);
 }

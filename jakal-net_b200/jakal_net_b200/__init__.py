@@ -58,6 +58,7 @@ _SUPPORTED_OPS = (
     "propagation_window",
     "propagation_query_dense",
     "propagation_topk",
+    "transition_pairwise_dense",
     "transition_pairwise_topk",
     "transition_query_topk",
 )
@@ -380,6 +381,76 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
             out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))
 
 
+def _value_planes(pval: Tensor, proj_dtype: torch.dtype):
+    """Values for the window-kernel value GEMM: padded to 64 columns; f32 values become bf16
+    hi + lo planes (both multiplied by the hi + lo edge planes). Returns (val, val_lo, pad)."""
+    out_dim = pval.shape[-1]
+    pad = (-out_dim) % 64
+    if pad:
+        pval = torch.nn.functional.pad(pval, (0, pad))
+    pval_lo = None
+    if proj_dtype == torch.float32:
+        pval = pval.float().contiguous()
+        hi = torch.empty(pval.shape, device=pval.device, dtype=torch.bfloat16)
+        pval_lo = torch.empty_like(hi)
+        with torch.cuda.device(pval.device):
+            check(_LIBRARY.jk_split2_bf16(pval.data_ptr(), pval.numel(), hi.data_ptr(), pval_lo.data_ptr(),
+                                          _stream(pval.device)), "jk_split2_bf16")
+        pval = hi
+    elif pval.dtype != proj_dtype:
+        pval = pval.to(proj_dtype)
+    return pval.contiguous(), pval_lo, pad
+
+
+def transition_pairwise_dense(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                              hidden_weight, hidden_bias, out_weight, out_bias, route_compress_name, temperature,
+                              sender_strength, src_val, dst_val, projected_state, projected_val, src_block_size,
+                              dst_block_size):
+    """Dense pairwise Transition forward (jakal_net_native.cpp:6705-6914; transition.py:238-254):
+    routes of every source compressed over all destinations, sender-weighted, accumulated into
+    the destinations. Two fused launches: per-source route statistics, then the per-destination
+    aggregate with per-column normalisation."""
+    for name, t in (("sender_strength", sender_strength), ("src_val", src_val), ("dst_val", dst_val),
+                    ("projected_state", projected_state), ("projected_val", projected_val)):
+        _require_cuda(name, t)
+    if route_compress_name not in _ROUTE_CODE:
+        raise RuntimeError(f"Unsupported route compress {route_compress_name!r}")
+    batch_shape = src_val.shape[:-2]
+    n_src = src_val.shape[-2]
+    n_dst = dst_val.shape[-2]
+    out_dim = projected_val.shape[-1]
+    sv = _flatten_val(src_val)
+    dv = _flatten_val(dst_val)
+    src_proj, dst_proj, bias_t = _route_projections(route_kind, source_weight, source_bias, target_weight,
+                                                    target_bias, core_weight, bias, hidden_weight, hidden_bias,
+                                                    out_weight, out_bias, temperature, sv, dv)
+    pstate = _flatten_state(projected_state)
+    sender = _flatten_state(sender_strength).to(pstate.dtype).contiguous()
+    pval, pval_lo, pad = _value_planes(_flatten_val(projected_val), sv.dtype)
+    B = sv.shape[0]
+    dev = sv.device
+    same = projected_state.dtype == projected_val.dtype
+    out_dtype = projected_val.dtype if same else torch.float32
+    stats = torch.empty(B * n_src * 3, device=dev, dtype=torch.float32)
+    out_state = torch.empty((B, n_dst), device=dev, dtype=out_dtype)
+    out_val = torch.empty((B, n_dst, pval.shape[-1]), device=dev, dtype=out_dtype)
+    with torch.cuda.device(dev):
+        check(
+            _LIBRARY.jk_transition_pairwise_dense_forward(
+                src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1],
+                _proj_dtype(src_proj, sv.dtype == torch.float32),
+                pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
+                pval.data_ptr(), _ptr(pval_lo), pval.shape[-1],
+                0.0, _ptr(bias_t), _ROUTE_CODE[route_compress_name], stats.data_ptr(),
+                out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state), _stream(dev)),
+            "jk_transition_pairwise_dense_forward",
+        )
+    if pad:
+        out_val = out_val[..., :out_dim]
+    return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
+            out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))
+
+
 def masked_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, *, window: int = -1,
                      compress: int = _lib.JK_SOFTSIGN, bias: Optional[Tensor] = None, score_bias: float = 0.0,
                      out_dtype: Optional[torch.dtype] = None, split3: bool = False,
@@ -435,22 +506,7 @@ def _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, e
         pstate = (pstate.float() * ss).to(pstate.dtype)
         pval = (pval.float() * ss[..., None]).to(pval.dtype)
     f32 = tv.dtype == torch.float32
-    pad = (-out_dim) % 64  # the value GEMM works on 64-column boxes
-    if pad:
-        pval = torch.nn.functional.pad(pval, (0, pad))
-    pval_lo = None
-    if f32:
-        # f32 values: bf16 hi + lo planes, both multiplied by the hi + lo edge planes
-        pval = pval.float().contiguous()
-        hi = torch.empty(pval.shape, device=pval.device, dtype=torch.bfloat16)
-        pval_lo = torch.empty_like(hi)
-        with torch.cuda.device(pval.device):
-            check(_LIBRARY.jk_split2_bf16(pval.data_ptr(), pval.numel(), hi.data_ptr(), pval_lo.data_ptr(),
-                                          _stream(pval.device)), "jk_split2_bf16")
-        pval = hi
-    elif pval.dtype != tv.dtype:
-        pval = pval.to(tv.dtype)
-    pval = pval.contiguous()
+    pval, pval_lo, pad = _value_planes(pval, tv.dtype)
     row_proj = lowrank_project(tv, out_weight)
     col_proj = lowrank_project(sv, in_weight, core=weight)
     same = projected_state.dtype == projected_val.dtype

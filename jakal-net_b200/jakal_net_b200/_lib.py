@@ -53,6 +53,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _i64, _f32, _p, _i32,                  # window, score_bias, bias_dev, compress
          _p, _p, _i32, _p],                     # out_state, out_val, out_dtype, stream
     ),
+    "jk_transition_pairwise_dense_forward": (
+        _i32,
+        [_p, _p, _i64, _i64, _i64, _i64, _i32,  # src_proj, dst_proj, B, n_src, n_dst, rp, proj_dtype
+         _p, _p, _i32, _p, _p, _i64,            # src_state, sender, state_dtype, src_val, src_val_lo, dim
+         _f32, _p, _i32, _p,                    # score_bias, bias_dev, compress, stats
+         _p, _p, _i32, _p],                     # out_state, out_val, out_dtype, stream
+    ),
     "jk_split3_bf16": (_i32, [_p, _i64, _i64, _p, _p]),
     "jk_split2_bf16": (_i32, [_p, _i64, _p, _p, _p]),
     "jk_transition_query_topk_forward": (

@@ -99,3 +99,16 @@ def test_sparse_transition_matches_reference(dev, compress):
                                          float(g["temperature"]), sender, g["src_val"], g["dst_val"], g["src_state"],
                                          g["src_val"], int(g["k"]), 128, 128, route_compress_name=compress)
     _check(st, vv, g)
+
+
+@pytest.mark.parametrize("compress", ["softmax", "signed_abs_softmax", "signed_entmax15"])
+def test_dense_transition_matches_reference(dev, compress):
+    import jakal_net_b200 as jk
+
+    g = _load(f"transition_dense_{compress}", dev)
+    sender = torch.nn.functional.softplus(g["src_state"])
+    st, vv = jk.transition_pairwise_dense("low_rank_bilinear_route", g["w_s"], None, g["w_t"], None, g["core"],
+                                          torch.tensor(float(g["bias"]), device=dev), None, None, None, None,
+                                          compress, float(g["temperature"]), sender, g["src_val"], g["dst_val"],
+                                          g["src_state"], g["src_val"], 128, 128)
+    _check(st, vv, g)

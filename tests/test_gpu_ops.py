@@ -183,3 +183,29 @@ def test_query_dense_propagation_op(dev):
                                                   compress_name="signed_abs_softmax")
     parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
     parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")
+
+
+@pytest.mark.parametrize("compress", ["softmax", "signed_abs_softmax", "signed_entmax15"])
+@pytest.mark.parametrize("shape", [(2, 700, 300, 128), (1, 130, 1000, 64)])
+def test_transition_pairwise_dense_op(dev, compress, shape):
+    import jakal_net_b200 as jk
+
+    B, S, Dn, D = shape
+    g = np.random.default_rng(S + Dn)
+    R = 64
+    src = _t(g.standard_normal((B, S, D)), dev)
+    dst = _t(g.standard_normal((B, Dn, D)), dev)
+    sstate = _t(g.standard_normal((B, S)), dev)
+    w_s = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    w_t = _t(g.standard_normal((R, D)) / np.sqrt(D), dev)
+    core = _t(np.ones(R), dev)
+    sender = torch.nn.functional.softplus(sstate.float()).to(torch.bfloat16)
+    st, vv = jk.transition_pairwise_dense("low_rank_bilinear_route", w_s, None, w_t, None, core,
+                                          torch.tensor(0.1, device=dev), None, None, None, None, compress, 0.8,
+                                          sender, src, dst, sstate, src, 128, 128)
+    sp = _np(jk.lowrank_project(src, w_s, core=core, temperature=0.8))
+    dp = _np(jk.lowrank_project(dst, w_t))
+    o_st, o_val = oracle.transition_dense(sp, dp, _np(sstate), _np(src), _np(sender), bias=0.1 / 0.8,
+                                          compress_name=compress)
+    parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
+    parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")
