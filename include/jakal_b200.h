@@ -44,6 +44,25 @@ extern "C" {
 #define JK_SIGNED_ENTMAX15 2       /* sign(s) * entmax15(|s|)             kernels.py:155-236  */
 #define JK_SOFTMAX 3               /* softmax(s)  (routes)                transition.py:187-194 */
 
+/* ---- multi-head scorers (MultiHeadPairwise / MultiHeadRoute, modules.py:259-302) ------ */
+#define JK_HEADS_MAX 0              /* max_h s_h                       modules.py:291-298   */
+#define JK_HEADS_SMOOTHMAX 1        /* logsumexp_h s_h - log H         modules.py:276-280   */
+#define JK_HEADS_SIGNED_SMOOTHMAX 2 /* sum_h s_h * softmax_h(|s_h|)    modules.py:281-284   */
+
+/* Multi-head scorer for the *_mh entry points. The projection rows hold `heads` blocks of
+ * 16 * kph columns (head h at columns [16 kph h, 16 kph (h + 1)), zero padded up to rp);
+ * the score of head h is the f32 dot of its blocks plus head_bias[h], and the heads are
+ * combined per pair by `combine` before selection / compression. Replaces the
+ * multihead_{max,smoothmax,signed_smoothmax}_low_rank_bilinear pairwise kinds and the
+ * multihead_max_low_rank_bilinear_route (kernel_common.py:151-178;
+ * jakal_net_native.cpp:724-776; jakal_net_native_cuda.cu:881-1027, 1186-1350). */
+typedef struct jk_heads {
+  int heads;              /* 2..4 (top-k kernels), 2 (window / dense kernels)        */
+  int kph;                /* 16-column K steps per head; heads * 16 * kph <= rp       */
+  int combine;            /* JK_HEADS_*                                              */
+  const float* head_bias; /* device, `heads` floats added before combining, or NULL  */
+} jk_heads_t;
+
 typedef struct CUstream_st* jk_stream_t; /* == cudaStream_t; NULL = legacy default stream */
 
 /* Human-readable text for a status code. */
@@ -154,6 +173,46 @@ int jk_transition_pairwise_dense_forward(const void* src_proj, const void* dst_p
                                          float score_bias, const float* bias_dev, int compress,
                                          float* stats, void* out_state, void* out_val, int out_dtype,
                                          jk_stream_t stream);
+
+/* Multi-head variants: the entry point of the same name without _mh, with the scorer
+ * `heads` (jk_heads_t above; 16-bit projections only, not JK_BF16X3). */
+int jk_propagation_topk_forward_mh(const void* row_proj, const void* col_proj, int64_t batch,
+                                   int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
+                                   const void* col_state, const void* col_sender, int state_dtype,
+                                   const void* col_val, int64_t dim, int val_dtype, int64_t k,
+                                   int64_t window, float score_bias, const float* bias_dev,
+                                   int compress, void* out_state, void* out_val, int out_dtype,
+                                   float* out_scores, int64_t* out_index, const jk_heads_t* heads,
+                                   jk_stream_t stream);
+int jk_transition_query_topk_forward_mh(const void* query_proj, const void* source_proj, int64_t batch,
+                                        int64_t n_query, int64_t n_source, int64_t rp, int proj_dtype,
+                                        const void* source_state, const void* source_sender,
+                                        int state_dtype, const void* source_val, int64_t dim,
+                                        int val_dtype, int64_t k, float score_bias,
+                                        const float* bias_dev, int compress, void* out_state,
+                                        void* out_val, int out_dtype, float* out_scores,
+                                        int64_t* out_index, const jk_heads_t* heads, jk_stream_t stream);
+int jk_transition_pairwise_topk_forward_mh(const void* src_proj, const void* dst_proj, int64_t batch,
+                                           int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                           const void* src_state, const void* src_sender, int state_dtype,
+                                           const void* src_val, int64_t dim, int val_dtype, int64_t k,
+                                           float score_bias, const float* bias_dev, int compress,
+                                           float* accum, void* out_state, void* out_val, int out_dtype,
+                                           const jk_heads_t* heads, jk_stream_t stream);
+int jk_propagation_window_forward_mh(const void* row_proj, const void* col_proj, int64_t batch,
+                                     int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
+                                     const void* col_state, int state_dtype, const void* col_val,
+                                     const void* col_val_lo, int64_t dim, int64_t window,
+                                     float score_bias, const float* bias_dev, int compress,
+                                     void* out_state, void* out_val, int out_dtype,
+                                     const jk_heads_t* heads, jk_stream_t stream);
+int jk_transition_pairwise_dense_forward_mh(const void* src_proj, const void* dst_proj, int64_t batch,
+                                            int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                            const void* src_state, const void* sender, int state_dtype,
+                                            const void* src_val, const void* src_val_lo, int64_t dim,
+                                            float score_bias, const float* bias_dev, int compress,
+                                            float* stats, void* out_state, void* out_val, int out_dtype,
+                                            const jk_heads_t* heads, jk_stream_t stream);
 
 /* f32 -> three bf16 planes [h|m|l|0] of 32 columns (rank <= 32), out [rows, 128] bf16, for
  * JK_BF16X3 projections. Replaces nothing: the reference computes these dots in f32. */

@@ -29,4 +29,25 @@ int make_tmap_3d_16bit(CUtensorMap* map, const void* base, uint64_t d0, uint64_t
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Scorer heads of a call: 1 (single low-rank scorer) when h is null, else h checked
+// against the projection width rp and the kernel's head limit.
+struct Heads {
+  int heads = 1, kph = 0, combine = 0;
+  const float* bias = nullptr;
+};
+
+inline int read_heads(const jk_heads_t* h, int64_t rp, int proj_dtype, int max_heads, Heads& out) {
+  out = Heads{};
+  if (h == nullptr) return JK_OK;
+  if (proj_dtype == JK_BF16X3) return JK_ERR_UNSUPPORTED_KIND;
+  if (h->combine < JK_HEADS_MAX || h->combine > JK_HEADS_SIGNED_SMOOTHMAX) return JK_ERR_UNSUPPORTED_KIND;
+  if (h->heads < 2 || h->heads > max_heads || h->kph < 1 || int64_t(h->heads) * 16 * h->kph > rp)
+    return JK_ERR_BAD_SHAPE;
+  out.heads = h->heads;
+  out.kph = h->kph;
+  out.combine = h->combine;
+  out.bias = h->head_bias;
+  return JK_OK;
+}
+
 }  // namespace jk

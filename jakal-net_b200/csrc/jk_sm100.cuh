@@ -170,6 +170,16 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -237,6 +247,68 @@ __device__ __forceinline__ void score_mmas(uint32_t tmem_d, uint32_t a_addr, uin
     for (int kk = 0; kk < 4 * KATOMS; ++kk) {
       const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
       mma_f16_ss(tmem_d, sdesc_kmajor_sw128(a_addr + off), sdesc_kmajor_sw128(b_addr + off), idesc, kk > 0 ? 1u : 0u);
+    }
+  }
+}
+
+// Multi-head scores: head h owns the kph K steps [h * kph, (h + 1) * kph) of the projection
+// rows and accumulates into its own TMEM plane tmem_d + h * plane_cols.
+__device__ __forceinline__ void head_score_mmas(uint32_t tmem_d, uint32_t plane_cols, uint32_t a_addr,
+                                                uint32_t b_addr, uint32_t idesc, int heads, int kph) {
+  constexpr uint32_t kAtom = 128 * 128;
+  for (int h = 0; h < heads; ++h) {
+    for (int kk = 0; kk < kph; ++kk) {
+      const int g = h * kph + kk;
+      const uint32_t off = (g >> 2) * kAtom + (g & 3) * 32;
+      mma_f16_ss(tmem_d + h * plane_cols, sdesc_kmajor_sw128(a_addr + off), sdesc_kmajor_sw128(b_addr + off), idesc,
+                 kk > 0 ? 1u : 0u);
+    }
+  }
+}
+
+// Head combination of MultiHeadPairwise (modules.py:274-299) for 16 score columns of this
+// thread's TMEM lane: every head plane (at taddr + h * plane_cols) plus its bias, then
+//   JK_HEADS_MAX: max_h s_h;  JK_HEADS_SMOOTHMAX: logsumexp_h s_h - log H;
+//   JK_HEADS_SIGNED_SMOOTHMAX: sum_h s_h * softmax_h(|s_h|)   (online over the heads).
+template <int H>
+__device__ __forceinline__ void combine_heads16(uint32_t taddr, uint32_t plane_cols, const float* head_bias,
+                                                int combine, float (&out)[16]) {
+  uint32_t t[H][16];
+#pragma unroll
+  for (int h = 0; h < H; ++h) tmem_ld_32x32b_x16(taddr + h * plane_cols, t[h]);
+  tmem_ld_wait();
+  float bh[H];
+#pragma unroll
+  for (int h = 0; h < H; ++h) bh[h] = head_bias ? __ldg(head_bias + h) : 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float s0 = __uint_as_float(t[0][i]) + bh[0];
+    if (combine == JK_HEADS_MAX) {
+      float m = s0;
+#pragma unroll
+      for (int h = 1; h < H; ++h) m = fmaxf(m, __uint_as_float(t[h][i]) + bh[h]);
+      out[i] = m;
+    } else if (combine == JK_HEADS_SMOOTHMAX) {
+      float m = s0;
+#pragma unroll
+      for (int h = 1; h < H; ++h) m = fmaxf(m, __uint_as_float(t[h][i]) + bh[h]);
+      float z = 0.f;
+#pragma unroll
+      for (int h = 0; h < H; ++h) z += expf(__uint_as_float(t[h][i]) + bh[h] - m);
+      out[i] = m + logf(z) - logf(static_cast<float>(H));
+    } else {
+      float m = fabsf(s0);
+#pragma unroll
+      for (int h = 1; h < H; ++h) m = fmaxf(m, fabsf(__uint_as_float(t[h][i]) + bh[h]));
+      float num = 0.f, den = 0.f;
+#pragma unroll
+      for (int h = 0; h < H; ++h) {
+        const float s = __uint_as_float(t[h][i]) + bh[h];
+        const float e = expf(fabsf(s) - m);
+        num = fmaf(s, e, num);
+        den += e;
+      }
+      out[i] = num / den;
     }
   }
 }

@@ -97,6 +97,9 @@ constexpr int kOCols = 384;   // TMEM columns of the aggregate's accumulator O (
 // written over the row's candidate values once the edges are final.
 __device__ __forceinline__ int gtab_off(int row) { return (row * kStride + 3) & ~3; }
 
+// TMEM score buffers: two of 128 columns per head while they fit the 512 columns, else one.
+__host__ __device__ constexpr int score_buffers(int heads) { return heads <= 2 ? 2 : 1; }
+
 struct Params {
   int64_t n_rows, n_cols, rp, dim;
   int k;
@@ -107,6 +110,10 @@ struct Params {
   int state_dtype, val_dtype, out_dtype;
   int slab_ok;  // tm_val is valid (windowed gather of 16-bit values, dim % 64 == 0)
   int split3;   // projections are the three-plane bf16 split of f32 values
+  // multi-head scorer (heads > 1): head h owns K steps [h * kph, (h + 1) * kph) and its own
+  // TMEM plane; the planes are combined (JK_HEADS_*) with head_bias as they are read
+  int heads, kph, combine;
+  const float* head_bias;
   const void* col_state;
   const void* col_val;
   const void* col_sender;
@@ -780,16 +787,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(bar_a, 0);
       int total = pre_passes * ntiles;
       const int decide_at = total - 1;
+      const int nb = score_buffers(p.heads);
       for (int g = 0; g < total && ok; ++g) {
         const int st = g % STAGES;
-        const int buf = g & 1;
+        const int buf = g % nb;
         if (!mbar_wait(&full[st], (g / STAGES) & 1)) { ok = false; break; }
-        if (g >= 2 && !mbar_wait(&tempty[buf], ((g >> 1) - 1) & 1)) { ok = false; break; }
+        if (g >= nb && !mbar_wait(&tempty[buf], ((g / nb) - 1) & 1)) { ok = false; break; }
         if (*abort_flag) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_addr = smem_u32(a_tile);
         const uint32_t b_addr = smem_u32(b_ring + st * L::kBBytes);
-        score_mmas<KATOMS>(tmem + buf * kCols, a_addr, b_addr, idesc, p.split3 != 0);
+        if (p.heads > 1)
+          head_score_mmas(tmem + buf * p.heads * kCols, kCols, a_addr, b_addr, idesc, p.heads, p.kph);
+        else
+          score_mmas<KATOMS>(tmem + buf * kCols, a_addr, b_addr, idesc, p.split3 != 0);
         mma_commit(&empty[st]);
         mma_commit(&tfull[buf]);
         if (g == decide_at) {
@@ -881,13 +892,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
 
     // Loads this thread's 64 scores of iteration g into v; false on timeout / abort.
+    const int nbuf = score_buffers(p.heads);
     auto load_tile = [&](uint32_t (&v)[2][32]) -> bool {
-      const int buf = g & 1;
-      if (!JK_PHASE_TIME(18, mbar_wait(&tfull[buf], (g >> 1) & 1)) || *abort_flag) return false;
+      const int buf = g % nbuf;
+      if (!JK_PHASE_TIME(18, mbar_wait(&tfull[buf], (g / nbuf) & 1)) || *abort_flag) return false;
       tc_fence_after();
-      tmem_ld_32x32b_x32(tmem + tbase + buf * kCols, v[0]);
-      tmem_ld_32x32b_x32(tmem + tbase + buf * kCols + 32, v[1]);
-      tmem_ld_wait();
+      if (p.heads > 1) {
+        const uint32_t base = tmem + tbase + buf * p.heads * kCols;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float f[16];
+          if (p.heads == 2) combine_heads16<2>(base + c * 16, kCols, p.head_bias, p.combine, f);
+          else if (p.heads == 3) combine_heads16<3>(base + c * 16, kCols, p.head_bias, p.combine, f);
+          else combine_heads16<4>(base + c * 16, kCols, p.head_bias, p.combine, f);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[c >> 1][(c & 1) * 16 + i] = __float_as_uint(f[i]);
+        }
+      } else {
+        tmem_ld_32x32b_x32(tmem + tbase + buf * kCols, v[0]);
+        tmem_ld_32x32b_x32(tmem + tbase + buf * kCols + 32, v[1]);
+        tmem_ld_wait();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -1342,22 +1367,26 @@ int validate_common(const void* row_proj, const void* col_proj, int64_t batch, i
 }  // namespace topk
 }  // namespace jk
 
-extern "C" int jk_propagation_topk_forward(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows,
-                                           int64_t n_cols, int64_t rp, int proj_dtype, const void* col_state,
-                                           const void* col_sender, int state_dtype, const void* col_val, int64_t dim,
-                                           int val_dtype, int64_t k, int64_t window, float score_bias,
-                                           const float* bias_dev, int compress, void* out_state, void* out_val,
-                                           int out_dtype, float* out_scores, int64_t* out_index, jk_stream_t stream) {
-  using namespace jk;
-  int st = topk::validate_common(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype,
-                                 col_val, dim, val_dtype, k, compress, out_dtype);
+namespace jk {
+namespace topk {
+
+int gather_forward(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols,
+                   int64_t rp, int proj_dtype, const void* col_state, const void* col_sender, int state_dtype,
+                   const void* col_val, int64_t dim, int val_dtype, int64_t k, int64_t window, float score_bias,
+                   const float* bias_dev, int compress, void* out_state, void* out_val, int out_dtype,
+                   float* out_scores, int64_t* out_index, const jk_heads_t* heads, jk_stream_t stream) {
+  int st = validate_common(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype, col_val,
+                           dim, val_dtype, k, compress, out_dtype);
   if (st != JK_OK) return st;
   if (out_state == nullptr || out_val == nullptr) return JK_ERR_BAD_ARG;
   if (dim % 8 == 0 && !aligned16(out_val)) return JK_ERR_ALIGNMENT;
   if (window < -1) return JK_ERR_BAD_ARG;
+  Heads hd;
+  st = read_heads(heads, rp, proj_dtype, 4, hd);
+  if (st != JK_OK) return st;
   st = check_device();
   if (st != JK_OK) return st;
-  topk::Params p{};
+  Params p{};
   p.n_rows = n_rows;
   p.n_cols = n_cols;
   p.rp = rp;
@@ -1377,35 +1406,27 @@ extern "C" int jk_propagation_topk_forward(const void* row_proj, const void* col
   p.out_val = out_val;
   p.out_scores = out_scores;
   p.out_index = out_index;
-  return topk::launch<topk::kGather>(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, p,
-                                     reinterpret_cast<cudaStream_t>(stream));
+  p.heads = hd.heads;
+  p.kph = hd.kph;
+  p.combine = hd.combine;
+  p.head_bias = hd.bias;
+  return launch<kGather>(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, p,
+                         reinterpret_cast<cudaStream_t>(stream));
 }
 
-extern "C" int jk_transition_query_topk_forward(const void* query_proj, const void* source_proj, int64_t batch,
-                                                int64_t n_query, int64_t n_source, int64_t rp, int proj_dtype,
-                                                const void* source_state, const void* source_sender, int state_dtype,
-                                                const void* source_val, int64_t dim, int val_dtype, int64_t k,
-                                                float score_bias, const float* bias_dev, int compress,
-                                                void* out_state, void* out_val, int out_dtype, float* out_scores,
-                                                int64_t* out_index, jk_stream_t stream) {
-  return jk_propagation_topk_forward(query_proj, source_proj, batch, n_query, n_source, rp, proj_dtype, source_state,
-                                     source_sender, state_dtype, source_val, dim, val_dtype, k, -1, score_bias,
-                                     bias_dev, compress, out_state, out_val, out_dtype, out_scores, out_index, stream);
-}
-
-extern "C" int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_proj, int64_t batch,
-                                                   int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
-                                                   const void* src_state, const void* src_sender, int state_dtype,
-                                                   const void* src_val, int64_t dim, int val_dtype, int64_t k,
-                                                   float score_bias, const float* bias_dev, int compress,
-                                                   float* accum, void* out_state, void* out_val, int out_dtype,
-                                                   jk_stream_t stream) {
-  using namespace jk;
-  int st = topk::validate_common(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_state, state_dtype,
-                                 src_val, dim, val_dtype, k, compress, out_dtype);
+int scatter_forward(const void* src_proj, const void* dst_proj, int64_t batch, int64_t n_src, int64_t n_dst,
+                    int64_t rp, int proj_dtype, const void* src_state, const void* src_sender, int state_dtype,
+                    const void* src_val, int64_t dim, int val_dtype, int64_t k, float score_bias,
+                    const float* bias_dev, int compress, float* accum, void* out_state, void* out_val, int out_dtype,
+                    const jk_heads_t* heads, jk_stream_t stream) {
+  int st = validate_common(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_state, state_dtype, src_val,
+                           dim, val_dtype, k, compress, out_dtype);
   if (st != JK_OK) return st;
   if (accum == nullptr || out_state == nullptr || out_val == nullptr) return JK_ERR_BAD_ARG;
   if (!aligned16(accum)) return JK_ERR_ALIGNMENT;
+  Heads hd;
+  st = read_heads(heads, rp, proj_dtype, 4, hd);
+  if (st != JK_OK) return st;
   st = check_device();
   if (st != JK_OK) return st;
   auto cs = reinterpret_cast<cudaStream_t>(stream);
@@ -1415,7 +1436,7 @@ extern "C" int jk_transition_pairwise_topk_forward(const void* src_proj, const v
   float* acc_val = accum;
   float* acc_state = accum + n_val;
   if (cudaMemsetAsync(accum, 0, sizeof(float) * (n_state + n_val), cs) != cudaSuccess) return launch_status();
-  topk::Params p{};
+  Params p{};
   p.n_rows = n_src;
   p.n_cols = n_dst;
   p.rp = rp;
@@ -1433,14 +1454,96 @@ extern "C" int jk_transition_pairwise_topk_forward(const void* src_proj, const v
   p.col_sender = src_sender;
   p.acc_state = acc_state;
   p.acc_val = acc_val;
-  st = topk::launch<topk::kScatter>(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, p, cs);
+  p.heads = hd.heads;
+  p.kph = hd.kph;
+  p.combine = hd.combine;
+  p.head_bias = hd.bias;
+  st = launch<kScatter>(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, p, cs);
   if (st != JK_OK) return st;
   const int64_t work = n_val > n_state ? n_val : n_state;
   int blocks = static_cast<int>((work + 255) / 256);
   if (blocks > 4 * 148 * 8) blocks = 4 * 148 * 8;
   if (blocks < 1) blocks = 1;
-  topk::finalize_scatter<<<blocks, 256, 0, cs>>>(acc_state, acc_val, n_state, n_val, out_state, out_val, out_dtype);
+  finalize_scatter<<<blocks, 256, 0, cs>>>(acc_state, acc_val, n_state, n_val, out_state, out_val, out_dtype);
   return launch_status();
+}
+
+}  // namespace topk
+}  // namespace jk
+
+extern "C" int jk_propagation_topk_forward(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows,
+                                           int64_t n_cols, int64_t rp, int proj_dtype, const void* col_state,
+                                           const void* col_sender, int state_dtype, const void* col_val, int64_t dim,
+                                           int val_dtype, int64_t k, int64_t window, float score_bias,
+                                           const float* bias_dev, int compress, void* out_state, void* out_val,
+                                           int out_dtype, float* out_scores, int64_t* out_index, jk_stream_t stream) {
+  return jk::topk::gather_forward(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, col_sender,
+                                  state_dtype, col_val, dim, val_dtype, k, window, score_bias, bias_dev, compress,
+                                  out_state, out_val, out_dtype, out_scores, out_index, nullptr, stream);
+}
+
+extern "C" int jk_propagation_topk_forward_mh(const void* row_proj, const void* col_proj, int64_t batch,
+                                              int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
+                                              const void* col_state, const void* col_sender, int state_dtype,
+                                              const void* col_val, int64_t dim, int val_dtype, int64_t k,
+                                              int64_t window, float score_bias, const float* bias_dev, int compress,
+                                              void* out_state, void* out_val, int out_dtype, float* out_scores,
+                                              int64_t* out_index, const jk_heads_t* heads, jk_stream_t stream) {
+  if (heads == nullptr) return JK_ERR_BAD_ARG;
+  return jk::topk::gather_forward(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, col_sender,
+                                  state_dtype, col_val, dim, val_dtype, k, window, score_bias, bias_dev, compress,
+                                  out_state, out_val, out_dtype, out_scores, out_index, heads, stream);
+}
+
+extern "C" int jk_transition_query_topk_forward(const void* query_proj, const void* source_proj, int64_t batch,
+                                                int64_t n_query, int64_t n_source, int64_t rp, int proj_dtype,
+                                                const void* source_state, const void* source_sender, int state_dtype,
+                                                const void* source_val, int64_t dim, int val_dtype, int64_t k,
+                                                float score_bias, const float* bias_dev, int compress,
+                                                void* out_state, void* out_val, int out_dtype, float* out_scores,
+                                                int64_t* out_index, jk_stream_t stream) {
+  return jk::topk::gather_forward(query_proj, source_proj, batch, n_query, n_source, rp, proj_dtype, source_state,
+                                  source_sender, state_dtype, source_val, dim, val_dtype, k, -1, score_bias, bias_dev,
+                                  compress, out_state, out_val, out_dtype, out_scores, out_index, nullptr, stream);
+}
+
+extern "C" int jk_transition_query_topk_forward_mh(const void* query_proj, const void* source_proj, int64_t batch,
+                                                   int64_t n_query, int64_t n_source, int64_t rp, int proj_dtype,
+                                                   const void* source_state, const void* source_sender,
+                                                   int state_dtype, const void* source_val, int64_t dim,
+                                                   int val_dtype, int64_t k, float score_bias, const float* bias_dev,
+                                                   int compress, void* out_state, void* out_val, int out_dtype,
+                                                   float* out_scores, int64_t* out_index, const jk_heads_t* heads,
+                                                   jk_stream_t stream) {
+  if (heads == nullptr) return JK_ERR_BAD_ARG;
+  return jk::topk::gather_forward(query_proj, source_proj, batch, n_query, n_source, rp, proj_dtype, source_state,
+                                  source_sender, state_dtype, source_val, dim, val_dtype, k, -1, score_bias, bias_dev,
+                                  compress, out_state, out_val, out_dtype, out_scores, out_index, heads, stream);
+}
+
+extern "C" int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_proj, int64_t batch,
+                                                   int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                                   const void* src_state, const void* src_sender, int state_dtype,
+                                                   const void* src_val, int64_t dim, int val_dtype, int64_t k,
+                                                   float score_bias, const float* bias_dev, int compress,
+                                                   float* accum, void* out_state, void* out_val, int out_dtype,
+                                                   jk_stream_t stream) {
+  return jk::topk::scatter_forward(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_state, src_sender,
+                                   state_dtype, src_val, dim, val_dtype, k, score_bias, bias_dev, compress, accum,
+                                   out_state, out_val, out_dtype, nullptr, stream);
+}
+
+extern "C" int jk_transition_pairwise_topk_forward_mh(const void* src_proj, const void* dst_proj, int64_t batch,
+                                                      int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                                      const void* src_state, const void* src_sender, int state_dtype,
+                                                      const void* src_val, int64_t dim, int val_dtype, int64_t k,
+                                                      float score_bias, const float* bias_dev, int compress,
+                                                      float* accum, void* out_state, void* out_val, int out_dtype,
+                                                      const jk_heads_t* heads, jk_stream_t stream) {
+  if (heads == nullptr) return JK_ERR_BAD_ARG;
+  return jk::topk::scatter_forward(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_state, src_sender,
+                                   state_dtype, src_val, dim, val_dtype, k, score_bias, bias_dev, compress, accum,
+                                   out_state, out_val, out_dtype, heads, stream);
 }
 
 #ifdef JK_PHASE_PROFILE

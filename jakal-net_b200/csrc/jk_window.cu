@@ -66,6 +66,10 @@ struct Params {
   // normalised per COLUMN with the (max, scale / normaliser, tau) triples a statistics-mode
   // launch wrote for the columns (the transposed route normalisation of a transition).
   const float* col_stats;
+  // multi-head scorer (heads == 2): one 256-column score buffer holding both head planes,
+  // combined as they are read (JK_HEADS_*); heads == 1 keeps two 128-column buffers
+  int heads, kph, combine;
+  const float* head_bias;
 };
 
 // One edge from a score and the (max, scale / normaliser, tau) of its normalisation set.
@@ -234,16 +238,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return true;
       };
+      const int nb = p.heads > 1 ? 1 : 2;  // TMEM score buffers
       auto issue_s = [&]() -> bool {  // score MMA of global tile g
         const int st = g % PS;
-        const int buf = g & 1;
+        const int buf = g % nb;
         if (!mbar_wait(&full[st], (g / PS) & 1)) return false;
-        if (g >= 2 && !mbar_wait(&tempty[buf], ((g >> 1) - 1) & 1)) return false;
+        if (g >= nb && !mbar_wait(&tempty[buf], ((g / nb) - 1) & 1)) return false;
         if (*abort_flag) return false;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(a_tile);
         const uint32_t b_addr = smem_u32(ps_ring + st * KATOMS * L::kAtom);
-        score_mmas<KATOMS>(tmem + buf * kCols, a_addr, b_addr, idesc_s, p.split3 != 0);
+        if (p.heads > 1)
+          head_score_mmas(tmem, kCols, a_addr, b_addr, idesc_s, p.heads, p.kph);
+        else
+          score_mmas<KATOMS>(tmem + buf * kCols, a_addr, b_addr, idesc_s, p.split3 != 0);
         mma_commit(&empty[st]);
         mma_commit(&tfull[buf]);
         ++g;
@@ -335,14 +343,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     int g = 0;
     bool ok = true;
 
+    const int nbuf = p.heads > 1 ? 1 : 2;
     auto load_tile = [&](float (&x)[64]) -> bool {
-      const int buf = g & 1;
-      if (!mbar_wait(&tfull[buf], (g >> 1) & 1) || *abort_flag) return false;
+      const int buf = g % nbuf;
+      if (!mbar_wait(&tfull[buf], (g / nbuf) & 1) || *abort_flag) return false;
       tc_fence_after();
       uint32_t v[2][32];
-      tmem_ld_32x32b_x32(tmem + tbase + buf * kCols, v[0]);
-      tmem_ld_32x32b_x32(tmem + tbase + buf * kCols + 32, v[1]);
-      tmem_ld_wait();
+      if (p.heads > 1) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float f[16];
+          combine_heads16<2>(tmem + tbase + c * 16, kCols, p.head_bias, p.combine, f);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[c >> 1][(c & 1) * 16 + i] = __float_as_uint(f[i]);
+        }
+      } else {
+        tmem_ld_32x32b_x32(tmem + tbase + buf * kCols, v[0]);
+        tmem_ld_32x32b_x32(tmem + tbase + buf * kCols + 32, v[1]);
+        tmem_ld_wait();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -644,7 +663,7 @@ namespace win {
 int prepare(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols, int64_t rp,
             int proj_dtype, const void* col_state, int state_dtype, const void* col_val, const void* col_val_lo,
             int64_t dim, float score_bias, const float* bias_dev, int compress, void* out_state, void* out_val,
-            int out_dtype, Params& p) {
+            int out_dtype, const jk_heads_t* heads, Params& p) {
   if (row_proj == nullptr || col_proj == nullptr || col_state == nullptr || col_val == nullptr ||
       out_state == nullptr || out_val == nullptr)
     return JK_ERR_BAD_ARG;
@@ -658,7 +677,14 @@ int prepare(const void* row_proj, const void* col_proj, int64_t batch, int64_t n
   if (!aligned16(row_proj) || !aligned16(col_proj) || !aligned16(col_val) || !aligned16(out_val) ||
       (col_val_lo != nullptr && !aligned16(col_val_lo)))
     return JK_ERR_ALIGNMENT;
+  Heads hd;
+  const int hs = read_heads(heads, rp, proj_dtype, 2, hd);
+  if (hs != JK_OK) return hs;
   p = Params{};
+  p.heads = hd.heads;
+  p.kph = hd.kph;
+  p.combine = hd.combine;
+  p.head_bias = hd.bias;
   p.n_rows = n_rows;
   p.n_cols = n_cols;
   p.dim = dim;
@@ -688,23 +714,78 @@ int run(const void* row_proj, const void* col_proj, const void* col_val, const v
 }  // namespace win
 }  // namespace jk
 
+namespace jk {
+namespace win {
+
+int window_forward(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols,
+                   int64_t rp, int proj_dtype, const void* col_state, int state_dtype, const void* col_val,
+                   const void* col_val_lo, int64_t dim, int64_t window, float score_bias, const float* bias_dev,
+                   int compress, void* out_state, void* out_val, int out_dtype, const jk_heads_t* heads,
+                   jk_stream_t stream) {
+  if (compress != JK_SOFTSIGN && compress != JK_SIGNED_ABS_SOFTMAX && compress != JK_SIGNED_ENTMAX15)
+    return JK_ERR_UNSUPPORTED_KIND;
+  if (window < -1) return JK_ERR_BAD_ARG;
+  Params p;
+  const int st = prepare(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype, col_val,
+                         col_val_lo, dim, score_bias, bias_dev, compress, out_state, out_val, out_dtype, heads, p);
+  if (st != JK_OK) return st;
+  p.window = window;
+  return run(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, proj_dtype, p, stream);
+}
+
+int transition_dense_forward(const void* src_proj, const void* dst_proj, int64_t batch, int64_t n_src,
+                             int64_t n_dst, int64_t rp, int proj_dtype, const void* src_state, const void* sender,
+                             int state_dtype, const void* src_val, const void* src_val_lo, int64_t dim,
+                             float score_bias, const float* bias_dev, int compress, float* stats, void* out_state,
+                             void* out_val, int out_dtype, const jk_heads_t* heads, jk_stream_t stream) {
+  if (compress != JK_SOFTMAX && compress != JK_SIGNED_ABS_SOFTMAX && compress != JK_SIGNED_ENTMAX15)
+    return JK_ERR_UNSUPPORTED_KIND;
+  if (stats == nullptr) return JK_ERR_BAD_ARG;
+  // Aggregate launch: rows = destinations, columns = sources, per-column normalisation.
+  Params agg;
+  int st = prepare(dst_proj, src_proj, batch, n_dst, n_src, rp, proj_dtype, src_state, state_dtype, src_val,
+                   src_val_lo, dim, score_bias, bias_dev, compress, out_state, out_val, out_dtype, heads, agg);
+  if (st != JK_OK) return st;
+  // Statistics launch: rows = sources, columns = destinations; the sender strength scales
+  // each source's normaliser.
+  Params sp = agg;
+  sp.n_rows = n_src;
+  sp.n_cols = n_dst;
+  sp.stats_out = stats;
+  sp.row_scale = sender;
+  sp.out_state = nullptr;
+  sp.out_val = nullptr;
+  st = run(src_proj, dst_proj, nullptr, nullptr, batch, n_src, n_dst, rp, proj_dtype, sp, stream);
+  if (st != JK_OK) return st;
+  agg.col_stats = stats;
+  return run(dst_proj, src_proj, src_val, src_val_lo, batch, n_dst, n_src, rp, proj_dtype, agg, stream);
+}
+
+}  // namespace win
+}  // namespace jk
+
 extern "C" int jk_propagation_window_forward(const void* row_proj, const void* col_proj, int64_t batch,
                                              int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
                                              const void* col_state, int state_dtype, const void* col_val,
                                              const void* col_val_lo, int64_t dim, int64_t window, float score_bias,
                                              const float* bias_dev, int compress, void* out_state, void* out_val,
                                              int out_dtype, jk_stream_t stream) {
-  using namespace jk;
-  if (compress != JK_SOFTSIGN && compress != JK_SIGNED_ABS_SOFTMAX && compress != JK_SIGNED_ENTMAX15)
-    return JK_ERR_UNSUPPORTED_KIND;
-  if (window < -1) return JK_ERR_BAD_ARG;
-  win::Params p;
-  const int st = win::prepare(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype,
-                              col_val, col_val_lo, dim, score_bias, bias_dev, compress, out_state, out_val, out_dtype,
-                              p);
-  if (st != JK_OK) return st;
-  p.window = window;
-  return win::run(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, proj_dtype, p, stream);
+  return jk::win::window_forward(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype,
+                                 col_val, col_val_lo, dim, window, score_bias, bias_dev, compress, out_state, out_val,
+                                 out_dtype, nullptr, stream);
+}
+
+extern "C" int jk_propagation_window_forward_mh(const void* row_proj, const void* col_proj, int64_t batch,
+                                                int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
+                                                const void* col_state, int state_dtype, const void* col_val,
+                                                const void* col_val_lo, int64_t dim, int64_t window,
+                                                float score_bias, const float* bias_dev, int compress,
+                                                void* out_state, void* out_val, int out_dtype,
+                                                const jk_heads_t* heads, jk_stream_t stream) {
+  if (heads == nullptr) return JK_ERR_BAD_ARG;
+  return jk::win::window_forward(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype,
+                                 col_val, col_val_lo, dim, window, score_bias, bias_dev, compress, out_state, out_val,
+                                 out_dtype, heads, stream);
 }
 
 extern "C" int jk_transition_pairwise_dense_forward(const void* src_proj, const void* dst_proj, int64_t batch,
@@ -714,26 +795,20 @@ extern "C" int jk_transition_pairwise_dense_forward(const void* src_proj, const 
                                                     float score_bias, const float* bias_dev, int compress,
                                                     float* stats, void* out_state, void* out_val, int out_dtype,
                                                     jk_stream_t stream) {
-  using namespace jk;
-  if (compress != JK_SOFTMAX && compress != JK_SIGNED_ABS_SOFTMAX && compress != JK_SIGNED_ENTMAX15)
-    return JK_ERR_UNSUPPORTED_KIND;
-  if (stats == nullptr) return JK_ERR_BAD_ARG;
-  // Aggregate launch: rows = destinations, columns = sources, per-column normalisation.
-  win::Params agg;
-  int st = win::prepare(dst_proj, src_proj, batch, n_dst, n_src, rp, proj_dtype, src_state, state_dtype, src_val,
-                        src_val_lo, dim, score_bias, bias_dev, compress, out_state, out_val, out_dtype, agg);
-  if (st != JK_OK) return st;
-  // Statistics launch: rows = sources, columns = destinations; the sender strength scales
-  // each source's normaliser.
-  win::Params sp = agg;
-  sp.n_rows = n_src;
-  sp.n_cols = n_dst;
-  sp.stats_out = stats;
-  sp.row_scale = sender;
-  sp.out_state = nullptr;
-  sp.out_val = nullptr;
-  st = win::run(src_proj, dst_proj, nullptr, nullptr, batch, n_src, n_dst, rp, proj_dtype, sp, stream);
-  if (st != JK_OK) return st;
-  agg.col_stats = stats;
-  return win::run(dst_proj, src_proj, src_val, src_val_lo, batch, n_dst, n_src, rp, proj_dtype, agg, stream);
+  return jk::win::transition_dense_forward(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_state, sender,
+                                           state_dtype, src_val, src_val_lo, dim, score_bias, bias_dev, compress,
+                                           stats, out_state, out_val, out_dtype, nullptr, stream);
+}
+
+extern "C" int jk_transition_pairwise_dense_forward_mh(const void* src_proj, const void* dst_proj, int64_t batch,
+                                                       int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                                       const void* src_state, const void* sender, int state_dtype,
+                                                       const void* src_val, const void* src_val_lo, int64_t dim,
+                                                       float score_bias, const float* bias_dev, int compress,
+                                                       float* stats, void* out_state, void* out_val, int out_dtype,
+                                                       const jk_heads_t* heads, jk_stream_t stream) {
+  if (heads == nullptr) return JK_ERR_BAD_ARG;
+  return jk::win::transition_dense_forward(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_state, sender,
+                                           state_dtype, src_val, src_val_lo, dim, score_bias, bias_dev, compress,
+                                           stats, out_state, out_val, out_dtype, heads, stream);
 }

@@ -13,6 +13,7 @@ back to another implementation.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional
 
 import torch
@@ -52,6 +53,13 @@ _ROUTE_CODE = {
     "signed_entmax15": _lib.JK_SIGNED_ENTMAX15,
 }
 _MAX_K = 64
+# MultiHeadPairwise aggregate -> jk_heads_t.combine (kernel_common.py:151-178 spec kinds
+# multihead_{max,smoothmax,signed_smoothmax}_low_rank_bilinear)
+_HEAD_COMBINE = {
+    "max": _lib.JK_HEADS_MAX,
+    "smoothmax": _lib.JK_HEADS_SMOOTHMAX,
+    "signed_smoothmax": _lib.JK_HEADS_SIGNED_SMOOTHMAX,
+}
 
 _SUPPORTED_OPS = (
     "propagation_dense",
@@ -175,11 +183,84 @@ def _bias_tensor(bias: Optional[Tensor], device: torch.device, scale: float = 1.
     return b / scale if scale != 1.0 else b.contiguous()
 
 
+class Heads:
+    """Multi-head scorer of one call (jk_heads_t): the projection rows hold `heads` blocks of
+    16 * kph columns; per-head scores plus `bias` [heads] are combined by `combine`."""
+
+    def __init__(self, heads: int, kph: int, combine: int, bias: Optional[Tensor] = None):
+        self.bias = bias  # keeps the device tensor alive for the call
+        self.struct = _lib.JkHeads(int(heads), int(kph), int(combine), _ptr(bias))
+
+    def ref(self):
+        return ctypes.byref(self.struct)
+
+
+def _multihead_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None, temperature: float = 1.0):
+    """Per-head projections x @ weight[h]^T [* core[h]] [/ T] packed head-major into one
+    projection row: head h at columns [16 kph h, 16 kph h + R), zeros elsewhere. weight
+    [H, R, D], core [H, R]. Returns (proj [..., rp], kph)."""
+    if x.dtype == torch.float32:
+        raise RuntimeError("b200_sm100a multi-head scorers take bf16 / f16 inputs.")
+    H, R, D = weight.shape
+    rb = -(-R // 16) * 16
+    if H * rb > 128:
+        raise RuntimeError(f"b200_sm100a multi-head scorers need heads * roundup16(rank) <= 128 (got {H} x {R}).")
+    w = weight.detach().new_zeros((H, rb, D))
+    w[:, :R] = weight.detach()
+    c = None
+    if core is not None:
+        c = core.detach().new_zeros((H, rb))
+        c[:, :R] = core.detach().reshape(H, R)
+        c = c.reshape(-1)
+    return lowrank_project(x, w.reshape(H * rb, D), core=c, temperature=temperature), rb // 16
+
+
+def _head_bias(bias: Optional[Tensor], heads: int, device: torch.device, scale: float = 1.0) -> Optional[Tensor]:
+    if bias is None:
+        return None
+    b = bias.detach().reshape(-1).to(device=device, dtype=torch.float32)
+    if b.numel() == 0:
+        return None
+    if b.numel() == 1:
+        b = b.expand(heads)
+    if b.numel() != heads:
+        raise RuntimeError(f"multi-head bias must have {heads} entries (got {b.numel()}).")
+    return (b / scale).contiguous()
+
+
+def _pair_scorer(kind: str, weight: Tensor, bias, in_weight, in_bias, out_weight, out_bias, target_val: Tensor,
+                 source_val: Tensor):
+    """Projections of a pairwise spec (kernel_common.py:151-192): low_rank_bilinear or
+    multihead_{max,smoothmax,signed_smoothmax}_low_rank_bilinear. Returns (row_proj [target],
+    col_proj [source, * core], scalar bias tensor or None, Heads or None)."""
+    if in_weight is None or out_weight is None:
+        raise RuntimeError("Low-rank bilinear pairwise kernel is missing projection weights.")
+    if in_bias is not None or out_bias is not None:
+        raise RuntimeError("Low-rank bilinear projections take no bias.")
+    if kind == "low_rank_bilinear":
+        row_proj = lowrank_project(target_val, out_weight)                # target side
+        col_proj = lowrank_project(source_val, in_weight, core=weight)    # source side, * w_hat
+        return row_proj, col_proj, _bias_tensor(bias, target_val.device), None
+    prefix, base = "multihead_", "_low_rank_bilinear"
+    agg = kind[len(prefix):-len(base)] if kind.startswith(prefix) and kind.endswith(base) else None
+    if agg not in _HEAD_COMBINE:
+        raise RuntimeError(f"Unsupported pairwise kernel kind for b200_sm100a: {kind}")
+    if in_weight.dim() != 3 or out_weight.dim() != 3:
+        raise RuntimeError("multi-head projection weights must be [heads, rank, dim].")
+    H = in_weight.shape[0]
+    row_proj, kph = _multihead_project(target_val, out_weight)
+    col_proj, _ = _multihead_project(source_val, in_weight, core=weight)
+    heads = Heads(H, kph, _HEAD_COMBINE[agg], _head_bias(bias, H, target_val.device))
+    return row_proj, col_proj, None, heads
+
+
 def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, k: int, *,
                    window: int = -1, compress: int = _lib.JK_SOFTSIGN, col_sender: Optional[Tensor] = None,
                    bias: Optional[Tensor] = None, score_bias: float = 0.0,
-                   out_dtype: Optional[torch.dtype] = None, return_selection: bool = False, split3: bool = False):
-    """Raw fused top-k aggregate over already-projected inputs (jk_propagation_topk_forward).
+                   out_dtype: Optional[torch.dtype] = None, return_selection: bool = False, split3: bool = False,
+                   heads: Optional[Heads] = None):
+    """Raw fused top-k aggregate over already-projected inputs (jk_propagation_topk_forward,
+    or jk_propagation_topk_forward_mh with a multi-head scorer).
 
     row_proj [B, T, rp], col_proj [B, S, rp], col_state [B, S], col_val [B, S, D].
     Returns (state [B, T], val [B, T, D]) and, with return_selection, also the selected
@@ -197,33 +278,21 @@ def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_va
     scores = torch.empty((B, T, k), device=dev, dtype=torch.float32) if return_selection else None
     index = torch.empty((B, T, k), device=dev, dtype=torch.int64) if return_selection else None
     sender = None if col_sender is None else col_sender.to(col_state.dtype).contiguous()
+    args = (row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj, split3),
+            col_state.data_ptr(), _ptr(sender), _dtype_code("state", col_state),
+            col_val.data_ptr(), D, _dtype_code("val", col_val),
+            k, window, float(score_bias), _ptr(bias), compress,
+            out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state),
+            _ptr(scores), _ptr(index))
     with torch.cuda.device(dev):
-        check(
-            _LIBRARY.jk_propagation_topk_forward(
-                row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj, split3),
-                col_state.data_ptr(), _ptr(sender), _dtype_code("state", col_state),
-                col_val.data_ptr(), D, _dtype_code("val", col_val),
-                k, window, float(score_bias), _ptr(bias), compress,
-                out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state),
-                _ptr(scores), _ptr(index), _stream(dev)),
-            "jk_propagation_topk_forward",
-        )
+        if heads is None:
+            check(_LIBRARY.jk_propagation_topk_forward(*args, _stream(dev)), "jk_propagation_topk_forward")
+        else:
+            check(_LIBRARY.jk_propagation_topk_forward_mh(*args, heads.ref(), _stream(dev)),
+                  "jk_propagation_topk_forward_mh")
     if return_selection:
         return out_state, out_val, scores, index
     return out_state, out_val
-
-
-def _lowrank_pair_projections(kind: str, weight: Tensor, in_weight: Optional[Tensor], in_bias, out_weight, out_bias,
-                              layer_val: Tensor):
-    if kind != "low_rank_bilinear":
-        raise RuntimeError(f"Unsupported pairwise kernel kind for b200_sm100a: {kind}")
-    if in_weight is None or out_weight is None:
-        raise RuntimeError("Low-rank bilinear pairwise kernel is missing projection weights.")
-    if in_bias is not None or out_bias is not None:
-        raise RuntimeError("Low-rank bilinear projections take no bias.")
-    row_proj = lowrank_project(layer_val, out_weight)              # target side
-    col_proj = lowrank_project(layer_val, in_weight, core=weight)  # source side, * w_hat
-    return row_proj, col_proj
 
 
 def _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
@@ -245,13 +314,13 @@ def _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, o
     k = min(int(topk), n)
     if k > _MAX_K:
         raise RuntimeError(f"b200_sm100a top-k supports k <= {_MAX_K} (got {k}).")
-    row_proj, col_proj = _lowrank_pair_projections(kind, weight, in_weight, in_bias, out_weight, out_bias, val)
+    row_proj, col_proj, bias_t, heads = _pair_scorer(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
+                                                     val, val)
     same = projected_state.dtype == projected_val.dtype
     out_dtype = projected_val.dtype if same else torch.float32
-    bias_t = _bias_tensor(bias, val.device)
     state, out = topk_aggregate(row_proj, col_proj, pstate, pval, k, window=window,
                                 compress=_EDGE_CODE[edge_compress_name], bias=bias_t, out_dtype=out_dtype,
-                                split3=val.dtype == torch.float32)
+                                split3=val.dtype == torch.float32, heads=heads)
     state = state.to(projected_state.dtype).reshape(*batch_shape, n)
     out = out.to(projected_val.dtype).reshape(*batch_shape, n, out_dim)
     return state, out
@@ -282,7 +351,10 @@ def propagation_window_topk(kind, weight, bias, in_weight, in_bias, out_weight, 
 
 def _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
                        hidden_weight, hidden_bias, out_weight, out_bias, temperature, src_val, dst_val):
-    if route_kind != "low_rank_bilinear_route":
+    """Route projections (kernel_common.py:238-295): low_rank_bilinear_route or
+    multihead_max_low_rank_bilinear_route; logits = (ps . pd + b) / T. Returns
+    (src_proj / T, dst_proj, scalar bias / T or None, Heads or None)."""
+    if route_kind not in ("low_rank_bilinear_route", "multihead_max_low_rank_bilinear_route"):
         raise TypeError(f"Unsupported pairwise route kind for b200_sm100a: {route_kind}")
     if source_weight is None or target_weight is None:
         raise RuntimeError("Low-rank route kernel is missing projection weights.")
@@ -291,9 +363,16 @@ def _route_projections(route_kind, source_weight, source_bias, target_weight, ta
     temperature = float(temperature)
     if temperature <= 0.0:
         raise RuntimeError("route temperature must be positive.")
+    if route_kind == "multihead_max_low_rank_bilinear_route":
+        # max_h(l_h) / T == max_h(l_h / T): every head's source projection and bias take the 1 / T
+        H = source_weight.shape[0]
+        src_proj, kph = _multihead_project(src_val, source_weight, core=core_weight, temperature=temperature)
+        dst_proj, _ = _multihead_project(dst_val, target_weight)
+        heads = Heads(H, kph, _lib.JK_HEADS_MAX, _head_bias(bias, H, src_val.device, temperature))
+        return src_proj, dst_proj, None, heads
     src_proj = lowrank_project(src_val, source_weight, core=core_weight, temperature=temperature)
     dst_proj = lowrank_project(dst_val, target_weight)
-    return src_proj, dst_proj, _bias_tensor(bias, src_val.device, temperature)
+    return src_proj, dst_proj, _bias_tensor(bias, src_val.device, temperature), None
 
 
 def transition_query_topk(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
@@ -316,16 +395,17 @@ def transition_query_topk(route_kind, source_weight, source_bias, target_weight,
     k = min(int(topk), n_src)
     if k > _MAX_K:
         raise RuntimeError(f"b200_sm100a top-k supports k <= {_MAX_K} (got {k}).")
-    src_proj, q_proj, bias_t = _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias,
-                                                  core_weight, bias, hidden_weight, hidden_bias, out_weight,
-                                                  out_bias, temperature, sv, qv)
+    src_proj, q_proj, bias_t, heads = _route_projections(route_kind, source_weight, source_bias, target_weight,
+                                                         target_bias, core_weight, bias, hidden_weight, hidden_bias,
+                                                         out_weight, out_bias, temperature, sv, qv)
     pstate = _flatten_state(projected_state)
     sender = _flatten_state(sender_strength).to(pstate.dtype)
     pval = _flatten_val(projected_val)
     same = projected_state.dtype == projected_val.dtype
     out_dtype = projected_val.dtype if same else torch.float32
     state, out = topk_aggregate(q_proj, src_proj, pstate, pval, k, window=-1, compress=_lib.JK_SOFTMAX,
-                                col_sender=sender, bias=bias_t, out_dtype=out_dtype, split3=sv.dtype == torch.float32)
+                                col_sender=sender, bias=bias_t, out_dtype=out_dtype, split3=sv.dtype == torch.float32,
+                                heads=heads)
     return (state.to(projected_state.dtype).reshape(*batch_shape, n_query),
             out.to(projected_val.dtype).reshape(*batch_shape, n_query, out_dim))
 
@@ -353,9 +433,9 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
     k = min(int(topk), n_dst)
     if k > _MAX_K:
         raise RuntimeError(f"b200_sm100a top-k supports k <= {_MAX_K} (got {k}).")
-    src_proj, dst_proj, bias_t = _route_projections(route_kind, source_weight, source_bias, target_weight,
-                                                    target_bias, core_weight, bias, hidden_weight, hidden_bias,
-                                                    out_weight, out_bias, temperature, sv, dv)
+    src_proj, dst_proj, bias_t, heads = _route_projections(route_kind, source_weight, source_bias, target_weight,
+                                                           target_bias, core_weight, bias, hidden_weight,
+                                                           hidden_bias, out_weight, out_bias, temperature, sv, dv)
     pstate = _flatten_state(projected_state)
     sender = _flatten_state(sender_strength).to(pstate.dtype)
     pval = _flatten_val(projected_val)
@@ -366,17 +446,19 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
     accum = torch.empty(B * n_dst * (out_dim + 1) + 4, device=dev, dtype=torch.float32)
     out_state = torch.empty((B, n_dst), device=dev, dtype=out_dtype)
     out_val = torch.empty((B, n_dst, out_dim), device=dev, dtype=out_dtype)
+    args = (src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1],
+            _proj_dtype(src_proj, sv.dtype == torch.float32),
+            pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
+            pval.data_ptr(), out_dim, _dtype_code("val", pval),
+            k, 0.0, _ptr(bias_t), _ROUTE_CODE[route_compress_name], accum.data_ptr(),
+            out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
     with torch.cuda.device(dev):
-        check(
-            _LIBRARY.jk_transition_pairwise_topk_forward(
-                src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1],
-                _proj_dtype(src_proj, sv.dtype == torch.float32),
-                pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
-                pval.data_ptr(), out_dim, _dtype_code("val", pval),
-                k, 0.0, _ptr(bias_t), _ROUTE_CODE[route_compress_name], accum.data_ptr(),
-                out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state), _stream(dev)),
-            "jk_transition_pairwise_topk_forward",
-        )
+        if heads is None:
+            check(_LIBRARY.jk_transition_pairwise_topk_forward(*args, _stream(dev)),
+                  "jk_transition_pairwise_topk_forward")
+        else:
+            check(_LIBRARY.jk_transition_pairwise_topk_forward_mh(*args, heads.ref(), _stream(dev)),
+                  "jk_transition_pairwise_topk_forward_mh")
     return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
             out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))
 
@@ -421,9 +503,9 @@ def transition_pairwise_dense(route_kind, source_weight, source_bias, target_wei
     out_dim = projected_val.shape[-1]
     sv = _flatten_val(src_val)
     dv = _flatten_val(dst_val)
-    src_proj, dst_proj, bias_t = _route_projections(route_kind, source_weight, source_bias, target_weight,
-                                                    target_bias, core_weight, bias, hidden_weight, hidden_bias,
-                                                    out_weight, out_bias, temperature, sv, dv)
+    src_proj, dst_proj, bias_t, heads = _route_projections(route_kind, source_weight, source_bias, target_weight,
+                                                           target_bias, core_weight, bias, hidden_weight,
+                                                           hidden_bias, out_weight, out_bias, temperature, sv, dv)
     pstate = _flatten_state(projected_state)
     sender = _flatten_state(sender_strength).to(pstate.dtype).contiguous()
     pval, pval_lo, pad = _value_planes(_flatten_val(projected_val), sv.dtype)
@@ -434,17 +516,19 @@ def transition_pairwise_dense(route_kind, source_weight, source_bias, target_wei
     stats = torch.empty(B * n_src * 3, device=dev, dtype=torch.float32)
     out_state = torch.empty((B, n_dst), device=dev, dtype=out_dtype)
     out_val = torch.empty((B, n_dst, pval.shape[-1]), device=dev, dtype=out_dtype)
+    args = (src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1],
+            _proj_dtype(src_proj, sv.dtype == torch.float32),
+            pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
+            pval.data_ptr(), _ptr(pval_lo), pval.shape[-1],
+            0.0, _ptr(bias_t), _ROUTE_CODE[route_compress_name], stats.data_ptr(),
+            out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
     with torch.cuda.device(dev):
-        check(
-            _LIBRARY.jk_transition_pairwise_dense_forward(
-                src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1],
-                _proj_dtype(src_proj, sv.dtype == torch.float32),
-                pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
-                pval.data_ptr(), _ptr(pval_lo), pval.shape[-1],
-                0.0, _ptr(bias_t), _ROUTE_CODE[route_compress_name], stats.data_ptr(),
-                out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state), _stream(dev)),
-            "jk_transition_pairwise_dense_forward",
-        )
+        if heads is None:
+            check(_LIBRARY.jk_transition_pairwise_dense_forward(*args, _stream(dev)),
+                  "jk_transition_pairwise_dense_forward")
+        else:
+            check(_LIBRARY.jk_transition_pairwise_dense_forward_mh(*args, heads.ref(), _stream(dev)),
+                  "jk_transition_pairwise_dense_forward_mh")
     if pad:
         out_val = out_val[..., :out_dim]
     return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
@@ -454,7 +538,7 @@ def transition_pairwise_dense(route_kind, source_weight, source_bias, target_wei
 def masked_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, *, window: int = -1,
                      compress: int = _lib.JK_SOFTSIGN, bias: Optional[Tensor] = None, score_bias: float = 0.0,
                      out_dtype: Optional[torch.dtype] = None, split3: bool = False,
-                     col_val_lo: Optional[Tensor] = None):
+                     col_val_lo: Optional[Tensor] = None, heads: Optional[Heads] = None):
     """Raw fused window / dense aggregate over already-projected inputs
     (jk_propagation_window_forward). row_proj [B, T, rp], col_proj [B, S, rp], col_state [B, S],
     col_val [B, S, D] in the projections' dtype, D a multiple of 64. window -1 = dense."""
@@ -467,15 +551,16 @@ def masked_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_
     out_dtype = out_dtype or col_val.dtype
     out_state = torch.empty((B, T), device=dev, dtype=out_dtype)
     out_val = torch.empty((B, T, D), device=dev, dtype=out_dtype)
+    args = (row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj, split3),
+            col_state.data_ptr(), _dtype_code("state", col_state), col_val.data_ptr(), _ptr(col_val_lo), D,
+            int(window), float(score_bias), _ptr(bias), compress,
+            out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
     with torch.cuda.device(dev):
-        check(
-            _LIBRARY.jk_propagation_window_forward(
-                row_proj.data_ptr(), col_proj.data_ptr(), B, T, S, rp, _proj_dtype(row_proj, split3),
-                col_state.data_ptr(), _dtype_code("state", col_state), col_val.data_ptr(), _ptr(col_val_lo), D,
-                int(window), float(score_bias), _ptr(bias), compress,
-                out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state), _stream(dev)),
-            "jk_propagation_window_forward",
-        )
+        if heads is None:
+            check(_LIBRARY.jk_propagation_window_forward(*args, _stream(dev)), "jk_propagation_window_forward")
+        else:
+            check(_LIBRARY.jk_propagation_window_forward_mh(*args, heads.ref(), _stream(dev)),
+                  "jk_propagation_window_forward_mh")
     return out_state, out_val
 
 
@@ -488,10 +573,6 @@ def _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, e
     for name, t in (("target_val", target_val), ("source_val", source_val), ("projected_state", projected_state),
                     ("projected_val", projected_val)):
         _require_cuda(name, t)
-    if kind != "low_rank_bilinear":
-        raise RuntimeError(f"Unsupported pairwise kernel kind for b200_sm100a: {kind}")
-    if in_weight is None or out_weight is None:
-        raise RuntimeError("Low-rank bilinear pairwise kernel is missing projection weights.")
     batch_shape = target_val.shape[:-2]
     n_t = target_val.shape[-2]
     out_dim = projected_val.shape[-1]
@@ -507,13 +588,13 @@ def _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, e
         pval = (pval.float() * ss[..., None]).to(pval.dtype)
     f32 = tv.dtype == torch.float32
     pval, pval_lo, pad = _value_planes(pval, tv.dtype)
-    row_proj = lowrank_project(tv, out_weight)
-    col_proj = lowrank_project(sv, in_weight, core=weight)
+    row_proj, col_proj, bias_t, heads = _pair_scorer(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
+                                                     tv, sv)
     same = projected_state.dtype == projected_val.dtype
     out_dtype = projected_val.dtype if same else torch.float32
     st, out = masked_aggregate(row_proj, col_proj, pstate, pval, window=window,
-                               compress=_EDGE_CODE[edge_compress_name], bias=_bias_tensor(bias, tv.device),
-                               out_dtype=out_dtype, split3=f32, col_val_lo=pval_lo)
+                               compress=_EDGE_CODE[edge_compress_name], bias=bias_t,
+                               out_dtype=out_dtype, split3=f32, col_val_lo=pval_lo, heads=heads)
     if pad:
         out = out[..., :out_dim]
     return (st.to(projected_state.dtype).reshape(*batch_shape, n_t),

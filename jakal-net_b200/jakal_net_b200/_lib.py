@@ -26,6 +26,16 @@ JK_ERR_ALIGNMENT = -8
 JK_F32, JK_BF16, JK_F16, JK_BF16X3 = 0, 1, 2, 3
 JK_SOFTSIGN, JK_SIGNED_ABS_SOFTMAX, JK_SIGNED_ENTMAX15, JK_SOFTMAX = 0, 1, 2, 3
 
+JK_HEADS_MAX, JK_HEADS_SMOOTHMAX, JK_HEADS_SIGNED_SMOOTHMAX = 0, 1, 2
+
+
+class JkHeads(ctypes.Structure):
+    """jk_heads_t: multi-head scorer of the *_mh entry points."""
+
+    _fields_ = [("heads", ctypes.c_int), ("kph", ctypes.c_int), ("combine", ctypes.c_int),
+                ("head_bias", ctypes.c_void_p)]
+
+
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int
@@ -88,6 +98,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "jk_transition_pairwise_topk_noalloc_capacity": (_i64, []),
 }
+# The multi-head variants take the same arguments plus a jk_heads_t* before the stream.
+_HP = ctypes.POINTER(JkHeads)
+for _name in ("jk_propagation_topk_forward", "jk_transition_query_topk_forward", "jk_transition_pairwise_topk_forward",
+              "jk_propagation_window_forward", "jk_transition_pairwise_dense_forward"):
+    _res, _args = SIGNATURES[_name]
+    SIGNATURES[_name + "_mh"] = (_res, _args[:-1] + [_HP, _p])
 
 _LIB: ctypes.CDLL | None = None
 

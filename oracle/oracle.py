@@ -21,6 +21,7 @@ __all__ = [
     "round_to",
     "lowrank_project",
     "lowrank_scores",
+    "multihead_scores",
     "causal_window_visible",
     "select_topk",
     "compress",
@@ -88,6 +89,28 @@ def lowrank_project(x, w, core=None, temperature: float = 1.0, dtype: str = "bf1
 def lowrank_scores(row_proj, col_proj, bias: float = 0.0) -> np.ndarray:
     """score[b, t, s] = row_proj[b, t] . col_proj[b, s] + bias  (modules.py:93-100)."""
     return np.einsum("btr,bsr->bts", np.asarray(row_proj, np.float64), np.asarray(col_proj, np.float64)) + bias
+
+
+def multihead_scores(row_proj, col_proj, head_bias=None, combine: str = "max") -> np.ndarray:
+    """MultiHeadPairwise scores (modules.py:274-299): per-head s_h = row_proj[:, h] .
+    col_proj[:, h] + bias[h] for row_proj [B, H, T, R], col_proj [B, H, S, R] (core applied),
+    combined over the heads: max (:291-298); smoothmax = logsumexp - log H (:276-280);
+    signed_smoothmax = sum_h s_h softmax_h(|s_h|) (:281-284). Returns [B, T, S]."""
+    s = np.einsum("bhtr,bhsr->bhts", np.asarray(row_proj, np.float64), np.asarray(col_proj, np.float64))
+    H = s.shape[1]
+    if head_bias is not None:
+        s = s + np.asarray(head_bias, np.float64).reshape(1, H, 1, 1)
+    if combine == "max":
+        return s.max(axis=1)
+    if combine == "smoothmax":
+        m = s.max(axis=1, keepdims=True)
+        return (m + np.log(np.exp(s - m).sum(axis=1, keepdims=True)))[:, 0] - np.log(H)
+    if combine == "signed_smoothmax":
+        a = np.abs(s)
+        w = np.exp(a - a.max(axis=1, keepdims=True))
+        w = w / w.sum(axis=1, keepdims=True)
+        return (s * w).sum(axis=1)
+    raise ValueError(f"unknown head combine {combine!r}")
 
 
 def causal_window_visible(n_rows: int, n_cols: int, window: int | None) -> np.ndarray:

@@ -119,6 +119,25 @@ def main():
                                             out_val=_np(d_val), k=np.int64(4), window=np.int64(9),
                                             compress="softsign")
 
+    # multi-head scorers (modules.py:259-299): per-head low-rank scores combined by max /
+    # smoothmax / signed_smoothmax; the raw combined scores and a top-k propagation over them
+    for ai, agg in enumerate(("max", "smoothmax", "signed_smoothmax")):
+        hs = [pairwise(D, R, 80 + 3 * ai + h) for h in range(3)]
+        with torch.no_grad():
+            for h, hm in enumerate(hs):
+                hm.bias.fill_(0.05 * (h - 1))
+        mh = jn.MultiHeadPairwise(hs, aggregate=agg)
+        lay = layer(B, N, D, 90 + ai)
+        with torch.no_grad():
+            scores = mh(lay.val, lay.val)
+        op = jn.SparsePropagation(pairwise_fn=mh, sparse_type="topk", topk=5, implementation="reference")
+        delta = op(lay)
+        out[f"multihead_{agg}"] = dict(
+            val=_np(lay.val), state=_np(lay.state), w_s=np.stack([_np(h.source_proj.weight) for h in hs]),
+            w_t=np.stack([_np(h.target_proj.weight) for h in hs]), core=np.stack([_np(h.normalized_weight()) for h in hs]),
+            bias=np.array([h.bias.item() for h in hs], np.float32), scores=_np(scores), k=np.int64(5),
+            compress="softsign", out_state=_np(delta.delta_state), out_val=_np(delta.delta_val))
+
     # transitions with a low-rank route
     def route(src_dim, dst_dim, rank, seed, temperature):
         torch.manual_seed(seed)

@@ -155,3 +155,28 @@ def test_entmax15_sums_to_one_and_is_sparse():
     p = oracle.entmax15(np.array([3.0, 1.0, 0.2, -1.0]))
     assert abs(p.sum() - 1.0) < 1e-12
     assert p[-1] == 0.0
+
+
+def _multihead_projections(g, dtype="f32"):
+    """Per-head projections [B, H, N, R] of a multi-head fixture."""
+    H = g["w_s"].shape[0]
+    pt = np.stack([oracle.lowrank_project(g["val"], g["w_t"][h], None, 1.0, dtype) for h in range(H)], axis=1)
+    ps = np.stack([oracle.lowrank_project(g["val"], g["w_s"][h], g["core"][h], 1.0, dtype) for h in range(H)], axis=1)
+    return pt, ps
+
+
+@pytest.mark.parametrize("combine", ["max", "smoothmax", "signed_smoothmax"])
+def test_multihead_scores_match_reference(combine):
+    g = _load(f"multihead_{combine}")
+    pt, ps = _multihead_projections(g)
+    _close(oracle.multihead_scores(pt, ps, g["bias"], combine), g["scores"])
+
+
+@pytest.mark.parametrize("combine", ["max", "smoothmax", "signed_smoothmax"])
+def test_multihead_topk_propagation_matches_reference(combine):
+    g = _load(f"multihead_{combine}")
+    pt, ps = _multihead_projections(g)
+    scores = oracle.multihead_scores(pt, ps, g["bias"], combine)
+    st, val, _, _ = oracle.topk_from_scores(scores, g["state"], g["val"], int(g["k"]), compress_name="softsign")
+    _close(st, g["out_state"])
+    _close(val, g["out_val"])
