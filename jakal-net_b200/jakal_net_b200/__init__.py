@@ -228,11 +228,27 @@ def _head_bias(bias: Optional[Tensor], heads: int, device: torch.device, scale: 
     return (b / scale).contiguous()
 
 
+def _diagonal_projections(target_val: Tensor, source_val: Tensor, w_hat: Tensor, temperature: float = 1.0):
+    """Diagonal bilinear scorer (modules.py:37-53, 385-412): score = target . (source * w_hat).
+    The projections are identity / diag(w_hat) GEMMs through jk_lowrank_project: one exact
+    product per output, rounded once -- the reference's elementwise multiply."""
+    D = target_val.shape[-1]
+    if source_val.shape[-1] != D or w_hat.numel() != D:
+        raise RuntimeError("diagonal bilinear scorer needs matching dims.")
+    eye = torch.eye(D, device=target_val.device, dtype=torch.float32)
+    row_proj = lowrank_project(target_val, eye)
+    col_proj = lowrank_project(source_val, eye, core=w_hat, temperature=temperature)
+    return row_proj, col_proj
+
+
 def _pair_scorer(kind: str, weight: Tensor, bias, in_weight, in_bias, out_weight, out_bias, target_val: Tensor,
                  source_val: Tensor):
-    """Projections of a pairwise spec (kernel_common.py:151-192): low_rank_bilinear or
-    multihead_{max,smoothmax,signed_smoothmax}_low_rank_bilinear. Returns (row_proj [target],
-    col_proj [source, * core], scalar bias tensor or None, Heads or None)."""
+    """Projections of a pairwise spec (kernel_common.py:151-192): low_rank_bilinear,
+    diagonal_bilinear (dim <= 128) or multihead_{max,smoothmax,signed_smoothmax}_low_rank_bilinear.
+    Returns (row_proj [target], col_proj [source, * core], scalar bias tensor or None, Heads or None)."""
+    if kind == "diagonal_bilinear":
+        row_proj, col_proj = _diagonal_projections(target_val, source_val, weight)
+        return row_proj, col_proj, _bias_tensor(bias, target_val.device), None
     if in_weight is None or out_weight is None:
         raise RuntimeError("Low-rank bilinear pairwise kernel is missing projection weights.")
     if in_bias is not None or out_bias is not None:
@@ -351,18 +367,26 @@ def propagation_window_topk(kind, weight, bias, in_weight, in_bias, out_weight, 
 
 def _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
                        hidden_weight, hidden_bias, out_weight, out_bias, temperature, src_val, dst_val):
-    """Route projections (kernel_common.py:238-295): low_rank_bilinear_route or
-    multihead_max_low_rank_bilinear_route; logits = (ps . pd + b) / T. Returns
-    (src_proj / T, dst_proj, scalar bias / T or None, Heads or None)."""
-    if route_kind not in ("low_rank_bilinear_route", "multihead_max_low_rank_bilinear_route"):
+    """Route projections (kernel_common.py:238-295): low_rank_bilinear_route,
+    diagonal_bilinear_route (dim <= 128) or multihead_max_low_rank_bilinear_route;
+    logits = (ps . pd + b) / T. Returns (src_proj / T, dst_proj, scalar bias / T or None,
+    Heads or None)."""
+    if route_kind not in ("low_rank_bilinear_route", "multihead_max_low_rank_bilinear_route",
+                          "diagonal_bilinear_route"):
         raise TypeError(f"Unsupported pairwise route kind for b200_sm100a: {route_kind}")
+    temperature = float(temperature)
+    if temperature <= 0.0:
+        raise RuntimeError("route temperature must be positive.")
+    if route_kind == "diagonal_bilinear_route":
+        if any(t is not None for t in (source_weight, source_bias, target_weight, target_bias, hidden_weight,
+                                       hidden_bias, out_weight, out_bias)):
+            raise TypeError("Diagonal routes take no projection / hidden layers.")
+        dst_proj, src_proj = _diagonal_projections(dst_val, src_val, core_weight, temperature)
+        return src_proj, dst_proj, _bias_tensor(bias, src_val.device, temperature), None
     if source_weight is None or target_weight is None:
         raise RuntimeError("Low-rank route kernel is missing projection weights.")
     if any(t is not None for t in (source_bias, target_bias, hidden_weight, hidden_bias, out_weight, out_bias)):
         raise TypeError("Low-rank route projections take no bias / hidden layers.")
-    temperature = float(temperature)
-    if temperature <= 0.0:
-        raise RuntimeError("route temperature must be positive.")
     if route_kind == "multihead_max_low_rank_bilinear_route":
         # max_h(l_h) / T == max_h(l_h / T): every head's source projection and bias take the 1 / T
         H = source_weight.shape[0]

@@ -138,6 +138,32 @@ def main():
             bias=np.array([h.bias.item() for h in hs], np.float32), scores=_np(scores), k=np.int64(5),
             compress="softsign", out_state=_np(delta.delta_state), out_val=_np(delta.delta_val))
 
+    # diagonal bilinear scorer / route (modules.py:37-53, 385-412)
+    torch.manual_seed(95)
+    dm = jn.DiagonalBilinearPairwise(D)
+    with torch.no_grad():
+        dm.weight.copy_(torch.rand(D) + 0.5)
+        dm.bias.fill_(0.07)
+    lay = layer(B, N, D, 96)
+    op = jn.SparsePropagation(pairwise_fn=dm, sparse_type="topk", topk=5, implementation="reference")
+    delta = op(lay)
+    out["prop_topk_diagonal"] = dict(val=_np(lay.val), state=_np(lay.state), core=_np(dm.normalized_weight()),
+                                     bias=np.float32(dm.bias.item()), k=np.int64(5), compress="softsign",
+                                     out_state=_np(delta.delta_state), out_val=_np(delta.delta_val))
+    torch.manual_seed(97)
+    dr = jn.DiagonalBilinearRoute(D, D)
+    with torch.no_grad():
+        dr.weight.copy_(torch.rand(D) + 0.5)
+        dr.bias.fill_(-0.1)
+    src = layer(B, 29, D, 98)
+    dst = layer(B, 11, D, 99)
+    op = jn.SparseTransition(route_fn=dr, topk=3, route_compress_name="softmax", implementation="reference")
+    delta = op.compute_delta(src, dst)
+    out["transition_topk_diagonal"] = dict(
+        src_val=_np(src.val), src_state=_np(src.state), dst_val=_np(dst.val), core=_np(dr.normalized_weight()),
+        bias=np.float32(dr.bias.item()), temperature=np.float32(1.0), k=np.int64(3), compress="softmax",
+        out_state=_np(delta.delta_state), out_val=_np(delta.delta_val))
+
     # transitions with a low-rank route
     def route(src_dim, dst_dim, rank, seed, temperature):
         torch.manual_seed(seed)

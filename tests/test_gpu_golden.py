@@ -112,3 +112,24 @@ def test_dense_transition_matches_reference(dev, compress):
                                           compress, float(g["temperature"]), sender, g["src_val"], g["dst_val"],
                                           g["src_state"], g["src_val"], 128, 128)
     _check(st, vv, g)
+
+
+def test_diagonal_topk_matches_reference(dev):
+    import jakal_net_b200 as jk
+
+    g = _load("prop_topk_diagonal", dev)
+    st, vv = jk.propagation_topk("diagonal_bilinear", g["core"], torch.tensor(float(g["bias"]), device=dev), None,
+                                 None, None, None, "softsign", g["val"], g["state"], g["val"], int(g["k"]), 128, 128)
+    _check(st, vv, g)
+
+
+def test_diagonal_route_transition_matches_reference(dev):
+    import jakal_net_b200 as jk
+
+    g = _load("transition_topk_diagonal", dev)
+    sender = torch.nn.functional.softplus(g["src_state"])
+    st, vv = jk.transition_pairwise_topk("diagonal_bilinear_route", None, None, None, None, g["core"],
+                                         torch.tensor(float(g["bias"]), device=dev), None, None, None, None,
+                                         float(g["temperature"]), sender, g["src_val"], g["dst_val"], g["src_state"],
+                                         g["src_val"], int(g["k"]), 128, 128, route_compress_name="softmax")
+    _check(st, vv, g)

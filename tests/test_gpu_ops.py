@@ -209,3 +209,24 @@ def test_transition_pairwise_dense_op(dev, compress, shape):
                                           compress_name=compress)
     parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
     parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_diagonal_bilinear_topk_op(dev, D):
+    # diagonal_bilinear (modules.py:37-53): score = target . (source * w_hat) + b
+    import jakal_net_b200 as jk
+
+    g = np.random.default_rng(D)
+    B, N, k = 2, 400, 16
+    val = _t(g.standard_normal((B, N, D)) / np.sqrt(D), dev)
+    state = _t(g.standard_normal((B, N)), dev)
+    w = np.abs(g.standard_normal(D)) + 0.5
+    w_hat = _t(w * np.sqrt(D) / np.linalg.norm(w), dev)
+    st, vv = jk.propagation_topk("diagonal_bilinear", w_hat, torch.tensor(0.02, device=dev), None, None, None, None,
+                                 "signed_abs_softmax", val, state, val, k, 128, 128)
+    v = _np(val)
+    ps = oracle.round_to(v * _np(w_hat), "bf16")
+    o_st, o_val, _, _ = oracle.topk_from_scores(oracle.lowrank_scores(v, ps), _np(state), v, k, bias=0.02,
+                                                compress_name="signed_abs_softmax")
+    parity.assert_rows_close(_np(vv), o_val, rtol=OUT_RTOL, what="val")
+    parity.assert_rows_close(_np(st), o_st, rtol=OUT_RTOL, what="state")

@@ -180,3 +180,20 @@ def test_multihead_topk_propagation_matches_reference(combine):
     st, val, _, _ = oracle.topk_from_scores(scores, g["state"], g["val"], int(g["k"]), compress_name="softsign")
     _close(st, g["out_state"])
     _close(val, g["out_val"])
+
+
+def test_diagonal_topk_propagation_matches_reference():
+    g = _load("prop_topk_diagonal")
+    scores = oracle.lowrank_scores(g["val"], g["val"] * g["core"], float(g["bias"]))
+    st, val, _, _ = oracle.topk_from_scores(scores, g["state"], g["val"], int(g["k"]), compress_name="softsign")
+    _close(st, g["out_state"])
+    _close(val, g["out_val"])
+
+
+def test_diagonal_route_transition_matches_reference():
+    g = _load("transition_topk_diagonal")
+    logits = oracle.lowrank_scores(g["src_val"] * g["core"], g["dst_val"], float(g["bias"]))
+    st, val = oracle.sparse_transition_from_logits(logits, g["src_state"], g["src_val"], oracle.softplus(g["src_state"]),
+                                                   int(g["k"]), compress_name="softmax")
+    _close(st, g["out_state"])
+    _close(val, g["out_val"])
