@@ -174,6 +174,21 @@ int jk_transition_pairwise_dense_forward(const void* src_proj, const void* dst_p
                                          float* stats, void* out_state, void* out_val, int out_dtype,
                                          jk_stream_t stream);
 
+/* Row block of a propagation / per-query top-k (row-sharded multi-GPU): the arguments of
+ * jk_propagation_topk_forward over the FULL tensors, computing only the rows
+ * [row_begin, row_begin + row_count) (row_begin a multiple of 128; row_count a multiple of
+ * 128 unless the block runs to the last row); the other output rows are not written.
+ * Nothing in the reference corresponds (its kernels run on one GPU); this is the per-rank
+ * step of the query-row-block partition, whose outputs an all-gather then assembles. */
+int jk_propagation_topk_rows_forward(const void* row_proj, const void* col_proj, int64_t batch,
+                                     int64_t n_rows, int64_t row_begin, int64_t row_count,
+                                     int64_t n_cols, int64_t rp, int proj_dtype, const void* col_state,
+                                     const void* col_sender, int state_dtype, const void* col_val,
+                                     int64_t dim, int val_dtype, int64_t k, int64_t window,
+                                     float score_bias, const float* bias_dev, int compress,
+                                     void* out_state, void* out_val, int out_dtype, float* out_scores,
+                                     int64_t* out_index, jk_stream_t stream);
+
 /* Multi-head variants: the entry point of the same name without _mh, with the scorer
  * `heads` (jk_heads_t above; 16-bit projections only, not JK_BF16X3). */
 int jk_propagation_topk_forward_mh(const void* row_proj, const void* col_proj, int64_t batch,

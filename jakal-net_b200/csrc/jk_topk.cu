@@ -104,6 +104,7 @@ struct Params {
   int64_t n_rows, n_cols, rp, dim;
   int k;
   int64_t window;  // < 0: no mask
+  int64_t row_begin, row_count;  // the launch's row block (row_begin a multiple of kRows)
   float bias;
   const float* bias_dev;
   int compress;
@@ -674,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t b = blockIdx.y;
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kRows;
+  const int64_t t0 = p.row_begin + static_cast<int64_t>(blockIdx.x) * kRows;
   const int k = p.k;
 
   // Column-tile range (identical in every thread).
@@ -1309,7 +1310,7 @@ int launch_vt(const CUtensorMap& tr, const CUtensorMap& tc, const CUtensorMap& t
     cudaGetLastError();
     return JK_ERR_LAUNCH;
   }
-  const dim3 grid(static_cast<unsigned>((p.n_rows + kRows - 1) / kRows), static_cast<unsigned>(batch));
+  const dim3 grid(static_cast<unsigned>((p.row_count + kRows - 1) / kRows), static_cast<unsigned>(batch));
   kern<<<grid, kThreads, sm, st>>>(tr, tc, tv, p, idesc);
   return launch_status();
 }
@@ -1374,9 +1375,16 @@ int gather_forward(const void* row_proj, const void* col_proj, int64_t batch, in
                    int64_t rp, int proj_dtype, const void* col_state, const void* col_sender, int state_dtype,
                    const void* col_val, int64_t dim, int val_dtype, int64_t k, int64_t window, float score_bias,
                    const float* bias_dev, int compress, void* out_state, void* out_val, int out_dtype,
-                   float* out_scores, int64_t* out_index, const jk_heads_t* heads, jk_stream_t stream) {
+                   float* out_scores, int64_t* out_index, const jk_heads_t* heads, int64_t row_begin,
+                   int64_t row_count, jk_stream_t stream) {
   int st = validate_common(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype, col_val,
                            dim, val_dtype, k, compress, out_dtype);
+  if (st != JK_OK) return st;
+  // Row block [row_begin, row_begin + row_count): kRows-aligned start, and a whole number
+  // of kRows tiles unless it runs to the last row.
+  if (row_begin < 0 || row_count <= 0 || row_begin + row_count > n_rows || row_begin % kRows != 0 ||
+      (row_count % kRows != 0 && row_begin + row_count != n_rows))
+    return JK_ERR_BAD_ARG;
   if (st != JK_OK) return st;
   if (out_state == nullptr || out_val == nullptr) return JK_ERR_BAD_ARG;
   if (dim % 8 == 0 && !aligned16(out_val)) return JK_ERR_ALIGNMENT;
@@ -1393,6 +1401,8 @@ int gather_forward(const void* row_proj, const void* col_proj, int64_t batch, in
   p.dim = dim;
   p.k = static_cast<int>(k);
   p.window = window;
+  p.row_begin = row_begin;
+  p.row_count = row_count;
   p.bias = score_bias;
   p.bias_dev = bias_dev;
   p.compress = compress;
@@ -1438,6 +1448,7 @@ int scatter_forward(const void* src_proj, const void* dst_proj, int64_t batch, i
   if (cudaMemsetAsync(accum, 0, sizeof(float) * (n_state + n_val), cs) != cudaSuccess) return launch_status();
   Params p{};
   p.n_rows = n_src;
+  p.row_count = n_src;
   p.n_cols = n_dst;
   p.rp = rp;
   p.dim = dim;
@@ -1479,7 +1490,7 @@ extern "C" int jk_propagation_topk_forward(const void* row_proj, const void* col
                                            int out_dtype, float* out_scores, int64_t* out_index, jk_stream_t stream) {
   return jk::topk::gather_forward(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, col_sender,
                                   state_dtype, col_val, dim, val_dtype, k, window, score_bias, bias_dev, compress,
-                                  out_state, out_val, out_dtype, out_scores, out_index, nullptr, stream);
+                                  out_state, out_val, out_dtype, out_scores, out_index, nullptr, 0, n_rows, stream);
 }
 
 extern "C" int jk_propagation_topk_forward_mh(const void* row_proj, const void* col_proj, int64_t batch,
@@ -1492,7 +1503,21 @@ extern "C" int jk_propagation_topk_forward_mh(const void* row_proj, const void* 
   if (heads == nullptr) return JK_ERR_BAD_ARG;
   return jk::topk::gather_forward(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, col_sender,
                                   state_dtype, col_val, dim, val_dtype, k, window, score_bias, bias_dev, compress,
-                                  out_state, out_val, out_dtype, out_scores, out_index, heads, stream);
+                                  out_state, out_val, out_dtype, out_scores, out_index, heads, 0, n_rows, stream);
+}
+
+extern "C" int jk_propagation_topk_rows_forward(const void* row_proj, const void* col_proj, int64_t batch,
+                                                int64_t n_rows, int64_t row_begin, int64_t row_count, int64_t n_cols,
+                                                int64_t rp, int proj_dtype, const void* col_state,
+                                                const void* col_sender, int state_dtype, const void* col_val,
+                                                int64_t dim, int val_dtype, int64_t k, int64_t window,
+                                                float score_bias, const float* bias_dev, int compress, void* out_state,
+                                                void* out_val, int out_dtype, float* out_scores, int64_t* out_index,
+                                                jk_stream_t stream) {
+  return jk::topk::gather_forward(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, col_sender,
+                                  state_dtype, col_val, dim, val_dtype, k, window, score_bias, bias_dev, compress,
+                                  out_state, out_val, out_dtype, out_scores, out_index, nullptr, row_begin, row_count,
+                                  stream);
 }
 
 extern "C" int jk_transition_query_topk_forward(const void* query_proj, const void* source_proj, int64_t batch,
@@ -1504,7 +1529,7 @@ extern "C" int jk_transition_query_topk_forward(const void* query_proj, const vo
                                                 int64_t* out_index, jk_stream_t stream) {
   return jk::topk::gather_forward(query_proj, source_proj, batch, n_query, n_source, rp, proj_dtype, source_state,
                                   source_sender, state_dtype, source_val, dim, val_dtype, k, -1, score_bias, bias_dev,
-                                  compress, out_state, out_val, out_dtype, out_scores, out_index, nullptr, stream);
+                                  compress, out_state, out_val, out_dtype, out_scores, out_index, nullptr, 0, n_query, stream);
 }
 
 extern "C" int jk_transition_query_topk_forward_mh(const void* query_proj, const void* source_proj, int64_t batch,
@@ -1518,7 +1543,7 @@ extern "C" int jk_transition_query_topk_forward_mh(const void* query_proj, const
   if (heads == nullptr) return JK_ERR_BAD_ARG;
   return jk::topk::gather_forward(query_proj, source_proj, batch, n_query, n_source, rp, proj_dtype, source_state,
                                   source_sender, state_dtype, source_val, dim, val_dtype, k, -1, score_bias, bias_dev,
-                                  compress, out_state, out_val, out_dtype, out_scores, out_index, heads, stream);
+                                  compress, out_state, out_val, out_dtype, out_scores, out_index, heads, 0, n_query, stream);
 }
 
 extern "C" int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_proj, int64_t batch,

@@ -274,13 +274,15 @@ def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_va
                    window: int = -1, compress: int = _lib.JK_SOFTSIGN, col_sender: Optional[Tensor] = None,
                    bias: Optional[Tensor] = None, score_bias: float = 0.0,
                    out_dtype: Optional[torch.dtype] = None, return_selection: bool = False, split3: bool = False,
-                   heads: Optional[Heads] = None):
+                   heads: Optional[Heads] = None, rows: Optional[tuple[int, int]] = None):
     """Raw fused top-k aggregate over already-projected inputs (jk_propagation_topk_forward,
     or jk_propagation_topk_forward_mh with a multi-head scorer).
 
     row_proj [B, T, rp], col_proj [B, S, rp], col_state [B, S], col_val [B, S, D].
     Returns (state [B, T], val [B, T, D]) and, with return_selection, also the selected
     scores (f32 [B, T, k]) and indices (int64 [B, T, k]).
+    rows=(begin, count): compute only that row block (jk_propagation_topk_rows_forward;
+    begin a multiple of 128); the other output rows are left unwritten (zeros here).
     """
     for name, t in (("row_proj", row_proj), ("col_proj", col_proj), ("col_state", col_state), ("col_val", col_val)):
         _require_cuda(name, t)
@@ -289,8 +291,9 @@ def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_va
     D = col_val.shape[-1]
     dev = col_val.device
     out_dtype = out_dtype or col_val.dtype
-    out_state = torch.empty((B, T), device=dev, dtype=out_dtype)
-    out_val = torch.empty((B, T, D), device=dev, dtype=out_dtype)
+    alloc = torch.empty if rows is None else torch.zeros
+    out_state = alloc((B, T), device=dev, dtype=out_dtype)
+    out_val = alloc((B, T, D), device=dev, dtype=out_dtype)
     scores = torch.empty((B, T, k), device=dev, dtype=torch.float32) if return_selection else None
     index = torch.empty((B, T, k), device=dev, dtype=torch.int64) if return_selection else None
     sender = None if col_sender is None else col_sender.to(col_state.dtype).contiguous()
@@ -301,7 +304,13 @@ def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_va
             out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state),
             _ptr(scores), _ptr(index))
     with torch.cuda.device(dev):
-        if heads is None:
+        if rows is not None:
+            if heads is not None:
+                raise RuntimeError("row blocks take the single-head scorer")
+            check(_LIBRARY.jk_propagation_topk_rows_forward(*args[:4], int(rows[0]), int(rows[1]), *args[4:],
+                                                            _stream(dev)),
+                  "jk_propagation_topk_rows_forward")
+        elif heads is None:
             check(_LIBRARY.jk_propagation_topk_forward(*args, _stream(dev)), "jk_propagation_topk_forward")
         else:
             check(_LIBRARY.jk_propagation_topk_forward_mh(*args, heads.ref(), _stream(dev)),

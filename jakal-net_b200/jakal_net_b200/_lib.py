@@ -98,6 +98,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "jk_transition_pairwise_topk_noalloc_capacity": (_i64, []),
 }
+_args = SIGNATURES["jk_propagation_topk_forward"][1]
+SIGNATURES["jk_propagation_topk_rows_forward"] = (_i32, _args[:4] + [_i64, _i64] + _args[4:])  # + row block
 # The multi-head variants take the same arguments plus a jk_heads_t* before the stream.
 _HP = ctypes.POINTER(JkHeads)
 for _name in ("jk_propagation_topk_forward", "jk_transition_query_topk_forward", "jk_transition_pairwise_topk_forward",
