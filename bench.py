@@ -7,10 +7,15 @@ bf16 inputs with f32 accumulation, softsign edges, seed 1; synthetic inputs of t
 One step = the projections (two tcgen05 GEMMs) + the fused score / top-k / aggregate
 kernel over the whole batch. Metric: scored (target, visible source) pairs per second.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 2|5]
 
 Under torchrun every rank runs its own batch (weak scaling, no collective on the data
 path); timings are device-side CUDA events, max over ranks.
+
+--config 5 (B4, N32768, D512, R64, causal window 4096, top-k 64, bf16,
+seed 4) runs the query-row-block partition instead: inputs replicated on every rank, rank r
+computes rows [r N/P, (r+1) N/P) (jakal_net_b200.sharding), then an NCCL all-gather
+assembles the outputs (strong scaling: the total work is fixed).
 """
 from __future__ import annotations
 
@@ -300,6 +305,107 @@ def run_b200(args, rank, world, device):
     print(json.dumps(line), flush=True)
 
 
+C5 = dict(B=4, N=32768, D=512, R=64, K=64, W=4096, SEED=4)
+C5_WORKLOAD = "config5: causal window 4096 intersect top-k 64, B4 N32768 D512 R64, bf16, softsign, row-sharded"
+
+
+def run_config5(args, rank, world, device):
+    import jakal_net_b200 as jk
+    from jakal_net_b200 import sharding
+
+    b, n, d, r, k, w = C5["B"], C5["N"], C5["D"], C5["R"], C5["K"], C5["W"]
+    pairs = b * pairs_per_batch_item(n, w)
+    g = torch.Generator().manual_seed(C5["SEED"])
+    to = dict(device=device, dtype=torch.bfloat16)
+    h_val = torch.randn(b, n, d, generator=g).to(torch.bfloat16).pin_memory()
+    h_state = torch.randn(b, n, generator=g).to(torch.bfloat16).pin_memory()
+    w_s = (torch.randn(r, d, generator=g) / d ** 0.5).to(**to)
+    w_t = (torch.randn(r, d, generator=g) / d ** 0.5).to(**to)
+    core = torch.full((r,), r ** -0.5).to(**to)
+    val = torch.empty(b, n, d, **to)
+    state = torch.empty(b, n, **to)
+    if rank == 0:
+        val.copy_(h_val)
+        state.copy_(h_state)
+    if world > 1:  # inputs replicated once at setup
+        sharding.replicate(val)
+        sharding.replicate(state)
+    blocks = sharding.row_blocks(n, world)
+    begin, count = blocks[rank]
+    out_state = torch.zeros(b, n, **to)
+    out_val = torch.zeros(b, n, d, **to)
+
+    def compute(v, s):
+        rp = jk.lowrank_project(v, w_t)
+        cp = jk.lowrank_project(v, w_s, core=core)
+        sharding._kernel_block(rp, cp, s, v, k, w, begin, count, out_state, out_val)
+
+    def gather():
+        if world > 1:
+            sharding.gather_row_blocks(out_state, out_val, blocks)
+
+    def timed(fn, steps):
+        ms = []
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(device)
+            ms.append(e0.elapsed_time(e1))
+        return sum(ms) / len(ms)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        compute(val, state)
+        gather()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        compute_ms = max_over_ranks(timed(lambda: compute(val, state), args.steps))
+        if world > 1:
+            torch.distributed.barrier()
+        sharded_ms = max_over_ranks(timed(lambda: (compute(val, state), gather()), args.steps))
+    h_out_val = torch.empty(b, count, d, dtype=torch.bfloat16).pin_memory()
+
+    def e2e():
+        val.copy_(h_val, non_blocking=True)
+        state.copy_(h_state, non_blocking=True)
+        compute(val, state)
+        gather()
+        h_out_val.copy_(out_val[:, begin:begin + count], non_blocking=True)
+
+    if world > 1:
+        torch.distributed.barrier()
+    e2e_ms = max_over_ranks(timed(e2e, max(3, min(args.steps, 20))))
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": pairs / (compute_ms * 1e-3) / 1e9, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": compute_ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) inputs of the config shape, random-init weights)",
+        "config": {"workload": C5_WORKLOAD, "batch": b, "nodes": n, "dim": d, "rank": r, "topk": k, "window": w,
+                   "pairs_per_step": pairs, "l2": "inputs (134 MB values) larger than L2",
+                   "timing": "CUDA events per step, max over ranks",
+                   "parallelism": f"query-row blocks x{world}; value = block compute, outputs left row-sharded"},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clk.summary(),
+        "with_allgather": {"ms_per_step": sharded_ms, "value": pairs / (sharded_ms * 1e-3) / 1e9, "unit": UNIT},
+        "e2e": {"value": pairs / (e2e_ms * 1e-3) / 1e9, "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": (h_val.numel() + h_state.numel()) * 2,
+                "d2h_bytes_per_step": h_out_val.numel() * 2},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -307,6 +413,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=[2, 5], default=2)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -320,7 +427,7 @@ def main():
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=device)
     try:
-        run_b200(args, rank, world, device)
+        (run_config5 if args.config == 5 else run_b200)(args, rank, world, device)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

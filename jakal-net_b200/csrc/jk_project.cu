@@ -14,6 +14,18 @@
 namespace jk {
 namespace proj {
 
+#ifdef JK_PHASE_PROFILE
+__device__ long long g_ptrace[1024][16];
+#define JK_PSTAMP(i)                                     \
+  do {                                                   \
+    if (blockIdx.x < 1024) g_ptrace[blockIdx.x][i] = clock64(); \
+  } while (0)
+#else
+#define JK_PSTAMP(i) \
+  do {               \
+  } while (0)
+#endif
+
 constexpr int kRows = 128;
 constexpr int kStages = 4;
 constexpr int kThreads = 160;
@@ -31,10 +43,21 @@ struct Params {
 
 __host__ __device__ constexpr int a_bytes() { return kRows * 128; }
 
-template <int RP>
+// Rounds to the projection dtype and back (round to nearest even).
+template <bool BF16>
+__device__ __forceinline__ float round16(float x) {
+  if (BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  return __half2float(__float2half_rn(x));
+}
+
+// The dtype, core and temperature steps are template parameters: the epilogue below is
+// unrolled over every column of a row, and per-element runtime branches over all variants
+// made that straight-line code several times larger -- instruction fetch, not arithmetic,
+// then dominated the kernel.
+template <int RP, bool BF16, bool CORE, bool TEMP>
 __global__ void __launch_bounds__(kThreads, 1)
     project_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                   Params p) {
+                   const __grid_constant__ CUtensorMap tm_out, Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kABytes = a_bytes();
@@ -74,6 +97,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) JK_PSTAMP(0);
 
   if (warp == 4) {
     if (lane == 0) {
@@ -92,6 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < nchunks && ok; ++c) {
         const int s = c % kStages;
         if (!mbar_wait(&full[s], (c / kStages) & 1)) { ok = false; break; }
+        if (c < 8) JK_PSTAMP(1 + c);
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem + s * kStageBytes);
         const uint32_t b_addr = a_addr + kABytes;
@@ -123,59 +148,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // Epilogue: thread = row.
+    // Epilogue: thread = row. The rounded row goes into the (now idle) first operand stage
+    // in the 128-byte-swizzled layout of the output tensor map -- RP / 64 boxes of 128 rows
+    // x 64 columns -- and one thread stores the tile with TMA (rows past p.rows are clipped).
     bool ok = mbar_wait(done, 0);
+    if (threadIdx.x == 0) JK_PSTAMP(10);
     if (!ok) {
       atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
     } else {
       tc_fence_after();
       const int r_in = warp * 32 + lane;
-      const int64_t row = row0 + r_in;
-      uint8_t* out_row = reinterpret_cast<uint8_t*>(p.out) + row * p.rp * 2;
+      uint8_t* stage = smem;  // every MMA has retired: the stages are free
 #pragma unroll
       for (int cb = 0; cb < RP; cb += 32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + cb, v);
         tmem_ld_wait();
-        if (row < p.rows) {
-          uint32_t packed[16];
+        if (threadIdx.x == 0 && cb == 0) JK_PSTAMP(12);
+        uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float f[2];
+        for (int i = 0; i < 32; i += 2) {
+          float f[2];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int c = cb + i + h;
-              float x = __uint_as_float(v[i + h]);
-              if (c >= p.rank) {
-                x = 0.f;
-              } else if (p.bf16) {
-                x = __bfloat162float(__float2bfloat16_rn(x));
-                if (p.core) x = __bfloat162float(__float2bfloat16_rn(x * core_s[c]));
-                if (p.temperature != 1.f) x = __bfloat162float(__float2bfloat16_rn(x / p.temperature));
-              } else {
-                x = __half2float(__float2half_rn(x));
-                if (p.core) x = __half2float(__float2half_rn(x * core_s[c]));
-                if (p.temperature != 1.f) x = __half2float(__float2half_rn(x / p.temperature));
-              }
-              f[h] = x;
-            }
-            if (p.bf16) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(f[0], f[1]);
-              packed[i / 2] = *reinterpret_cast<uint32_t*>(&b2);
-            } else {
-              __half2 h2 = __floats2half2_rn(f[0], f[1]);
-              packed[i / 2] = *reinterpret_cast<uint32_t*>(&h2);
-            }
+          for (int h = 0; h < 2; ++h) {
+            const int c = cb + i + h;
+            float x = round16<BF16>(__uint_as_float(v[i + h]));
+            if (CORE) x = round16<BF16>(x * core_s[c]);
+            if (TEMP) x = round16<BF16>(x / p.temperature);
+            f[h] = c < p.rank ? x : 0.f;
           }
-          uint4* dst = reinterpret_cast<uint4*>(out_row + cb * 2);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          if (BF16) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(f[0], f[1]);
+            packed[i / 2] = *reinterpret_cast<uint32_t*>(&b2);
+          } else {
+            __half2 h2 = __floats2half2_rn(f[0], f[1]);
+            packed[i / 2] = *reinterpret_cast<uint32_t*>(&h2);
+          }
         }
+        // columns [cb, cb + 32) = 16-byte chunks (cb % 64) / 8 .. + 3 of box cb / 64
+        uint8_t* box = stage + (cb / 64) * (kRows * 128) + (r_in >> 3) * 1024 + (r_in & 7) * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = ((cb & 63) >> 3) + q;
+          *reinterpret_cast<uint4*>(box + ((chunk ^ (r_in & 7)) << 4)) =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        }
+        if (threadIdx.x == 0 && cb == 0) JK_PSTAMP(13);
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+      if (threadIdx.x == 0) {
+#pragma unroll
+        for (int bx = 0; bx < RP / 64; ++bx) tma_store_3d(&tm_out, stage + bx * kRows * 128, bx * 64, static_cast<int>(row0), 0);
+        bulk_commit_group();
+        bulk_wait_group_read0();
       }
     }
+    if (threadIdx.x == 0) JK_PSTAMP(14);
     tc_fence_before();
   }
   __syncthreads();
+  if (threadIdx.x == 0) JK_PSTAMP(11);
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, RP < 32 ? 32 : RP);
@@ -185,6 +218,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int RP>
 constexpr int smem_bytes() {
   return 1024 + kStages * (a_bytes() + RP * 128) + 256;
+}
+
+template <int RP, bool BF16, bool CORE, bool TEMP>
+int launch_one(dim3 grid, cudaStream_t s, const CUtensorMap& tm_x, const CUtensorMap& tm_w, const CUtensorMap& tm_out,
+               const Params& p) {
+  constexpr int sm = smem_bytes<RP>();
+  auto kern = project_kernel<RP, BF16, CORE, TEMP>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) {
+    cudaGetLastError();
+    return JK_ERR_LAUNCH;
+  }
+  kern<<<grid, kThreads, sm, s>>>(tm_x, tm_w, tm_out, p);
+  return JK_OK;
+}
+
+template <int RP>
+int dispatch(int variant, dim3 grid, cudaStream_t s, const CUtensorMap& tm_x, const CUtensorMap& tm_w,
+             const CUtensorMap& tm_out, const Params& p) {
+  switch (variant) {
+    case 0: return launch_one<RP, false, false, false>(grid, s, tm_x, tm_w, tm_out, p);
+    case 1: return launch_one<RP, false, false, true>(grid, s, tm_x, tm_w, tm_out, p);
+    case 2: return launch_one<RP, false, true, false>(grid, s, tm_x, tm_w, tm_out, p);
+    case 3: return launch_one<RP, false, true, true>(grid, s, tm_x, tm_w, tm_out, p);
+    case 4: return launch_one<RP, true, false, false>(grid, s, tm_x, tm_w, tm_out, p);
+    case 5: return launch_one<RP, true, false, true>(grid, s, tm_x, tm_w, tm_out, p);
+    case 6: return launch_one<RP, true, true, false>(grid, s, tm_x, tm_w, tm_out, p);
+    default: return launch_one<RP, true, true, true>(grid, s, tm_x, tm_w, tm_out, p);
+  }
 }
 
 }  // namespace proj
@@ -211,18 +272,26 @@ extern "C" int jk_lowrank_project(const void* x, int64_t rows, int64_t dim, cons
   if (st != JK_OK) return st;
   st = make_tmap_3d_16bit(&tm_w, w, dim, rank, 1, 64, static_cast<uint32_t>(rp), bf16);
   if (st != JK_OK) return st;
+  CUtensorMap tm_out;
+  st = make_tmap_3d_16bit(&tm_out, out, rp, rows, 1, 64, 128, bf16);
+  if (st != JK_OK) return st;
 
   proj::Params p{rows, dim, rank, rp, core, temperature, bf16 ? 1 : 0, out};
   const dim3 grid(static_cast<unsigned>((rows + 127) / 128));
   auto s = reinterpret_cast<cudaStream_t>(stream);
+  const int variant = (bf16 ? 4 : 0) | (core != nullptr ? 2 : 0) | (temperature != 1.f ? 1 : 0);
   if (rp == 64) {
-    constexpr int sm = proj::smem_bytes<64>();
-    cudaFuncSetAttribute(proj::project_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    proj::project_kernel<64><<<grid, proj::kThreads, sm, s>>>(tm_x, tm_w, p);
+    st = proj::dispatch<64>(variant, grid, s, tm_x, tm_w, tm_out, p);
   } else {
-    constexpr int sm = proj::smem_bytes<128>();
-    cudaFuncSetAttribute(proj::project_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    proj::project_kernel<128><<<grid, proj::kThreads, sm, s>>>(tm_x, tm_w, p);
+    st = proj::dispatch<128>(variant, grid, s, tm_x, tm_w, tm_out, p);
   }
+  if (st != JK_OK) return st;
   return launch_status();
 }
+
+#ifdef JK_PHASE_PROFILE
+extern "C" int jk_debug_ptrace(long long* out, int n) {
+  cudaDeviceSynchronize();
+  return cudaMemcpyFromSymbol(out, jk::proj::g_ptrace, sizeof(long long) * 16 * (n < 1024 ? n : 1024)) == cudaSuccess ? 0 : -1;
+}
+#endif

@@ -44,28 +44,28 @@ namespace jk {
 namespace topk {
 
 #ifdef JK_PHASE_PROFILE
-// Debug-only phase timer (sum over selection warps of clock64 deltas per phase).
-__device__ unsigned long long g_phase[24];
-#define JK_PHASE_MARK(i, t_prev)                                                                \
-  do {                                                                                         \
-    const long long _now = clock64();                                                          \
-    if ((threadIdx.x & 31) == 0) atomicAdd(&g_phase[i], (unsigned long long)(_now - (t_prev))); \
-    t_prev = _now;                                                                             \
+// Debug-only timeline: clock64 stamps of the phase boundaries of every CTA, stored by one
+// thread (no atomics, so the timeline is not perturbed). Slot 0 = start, 15 = SM id.
+constexpr int kTraceCtas = 4096;
+__device__ long long g_trace[kTraceCtas][16];
+#define JK_STAMP(i)                                                                  \
+  do {                                                                               \
+    const int _cta = blockIdx.y * gridDim.x + blockIdx.x;                            \
+    if (_cta < kTraceCtas) g_trace[_cta][i] = clock64();                            \
   } while (0)
-// Adds the cycles spent in `expr` (one thread) to slot i.
-#define JK_PHASE_TIME(i, expr)                                   \
-  ([&]() {                                                       \
-    const long long _t0 = clock64();                             \
-    auto _r = (expr);                                            \
-    if ((threadIdx.x & 31) == 0) atomicAdd(&g_phase[i], (unsigned long long)(clock64() - _t0)); \
-    return _r;                                                   \
-  }())
+#define JK_PHASE_MARK(i, t_prev) \
+  do {                           \
+    if (threadIdx.x == 0) JK_STAMP((i) + 1); \
+  } while (0)
 #else
-#define JK_PHASE_TIME(i, expr) (expr)
+#define JK_STAMP(i) \
+  do {              \
+  } while (0)
 #define JK_PHASE_MARK(i, t_prev) \
   do {                           \
   } while (0)
 #endif
+#define JK_PHASE_TIME(i, expr) (expr)
 
 constexpr int kRows = 128;      // rows per CTA (MMA M)
 constexpr int kCols = 128;      // columns per tile (MMA N)
@@ -78,8 +78,7 @@ constexpr int kMmaWarp = kSelWarps;       // tcgen05.mma issuer
 constexpr int kLoadWarp = kSelWarps + 1;  // TMA loader
 constexpr int kThreads = (kSelWarps + 2) * 32;
 constexpr int kSentinel = INT_MAX;
-constexpr int kJunk = kCap + 2 * kQueue;  // scratch slot of a row for branch-free appends
-static_assert(kStride > kJunk, "buffer row holds candidates, both fallback queues and the junk slot");
+static_assert(kStride >= kCap + 2 * kQueue, "buffer row holds candidates and both fallback queues");
 static_assert(kCap / 2 >= 64, "the score-rank permutation sits behind k <= 64 selected slots");
 
 enum Mode { kGather = 0, kScatter = 1 };
@@ -518,9 +517,6 @@ __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int l
     rank[q] = 0;
   }
   __syncwarp();  // from here on rv / ri of the row are free: every lane holds its keys
-#ifdef JK_PHASE_PROFILE
-  long long t_sel = clock64();
-#endif
   int j = 0;
   for (; j + 4 <= n; j += 4) {
     const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(ks + j);
@@ -534,10 +530,6 @@ __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int l
 #pragma unroll
     for (int q = 0; q < NQ; ++q) rank[q] += a > x[q];
   }
-#ifdef JK_PHASE_PROFILE
-  if (lane == 0) atomicAdd(&g_phase[16], (unsigned long long)(clock64() - t_sel));
-  t_sel = clock64();
-#endif
   int real = 0;
   bool keep[NQ];
   int col[NQ], slot[NQ];
@@ -589,9 +581,6 @@ __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int l
     }
   }
   __syncwarp();
-#ifdef JK_PHASE_PROFILE
-  if (lane == 0) atomicAdd(&g_phase[17], (unsigned long long)(clock64() - t_sel));
-#endif
   return real < k ? real : k;
 }
 
@@ -636,7 +625,7 @@ struct Layout {
   static constexpr int kTotal = 1024 + kRegion0 + kBufBytes + kRowArrays + kBarBytes;
 };
 
-template <int KATOMS, int STAGES, int MODE, typename VT>
+template <int KATOMS, int STAGES, int MODE, typename VT, bool MH>
 __global__ void __launch_bounds__(kThreads, 1)
     topk_kernel(const __grid_constant__ CUtensorMap tm_rows, const __grid_constant__ CUtensorMap tm_cols,
                 const __grid_constant__ CUtensorMap tm_val, Params p, uint32_t idesc) {
@@ -723,6 +712,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+#ifdef JK_PHASE_PROFILE
+  if (threadIdx.x == 0) {
+    JK_STAMP(0);
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    const int cta = blockIdx.y * gridDim.x + blockIdx.x;
+    if (cta < kTraceCtas) g_trace[cta][15] = smid;
+  }
+#endif
 
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ TMA loader
@@ -755,6 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (*any_fail) total += ntiles;
         }
       }
+      JK_STAMP(14);
       if (ok) ok = mbar_wait(slab_bar, 0);
       if (ok && *agg_mode) {
         const SlabRange sr = slab_range<VT>(p, t0);
@@ -788,7 +787,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(bar_a, 0);
       int total = pre_passes * ntiles;
       const int decide_at = total - 1;
-      const int nb = score_buffers(p.heads);
+      const int nb = MH ? score_buffers(p.heads) : 2;
       for (int g = 0; g < total && ok; ++g) {
         const int st = g % STAGES;
         const int buf = g % nb;
@@ -798,10 +797,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a_addr = smem_u32(a_tile);
         const uint32_t b_addr = smem_u32(b_ring + st * L::kBBytes);
-        if (p.heads > 1)
+        if (MH)
           head_score_mmas(tmem + buf * p.heads * kCols, kCols, a_addr, b_addr, idesc, p.heads, p.kph);
         else
           score_mmas<KATOMS>(tmem + buf * kCols, a_addr, b_addr, idesc, p.split3 != 0);
+        if (g == 0) JK_STAMP(10);
         mma_commit(&empty[st]);
         mma_commit(&tfull[buf]);
         if (g == decide_at) {
@@ -823,9 +823,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nkt = (sr.n + kEK - 1) / kEK;
         const int nsl = static_cast<int>((p.dim + kVSlice - 1) / kVSlice);
         uint8_t* vbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bufi) + 1023) & ~uintptr_t(1023));
-#ifdef JK_PHASE_PROFILE
-        const long long t_iss = clock64();
-#endif
+        JK_STAMP(11);
         for (int kt = 0; kt < nkt && ok; ++kt) {
           const int buf = kt & 1;
           if (!JK_PHASE_TIME(8, mbar_wait(&e_full[buf], (kt >> 1) & 1)) || *abort_flag) { ok = false; break; }
@@ -851,10 +849,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) {
           mma_commit(agg_bar);
-#ifdef JK_PHASE_PROFILE
-          atomicAdd(&g_phase[12], (unsigned long long)(clock64() - t_iss));
-#endif
-          ok = JK_PHASE_TIME(13, mbar_wait(agg_bar, 0));  // every MMA and commit retired before exit
+          JK_STAMP(12);
+          ok = mbar_wait(agg_bar, 0);  // every MMA and commit retired before the CTA exits
+          JK_STAMP(13);
         }
       }
       if (!ok) {
@@ -888,17 +885,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     int* ri = bufi + row * kStride;
     int g = 0;  // global iteration (tile x pass)
     bool ok = true;
-#ifdef JK_PHASE_PROFILE
-    long long t_prev = clock64();
-#endif
+    long long t_prev = 0;
+    (void)t_prev;
 
     // Loads this thread's 64 scores of iteration g into v; false on timeout / abort.
-    const int nbuf = score_buffers(p.heads);
+    const int nbuf = MH ? score_buffers(p.heads) : 2;
     auto load_tile = [&](uint32_t (&v)[2][32]) -> bool {
       const int buf = g % nbuf;
       if (!JK_PHASE_TIME(18, mbar_wait(&tfull[buf], (g / nbuf) & 1)) || *abort_flag) return false;
       tc_fence_after();
-      if (p.heads > 1) {
+      if (MH) {
         const uint32_t base = tmem + tbase + buf * p.heads * kCols;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -976,15 +972,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            // branch-free append: a failing column (or an overflowing one) goes to the
-            // row's junk slot kJunk
             const int col = col0 + c * 32 + e;
             const float x = __uint_as_float(v[c][e]);
-            const bool pass = static_cast<uint32_t>(col - lo_t) <= span && x >= th;
-            const int slot = (pass && myc < kCap) ? (half == 0 ? myc : kCap - 1 - myc) : kJunk;
-            rv[slot] = x;
-            ri[slot] = col;
-            myc += pass ? 1 : 0;
+            if (static_cast<uint32_t>(col - lo_t) <= span && x >= th) {
+              if (myc < kCap) {
+                const int slot = half == 0 ? myc : kCap - 1 - myc;
+                rv[slot] = x;
+                ri[slot] = col;
+              }
+              ++myc;
+            }
           }
       }
       (half == 0 ? cnt : nsel)[row] = myc;
@@ -1211,9 +1208,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ehi[16], elo[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) ehi[i] = elo[i] = 0u;
-#ifdef JK_PHASE_PROFILE
-            long long t_take = clock64();
-#endif
             while (static_cast<int>(nx.y >> 6) == kt) {
               const uint2 e = nx;
               ++cur;
@@ -1228,16 +1222,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 elo[i] |= (i == r) ? lb : 0u;
               }
             }
-#ifdef JK_PHASE_PROFILE
-            if (lane == 0) atomicAdd(&g_phase[14], (unsigned long long)(clock64() - t_take));
-            t_take = clock64();
-#endif
             tmem_st_32x32b_x16(lane_base + buf * 64, ehi);
             tmem_st_32x32b_x16(lane_base + buf * 64 + 32, elo);
             tmem_st_wait();
-#ifdef JK_PHASE_PROFILE
-            if (lane == 0) atomicAdd(&g_phase[15], (unsigned long long)(clock64() - t_take));
-#endif
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&e_full[buf]);
@@ -1284,6 +1271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
   }
   __syncthreads();
+  if (threadIdx.x == 0) JK_STAMP(9);
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -1305,7 +1293,7 @@ int launch_vt(const CUtensorMap& tr, const CUtensorMap& tc, const CUtensorMap& t
   constexpr int STAGES = KATOMS == 1 ? 4 : 1;
   constexpr int sm = Layout<KATOMS, STAGES>::kTotal;
   static_assert(sm <= 232448, "shared memory budget");
-  auto kern = topk_kernel<KATOMS, STAGES, MODE, VT>;
+  auto kern = p.heads > 1 ? topk_kernel<KATOMS, STAGES, MODE, VT, true> : topk_kernel<KATOMS, STAGES, MODE, VT, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) {
     cudaGetLastError();
     return JK_ERR_LAUNCH;
@@ -1572,13 +1560,9 @@ extern "C" int jk_transition_pairwise_topk_forward_mh(const void* src_proj, cons
 }
 
 #ifdef JK_PHASE_PROFILE
-extern "C" int jk_debug_phase(unsigned long long* out, int reset) {
+extern "C" int jk_debug_trace(long long* out, int n_ctas) {
   cudaDeviceSynchronize();
-  cudaMemcpyFromSymbol(out, jk::topk::g_phase, sizeof(unsigned long long) * 24);
-  if (reset) {
-    unsigned long long z[24] = {0};
-    cudaMemcpyToSymbol(jk::topk::g_phase, z, sizeof(z));
-  }
-  return 0;
+  const int n = n_ctas < jk::topk::kTraceCtas ? n_ctas : jk::topk::kTraceCtas;
+  return cudaMemcpyFromSymbol(out, jk::topk::g_trace, sizeof(long long) * 16 * n) == cudaSuccess ? 0 : -1;
 }
 #endif
