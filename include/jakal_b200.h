@@ -99,6 +99,14 @@ int jk_lowrank_project(const void* x, int64_t rows, int64_t dim, const void* w, 
                        const void* core, float temperature, int dtype, void* out,
                        int64_t out_stride, jk_stream_t stream);
 
+/* The target and source projections of a propagation in one pass over x (rank <= 64,
+ * bf16 / f16): out = round(x . w^T) and out2 = round(round(x . w2^T) * core) [/ T], each
+ * [rows, 64]; one N = 128 GEMM against w and w2 stacked. Replaces the two matmuls of
+ * jakal_net_native.cpp:6236-6239 (same rounding points as jk_lowrank_project). */
+int jk_lowrank_project_pair(const void* x, int64_t rows, int64_t dim, const void* w, const void* w2,
+                            int64_t rank, const void* core, float temperature, int dtype, void* out,
+                            void* out2, jk_stream_t stream);
+
 /*
  * Fused per-row top-k aggregate (tcgen05 score GEMM + streaming top-k + gather):
  *   score[b,t,s] = row_proj[b,t,:] . col_proj[b,s,:]              (f32 accumulation)

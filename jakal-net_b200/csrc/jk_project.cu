@@ -27,7 +27,7 @@ __device__ long long g_ptrace[1024][16];
 #endif
 
 constexpr int kRows = 128;
-constexpr int kStages = 4;
+constexpr int kStages = 6;  // a whole 384-wide row of x in flight: one HBM latency, not two
 constexpr int kThreads = 160;
 
 struct Params {
@@ -54,10 +54,15 @@ __device__ __forceinline__ float round16(float x) {
 // unrolled over every column of a row, and per-element runtime branches over all variants
 // made that straight-line code several times larger -- instruction fetch, not arithmetic,
 // then dominated the kernel.
-template <int RP, bool BF16, bool CORE, bool TEMP>
+// PAIR: one x tile against two weights (w then w2, rank <= 64 each, stacked into one N = 128
+// operand): columns 0-63 are the plain projection (out), 64-127 the core / temperature one
+// (out2) -- the target and source projections of a propagation in one pass over x.
+template <int RP, bool BF16, bool CORE, bool TEMP, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     project_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                   const __grid_constant__ CUtensorMap tm_out, Params p) {
+                   const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_out,
+                   const __grid_constant__ CUtensorMap tm_out2, Params p) {
+  static_assert(!PAIR || RP == 128, "a pair projection is one N = 128 GEMM");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kABytes = a_bytes();
@@ -103,6 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       prefetch_tmap(&tm_x);
       prefetch_tmap(&tm_w);
+      if (PAIR) prefetch_tmap(&tm_w2);
       const uint32_t idesc = idesc_f16(128, RP, p.bf16 ? 1u : 0u);
       bool ok = true;
       // Prefill.
@@ -112,6 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full[c], kStageBytes);
         tma_load_3d(st, &tm_x, &full[c], c * 64, static_cast<int>(row0), 0);
         tma_load_3d(st + kABytes, &tm_w, &full[c], c * 64, 0, 0);
+        if (PAIR) tma_load_3d(st + kABytes + 64 * 128, &tm_w2, &full[c], c * 64, 0, 0);
       }
       for (int c = 0; c < nchunks && ok; ++c) {
         const int s = c % kStages;
@@ -135,6 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[sp], kStageBytes);
           tma_load_3d(st, &tm_x, &full[sp], (cp + kStages) * 64, static_cast<int>(row0), 0);
           tma_load_3d(st + kABytes, &tm_w, &full[sp], (cp + kStages) * 64, 0, 0);
+          if (PAIR) tma_load_3d(st + kABytes + 64 * 128, &tm_w2, &full[sp], (cp + kStages) * 64, 0, 0);
         }
       }
       if (ok) {
@@ -171,10 +179,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           float f[2];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int c = cb + i + h;
+            const int c = PAIR ? (cb + i + h) & 63 : cb + i + h;
+            const bool weighted = !PAIR || cb >= 64;  // a pair's plain half takes no core / 1/T
             float x = round16<BF16>(__uint_as_float(v[i + h]));
-            if (CORE) x = round16<BF16>(x * core_s[c]);
-            if (TEMP) x = round16<BF16>(x / p.temperature);
+            if (CORE && weighted) x = round16<BF16>(x * core_s[c]);
+            if (TEMP && weighted) x = round16<BF16>(x / p.temperature);
             f[h] = c < p.rank ? x : 0.f;
           }
           if (BF16) {
@@ -199,7 +208,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
       if (threadIdx.x == 0) {
 #pragma unroll
-        for (int bx = 0; bx < RP / 64; ++bx) tma_store_3d(&tm_out, stage + bx * kRows * 128, bx * 64, static_cast<int>(row0), 0);
+        for (int bx = 0; bx < RP / 64; ++bx) {
+          if (PAIR)
+            tma_store_3d(bx == 0 ? &tm_out : &tm_out2, stage + bx * kRows * 128, 0, static_cast<int>(row0), 0);
+          else
+            tma_store_3d(&tm_out, stage + bx * kRows * 128, bx * 64, static_cast<int>(row0), 0);
+        }
         bulk_commit_group();
         bulk_wait_group_read0();
       }
@@ -220,16 +234,16 @@ constexpr int smem_bytes() {
   return 1024 + kStages * (a_bytes() + RP * 128) + 256;
 }
 
-template <int RP, bool BF16, bool CORE, bool TEMP>
+template <int RP, bool BF16, bool CORE, bool TEMP, bool PAIR = false>
 int launch_one(dim3 grid, cudaStream_t s, const CUtensorMap& tm_x, const CUtensorMap& tm_w, const CUtensorMap& tm_out,
-               const Params& p) {
+               const Params& p, const CUtensorMap* tm_w2 = nullptr, const CUtensorMap* tm_out2 = nullptr) {
   constexpr int sm = smem_bytes<RP>();
-  auto kern = project_kernel<RP, BF16, CORE, TEMP>;
+  auto kern = project_kernel<RP, BF16, CORE, TEMP, PAIR>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm) != cudaSuccess) {
     cudaGetLastError();
     return JK_ERR_LAUNCH;
   }
-  kern<<<grid, kThreads, sm, s>>>(tm_x, tm_w, tm_out, p);
+  kern<<<grid, kThreads, sm, s>>>(tm_x, tm_w, tm_w2 ? *tm_w2 : tm_w, tm_out, tm_out2 ? *tm_out2 : tm_out, p);
   return JK_OK;
 }
 
@@ -284,6 +298,42 @@ extern "C" int jk_lowrank_project(const void* x, int64_t rows, int64_t dim, cons
     st = proj::dispatch<64>(variant, grid, s, tm_x, tm_w, tm_out, p);
   } else {
     st = proj::dispatch<128>(variant, grid, s, tm_x, tm_w, tm_out, p);
+  }
+  if (st != JK_OK) return st;
+  return launch_status();
+}
+
+extern "C" int jk_lowrank_project_pair(const void* x, int64_t rows, int64_t dim, const void* w, const void* w2,
+                                       int64_t rank, const void* core, float temperature, int dtype, void* out,
+                                       void* out2, jk_stream_t stream) {
+  using namespace jk;
+  if (x == nullptr || w == nullptr || w2 == nullptr || out == nullptr || out2 == nullptr) return JK_ERR_BAD_ARG;
+  if (dtype != JK_BF16 && dtype != JK_F16) return JK_ERR_BAD_DTYPE;
+  if (rows <= 0 || dim <= 0 || rank <= 0 || rank > 64 || dim % 8 != 0) return JK_ERR_BAD_SHAPE;
+  if (rows > (int64_t(1) << 31) - 256 || dim > (int64_t(1) << 30)) return JK_ERR_BAD_SHAPE;
+  if (!(temperature > 0.f)) return JK_ERR_BAD_ARG;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(w2) || !aligned16(out) || !aligned16(out2)) return JK_ERR_ALIGNMENT;
+  int st = check_device();
+  if (st != JK_OK) return st;
+  const bool bf16 = dtype == JK_BF16;
+  CUtensorMap tm_x, tm_w, tm_w2, tm_out, tm_out2;
+  if ((st = make_tmap_3d_16bit(&tm_x, x, dim, rows, 1, 64, 128, bf16)) != JK_OK) return st;
+  if ((st = make_tmap_3d_16bit(&tm_w, w, dim, rank, 1, 64, 64, bf16)) != JK_OK) return st;
+  if ((st = make_tmap_3d_16bit(&tm_w2, w2, dim, rank, 1, 64, 64, bf16)) != JK_OK) return st;
+  if ((st = make_tmap_3d_16bit(&tm_out, out, 64, rows, 1, 64, 128, bf16)) != JK_OK) return st;
+  if ((st = make_tmap_3d_16bit(&tm_out2, out2, 64, rows, 1, 64, 128, bf16)) != JK_OK) return st;
+  proj::Params p{rows, dim, rank, 64, core, temperature, bf16 ? 1 : 0, out};
+  const dim3 grid(static_cast<unsigned>((rows + 127) / 128));
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const bool c = core != nullptr, t = temperature != 1.f;
+  if (bf16) {
+    if (c && !t) st = proj::launch_one<128, true, true, false, true>(grid, s, tm_x, tm_w, tm_out, p, &tm_w2, &tm_out2);
+    else if (c) st = proj::launch_one<128, true, true, true, true>(grid, s, tm_x, tm_w, tm_out, p, &tm_w2, &tm_out2);
+    else st = proj::launch_one<128, true, false, true, true>(grid, s, tm_x, tm_w, tm_out, p, &tm_w2, &tm_out2);
+  } else {
+    if (c && !t) st = proj::launch_one<128, false, true, false, true>(grid, s, tm_x, tm_w, tm_out, p, &tm_w2, &tm_out2);
+    else if (c) st = proj::launch_one<128, false, true, true, true>(grid, s, tm_x, tm_w, tm_out, p, &tm_w2, &tm_out2);
+    else st = proj::launch_one<128, false, false, true, true>(grid, s, tm_x, tm_w, tm_out, p, &tm_w2, &tm_out2);
   }
   if (st != JK_OK) return st;
   return launch_status();

@@ -47,7 +47,7 @@ namespace topk {
 // Debug-only timeline: clock64 stamps of the phase boundaries of every CTA, stored by one
 // thread (no atomics, so the timeline is not perturbed). Slot 0 = start, 15 = SM id.
 constexpr int kTraceCtas = 4096;
-__device__ long long g_trace[kTraceCtas][16];
+__device__ long long g_trace[kTraceCtas][24];
 #define JK_STAMP(i)                                                                  \
   do {                                                                               \
     const int _cta = blockIdx.y * gridDim.x + blockIdx.x;                            \
@@ -87,7 +87,6 @@ enum Mode { kGather = 0, kScatter = 1 };
 constexpr int kEK = 64;       // source rows per edge tile (MMA K)
 constexpr int kVSlice = 128;  // value columns per slice (MMA N)
 constexpr int kVBufs = 4;     // value-slice buffers (16 KB each)
-constexpr int kElStride = 65;  // 8-byte entries per row of the per-half edge lists (64 + pad)
 constexpr int kOCols = 384;   // TMEM columns of the aggregate's accumulator O (dim <= 384)
 // Edge tiles live in TMEM behind O: buffer e, plane q (hi / lo) at column
 // kOCols + e * 64 + q * 32; a row's 64 K elements are 32 columns of bf16 / f16 pairs.
@@ -588,7 +587,9 @@ __device__ __forceinline__ void sel_barrier() {
   asm volatile("bar.sync 1, %0;" ::"r"(kSelWarps * 32) : "memory");
 }
 
-// Source window of a CTA's tensor-core aggregate: rows [s_lo, s_lo + n) of the values.
+// Source window of a CTA's tensor-core aggregate: rows [s_lo, s_lo + n) of the values,
+// s_lo on the score-tile grid, so that 64-row source tile kt is the first (even kt) or the
+// second (odd kt) half of a score tile -- the columns of candidate stack 0 or 1.
 // Taken when the CTA's sources form a window of at most 1024 rows of 16-bit values whose
 // width fits the TMEM accumulator beside the edge tiles (identical in every thread).
 struct SlabRange {
@@ -601,7 +602,7 @@ __device__ __forceinline__ SlabRange slab_range(const Params& p, int64_t t0) {
   SlabRange r{0, 0, false};
   if (p.slab_ok && p.window >= 0 && sizeof(VT) == 2 && (p.dim % 64) == 0) {
     const int64_t lo = t0 - p.window;
-    r.s_lo = lo > 0 ? static_cast<int>(lo) : 0;
+    r.s_lo = static_cast<int>((lo > 0 ? lo : 0) / kCols * kCols);  // on the score-tile grid
     int64_t hi_col = t0 + kRows - 1;
     if (hi_col > p.n_cols - 1) hi_col = p.n_cols - 1;
     r.n = static_cast<int>(hi_col - r.s_lo + 1);
@@ -616,9 +617,9 @@ struct Layout {
   static constexpr int kAtomBytes = kRows * 128;  // 128 rows x 64 (16-bit) elements
   static constexpr int kABytes = KATOMS * kAtomBytes;
   static constexpr int kBBytes = KATOMS * kAtomBytes;
-  // A + ring; reused by the selection scratch and the aggregate's per-half edge lists
-  static constexpr int kRegion0 = kABytes + STAGES * kBBytes > kRows * kElStride * 8 ? kABytes + STAGES * kBBytes
-                                                                                     : kRows * kElStride * 8;
+  // A + ring; reused by the selection scratch, then by the aggregate's value buffers
+  static constexpr int kRegion0 = kABytes + STAGES * kBBytes;
+  static_assert(kRegion0 >= kVBufs * 16384, "the aggregate's value buffers reuse region 0");
   static constexpr int kBufBytes = 2 * kRows * kStride * 4;    // candidate values + indices
   static constexpr int kRowArrays = 10 * kRows * 4;            // per-row scalars
   static constexpr int kBarBytes = 320;
@@ -692,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&vb_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&e_full[i], kSelWarps);
+      mbar_init(&e_full[i], kSelWarps / 2);  // the four warps of one half build a tile
       mbar_init(&e_empty[i], 1);
     }
     for (int i = 0; i < STAGES; ++i) {
@@ -759,7 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const SlabRange sr = slab_range<VT>(p, t0);
         const int nkt = (sr.n + kEK - 1) / kEK;
         const int nsl = static_cast<int>((p.dim + kVSlice - 1) / kVSlice);
-        uint8_t* vbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bufi) + 1023) & ~uintptr_t(1023));
+        uint8_t* vbuf = smem;  // region 0: the score operands are consumed by now
         for (int pi = 0; pi < nkt * nsl && ok; ++pi) {
           const int vb = pi % kVBufs;
           if (pi >= kVBufs && !JK_PHASE_TIME(10, mbar_wait(&vb_empty[vb], ((pi - kVBufs) / kVBufs) & 1))) {
@@ -822,7 +823,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const SlabRange sr = slab_range<VT>(p, t0);
         const int nkt = (sr.n + kEK - 1) / kEK;
         const int nsl = static_cast<int>((p.dim + kVSlice - 1) / kVSlice);
-        uint8_t* vbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bufi) + 1023) & ~uintptr_t(1023));
+        uint8_t* vbuf = smem;
         JK_STAMP(11);
         for (int kt = 0; kt < nkt && ok; ++kt) {
           const int buf = kt & 1;
@@ -1102,7 +1103,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.out_index) p.out_index[o + r] = e < n ? static_cast<int64_t>(F.idx(e)) : -1;
         }
       }
+      if (threadIdx.x == 0) JK_STAMP(16);
       compress_row(F, n, p.compress);
+      if (threadIdx.x == 0) JK_STAMP(17);
       if (MODE == kGather && row_ok && good) {
         const int64_t cb = b * p.n_cols;
         float acc = 0.f;
@@ -1125,37 +1128,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         st_elem(p.out_state, b * p.n_rows + t, p.out_dtype, acc);
+        if (threadIdx.x == 0) JK_STAMP(18);
       }
       if (tc_agg) {
-        // Per-half edge lists of the tensor-core aggregate (region 0, kElStride entries
-        // per row): the two ascending column runs are merged, and every edge goes to the
-        // list of the source-tile half it falls in (bit 5 of its window-relative column):
-        // half 0 from entry 0 upwards, half 1 from entry 63 downwards, both ascending.
-        // Entry = (bf16 / f16 hi | lo << 16, window-relative column).
-        constexpr bool kHalfV = std::is_same<VT, __half>::value;
-        uint2* el = reinterpret_cast<uint2*>(smem) + row * kElStride;
-        const int m0 = cnt[row];
-        int a = 0, c = m0, l0 = 0, l1 = 0;
-        for (int e = 0; e < n; ++e) {
-          const bool from0 = a < m0 && (c >= n || F.idx(a) < F.idx(c));
-          const int s = from0 ? a++ : c++;
-          const float w = F.val(s);
-          const int rel = F.idx(s) - sr.s_lo;
-          uint32_t hb, lb;
-          if (kHalfV) {
-            const __half h = __float2half_rn(w);
-            hb = __half_as_ushort(h);
-            lb = __half_as_ushort(__float2half_rn(w - __half2float(h)));
-          } else {
-            const __nv_bfloat16 h = __float2bfloat16_rn(w);
-            hb = __bfloat16_as_ushort(h);
-            lb = __bfloat16_as_ushort(__float2bfloat16_rn(w - __bfloat162float(h)));
-          }
-          const uint2 ent = make_uint2(hb | (lb << 16), static_cast<uint32_t>(rel));
-          if (rel & 32) el[63 - l1++] = ent;
-          else el[l0++] = ent;
-        }
-        cnt[row] = l0;  // list 0 length; list 1 holds n - l0
+        // the tensor-core aggregate reads the weights and columns in place
       } else if (MODE == kGather) {
         // Pack (weight, column) pairs for the gather, back to front so that every write
         // lands on an already consumed candidate slot of the same row.
@@ -1182,52 +1158,73 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (MODE == kGather) {
         if (tc_agg) {
           // Tensor-core aggregate over the CTA's source window. For every 64-row source
-          // tile the selected edges of the 128 target rows form a sparse 128 x 64 matrix E
-          // (bf16 / f16 hi + lo planes), double-buffered in TMEM as the MMA's A operand:
-          // each thread packs its row's half (32 source rows) of the tile from the row's
-          // column-ordered edges in registers and stores it (tcgen05.st, thread = TMEM
-          // lane = row), then its warp signals e_full. The MMA warp forms
-          // O[128 x dim] += E_hi.V + E_lo.V in TMEM with V streamed through shared memory.
-          // The hi + lo planes keep the edge weights to ~16 bits.
+          // tile kt the selected edges of the 128 target rows form a sparse 128 x 64 matrix
+          // E (bf16 / f16 hi + lo planes), in TMEM as the MMA's A operand. Tile kt lies in
+          // half kt & 1 of a score tile, so its columns are exactly the candidates the
+          // selection half kt & 1 collected: the four warps of that half build it, from
+          // their rows' run of survivors (ascending columns), into buffer kt & 1 (thread =
+          // TMEM lane = row), and signal e_full; the two halves build alternate tiles. The
+          // MMA warp forms O[128 x dim] += E_hi.V + E_lo.V. The hi + lo planes keep the
+          // edge weights to ~16 bits.
+          constexpr bool kHalfV = std::is_same<VT, __half>::value;
           const int nkt = (sr.n + kEK - 1) / kEK;
-          // this thread's edge list (ascending window-relative columns)
-          const uint2* el = reinterpret_cast<const uint2*>(smem) + row * kElStride;
-          const int len = half == 0 ? cnt[row] : nsel[row] - cnt[row];
-          auto entry = [&](int i) { return el[half == 0 ? i : 63 - i]; };
-          int cur = 0;
-          uint2 nx = len > 0 ? entry(0) : make_uint2(0u, 0x7FFFFFFFu);
-          const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + kOCols + half * 16;
-          for (int kt = 0; kt < nkt; ++kt) {
-            const int buf = kt & 1;
-            if (kt >= 2 && !JK_PHASE_TIME(11, mbar_wait(&e_empty[buf], ((kt >> 1) - 1) & 1))) {
+          const int n = nsel[row];
+          const int m0 = cnt[row];
+          // rows of the exact fallback pass hold one sorted run, filtered by tile parity
+          const bool runs = failrow[row] == 0;
+          int cur = runs && half == 1 ? m0 : 0;
+          const int end = runs && half == 0 ? m0 : n;
+          auto next_rel = [&]() -> int {  // window-relative column of the next entry of this half
+            while (cur < end) {
+              const int rel = ri[cur] - sr.s_lo;
+              if (((rel >> 6) & 1) == half) return rel;
+              ++cur;
+            }
+            return INT_MAX;
+          };
+          int rel = next_rel();
+          const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + kOCols + half * 64;
+          for (int kt = half, use = 0; kt < nkt; kt += 2, ++use) {
+            if (use >= 1 && !mbar_wait(&e_empty[half], (use - 1) & 1)) {
               atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
               *abort_flag = 1;
             }
             if (*abort_flag) break;
             tc_fence_after();
-            uint32_t ehi[16], elo[16];
+            uint32_t ehi[32], elo[32];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) ehi[i] = elo[i] = 0u;
-            while (static_cast<int>(nx.y >> 6) == kt) {
-              const uint2 e = nx;
-              ++cur;
-              nx = cur < len ? entry(cur) : make_uint2(0u, 0x7FFFFFFFu);  // prefetch the next
-              const int kin = static_cast<int>(e.y & 31);
+            for (int i = 0; i < 32; ++i) ehi[i] = elo[i] = 0u;
+            while ((rel >> 6) == kt) {
+              const float w = rv[cur];
+              const int kin = rel & 63;
+              uint32_t hb, lb;
+              if (kHalfV) {
+                const __half h = __float2half_rn(w);
+                hb = __half_as_ushort(h);
+                lb = __half_as_ushort(__float2half_rn(w - __half2float(h)));
+              } else {
+                const __nv_bfloat16 h = __float2bfloat16_rn(w);
+                hb = __bfloat16_as_ushort(h);
+                lb = __bfloat16_as_ushort(__float2bfloat16_rn(w - __bfloat162float(h)));
+              }
               const int sh = (kin & 1) * 16;
               const int r = kin >> 1;
-              const uint32_t hb = (e.x & 0xFFFFu) << sh, lb = (e.x >> 16) << sh;
+              hb <<= sh;
+              lb <<= sh;
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+              for (int i = 0; i < 32; ++i) {
                 ehi[i] |= (i == r) ? hb : 0u;
                 elo[i] |= (i == r) ? lb : 0u;
               }
+              ++cur;
+              rel = next_rel();
             }
-            tmem_st_32x32b_x16(lane_base + buf * 64, ehi);
-            tmem_st_32x32b_x16(lane_base + buf * 64 + 32, elo);
+            tmem_st_32x32b_x32(lane_base, ehi);
+            tmem_st_32x32b_x32(lane_base + 32, elo);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&e_full[buf]);
+            if (lane == 0) mbar_arrive(&e_full[half]);
           }
           JK_PHASE_MARK(6, t_prev);
           if (!*abort_flag && !mbar_wait(agg_bar, 0)) {
@@ -1563,6 +1560,6 @@ extern "C" int jk_transition_pairwise_topk_forward_mh(const void* src_proj, cons
 extern "C" int jk_debug_trace(long long* out, int n_ctas) {
   cudaDeviceSynchronize();
   const int n = n_ctas < jk::topk::kTraceCtas ? n_ctas : jk::topk::kTraceCtas;
-  return cudaMemcpyFromSymbol(out, jk::topk::g_trace, sizeof(long long) * 16 * n) == cudaSuccess ? 0 : -1;
+  return cudaMemcpyFromSymbol(out, jk::topk::g_trace, sizeof(long long) * 24 * n) == cudaSuccess ? 0 : -1;
 }
 #endif

@@ -35,6 +35,7 @@ __all__ = [
     "transition_query_topk",
     "transition_pairwise_topk",
     "lowrank_project",
+    "lowrank_project_pair",
     "topk_aggregate",
     "JakalB200Error",
 ]
@@ -171,6 +172,31 @@ def lowrank_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None,
     return out.reshape(*x.shape[:-1], rp)
 
 
+def lowrank_project_pair(x: Tensor, weight: Tensor, weight2: Tensor, core: Optional[Tensor] = None,
+                         temperature: float = 1.0) -> tuple[Tensor, Tensor]:
+    """(lowrank_project(x, weight), lowrank_project(x, weight2, core, temperature)) in one
+    pass over x (jk_lowrank_project_pair): bf16 / f16 x, rank <= 64; other cases take the
+    two separate projections."""
+    _require_cuda("x", x)
+    rank, dim = weight.shape
+    if (x.dtype == torch.float32 or rank > 64 or tuple(weight2.shape) != (rank, dim) or x.shape[-1] != dim):
+        return lowrank_project(x, weight), lowrank_project(x, weight2, core=core, temperature=temperature)
+    x2 = x.reshape(-1, dim).contiguous()
+    w = weight.detach().to(device=x.device, dtype=x.dtype).contiguous()
+    w2 = weight2.detach().to(device=x.device, dtype=x.dtype).contiguous()
+    c = None if core is None else core.detach().reshape(-1).to(device=x.device, dtype=x.dtype).contiguous()
+    out = torch.empty((x2.shape[0], 64), device=x.device, dtype=x.dtype)
+    out2 = torch.empty((x2.shape[0], 64), device=x.device, dtype=x.dtype)
+    with torch.cuda.device(x.device):
+        check(
+            _LIBRARY.jk_lowrank_project_pair(x2.data_ptr(), x2.shape[0], dim, w.data_ptr(), w2.data_ptr(), rank, _ptr(c),
+                                             float(temperature), _proj_dtype(x), out.data_ptr(), out2.data_ptr(),
+                                             _stream(x.device)),
+            "jk_lowrank_project_pair",
+        )
+    return out.reshape(*x.shape[:-1], 64), out2.reshape(*x.shape[:-1], 64)
+
+
 def _bias_tensor(bias: Optional[Tensor], device: torch.device, scale: float = 1.0) -> Optional[Tensor]:
     if bias is None:
         return None
@@ -254,8 +280,11 @@ def _pair_scorer(kind: str, weight: Tensor, bias, in_weight, in_bias, out_weight
     if in_bias is not None or out_bias is not None:
         raise RuntimeError("Low-rank bilinear projections take no bias.")
     if kind == "low_rank_bilinear":
-        row_proj = lowrank_project(target_val, out_weight)                # target side
-        col_proj = lowrank_project(source_val, in_weight, core=weight)    # source side, * w_hat
+        if target_val is source_val:  # propagation: both projections in one pass over the values
+            row_proj, col_proj = lowrank_project_pair(target_val, out_weight, in_weight, core=weight)
+        else:
+            row_proj = lowrank_project(target_val, out_weight)                # target side
+            col_proj = lowrank_project(source_val, in_weight, core=weight)    # source side, * w_hat
         return row_proj, col_proj, _bias_tensor(bias, target_val.device), None
     prefix, base = "multihead_", "_low_rank_bilinear"
     agg = kind[len(prefix):-len(base)] if kind.startswith(prefix) and kind.endswith(base) else None

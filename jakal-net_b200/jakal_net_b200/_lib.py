@@ -48,6 +48,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "jk_device_status": (_i32, [_p, ctypes.POINTER(_i32)]),
     "jk_padded_rank": (_i64, [_i64]),
     "jk_lowrank_project": (_i32, [_p, _i64, _i64, _p, _i64, _p, _f32, _i32, _p, _i64, _p]),
+    "jk_lowrank_project_pair": (_i32, [_p, _i64, _i64, _p, _p, _i64, _p, _f32, _i32, _p, _p, _p]),
     "jk_propagation_topk_forward": (
         _i32,
         [_p, _p, _i64, _i64, _i64, _i64, _i32,  # row_proj, col_proj, B, n_rows, n_cols, rp, proj_dtype

@@ -165,3 +165,19 @@ def test_topk_bimodal_scores(dev):
     val[:, ::7] *= 12.0
     ties = _check_given(dev, val, k=32, window=-1)
     assert ties.mean() < 0.05
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rank,core,temperature", [(64, True, 1.0), (40, True, 0.7), (17, False, 1.0)])
+def test_pair_projection_equals_two_projections(dev, dtype, rank, core, temperature):
+    import jakal_net_b200 as jk
+
+    g = torch.Generator().manual_seed(rank)
+    rows, dim = 1000, 192
+    x = torch.randn(rows, dim, generator=g).to(dev, dtype)
+    w = (torch.randn(rank, dim, generator=g) / dim ** 0.5).to(dev, dtype)
+    w2 = (torch.randn(rank, dim, generator=g) / dim ** 0.5).to(dev, dtype)
+    c = (torch.rand(rank, generator=g) + 0.5).to(dev, dtype) if core else None
+    a, b = jk.lowrank_project_pair(x, w, w2, core=c, temperature=temperature)
+    assert torch.equal(a, jk.lowrank_project(x, w))
+    assert torch.equal(b, jk.lowrank_project(x, w2, core=c, temperature=temperature))
