@@ -40,8 +40,8 @@ METRIC = "fused propagation Gpairs/s"
 UNIT = "Gpairs/s"
 WORKLOAD = "config2: SparsePropagation causal window 512 intersect top-k 32, B8 N2048 D384 R64, bf16, softsign"
 # dram__bytes_read.sum + dram__bytes_write.sum of one fused-kernel launch on this workload,
-# from the ncu capture summarised in profiles/topk_kernel_config2.md (None until captured).
-NCU_TRAFFIC_BYTES = None
+# from the ncu capture summarised in profiles/topk_kernel_config2.md.
+NCU_TRAFFIC_BYTES = 16955392  # 16.96 MB read + 0 B written (outputs stay in L2), one launch
 
 
 def pairs_per_batch_item(n: int, window: int) -> int:
