@@ -490,8 +490,9 @@ __device__ __forceinline__ int key_idx(unsigned long long key) {
 
 
 // Rank selection: the row's n candidates (logical order: half-0 stack, then half-1 stack)
-// become 64-bit keys in the warp's scratch ks; every lane counts, for its NQ keys, how many
-// keys of the row beat them (broadcast reads, independent compares: no shuffle chains).
+// become keys in the warp's scratch ks; every lane counts, for its NQ keys, how many keys
+// of the row beat them (broadcast reads, independent compares: no shuffle chains) -- on the
+// 32-bit scores, or on 64-bit keys (score, then lower column) when the row has exact ties.
 // Keys are unique (distinct columns), so the best min(k, real) keys have ranks 0 .. k-1.
 // The survivors are written back in column order, as two ascending runs: when the stacks
 // hold columns in ascending order (`runs`: the threshold pass appends them that way),
@@ -504,37 +505,70 @@ template <int NQ>
 __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int lane, unsigned long long* ks,
                                 bool runs, int& m0) {
   const int n = c0 + c1;
+  const int n4 = (n + 3) & ~3;
   const unsigned long long kNone = make_key(-INFINITY, kSentinel);
   unsigned long long x[NQ];
+  uint32_t u[NQ];  // orderable score, 0 = no candidate (below every real score)
   int rank[NQ];
+  uint32_t* ku = reinterpret_cast<uint32_t*>(ks);
 #pragma unroll
   for (int q = 0; q < NQ; ++q) {
     const int i = q * 32 + lane;
     const int e = i < c0 ? i : kCap - 1 - (i - c0);
-    x[q] = (i < n && ri[e] != kSentinel) ? make_key(rv[e], ri[e]) : kNone;
-    if (i < n) ks[i] = x[q];
+    const bool real_i = i < n && ri[e] != kSentinel;
+    x[q] = real_i ? make_key(rv[e], ri[e]) : kNone;
+    u[q] = real_i ? static_cast<uint32_t>(x[q] >> 32) : 0u;
+    if (i < n4) ku[i] = u[q];
     rank[q] = 0;
   }
   __syncwarp();  // from here on rv / ri of the row are free: every lane holds its keys
-  int j = 0;
-  for (; j + 4 <= n; j += 4) {
-    const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(ks + j);
-    const ulonglong2 c = *reinterpret_cast<const ulonglong2*>(ks + j + 2);
+#ifdef JK_PHASE_PROFILE
+  long long tq0 = clock64();
+#endif
+  // Rank on the 32-bit scores (four keys per 16-byte broadcast read) ...
+  for (int j = 0; j < n4; j += 4) {
+    const uint4 a = *reinterpret_cast<const uint4*>(ku + j);
 #pragma unroll
-    for (int q = 0; q < NQ; ++q)
-      rank[q] += (a.x > x[q]) + (a.y > x[q]) + (c.x > x[q]) + (c.y > x[q]);
+    for (int q = 0; q < NQ; ++q) rank[q] += (a.x > u[q]) + (a.y > u[q]) + (a.z > u[q]) + (a.w > u[q]);
   }
-  for (; j < n; ++j) {
-    const unsigned long long a = ks[j];
+  // ... which is exact unless two candidates tie on the score: the ranks of the real keys are
+  // then not a permutation of 0 .. real-1 (tied keys share a rank), and the row is ranked
+  // again on the 64-bit keys (score, then lower column).
+  int real = 0, rsum = 0;
 #pragma unroll
-    for (int q = 0; q < NQ; ++q) rank[q] += a > x[q];
+  for (int q = 0; q < NQ; ++q) {
+    real += __popc(__ballot_sync(0xffffffffu, x[q] != kNone));
+    rsum += x[q] != kNone ? rank[q] : 0;
   }
-  int real = 0;
+  rsum = __reduce_add_sync(0xffffffffu, rsum);
+  if (rsum != real * (real - 1) / 2) {
+    __syncwarp();  // every lane has read the 32-bit keys
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int i = q * 32 + lane;
+      if (i < n) ks[i] = x[q];
+      rank[q] = 0;
+    }
+    __syncwarp();
+    int j = 0;
+    for (; j + 2 <= n; j += 2) {
+      const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(ks + j);
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) rank[q] += (a.x > x[q]) + (a.y > x[q]);
+    }
+    for (; j < n; ++j) {
+      const unsigned long long a = ks[j];
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) rank[q] += a > x[q];
+    }
+  }
+#ifdef JK_PHASE_PROFILE
+  long long tq1 = clock64();
+#endif
   bool keep[NQ];
   int col[NQ], slot[NQ];
 #pragma unroll
   for (int q = 0; q < NQ; ++q) {
-    real += __popc(__ballot_sync(0xffffffffu, x[q] != kNone));
     keep[q] = x[q] != kNone && rank[q] < k;
     col[q] = key_idx(x[q]);
   }
@@ -559,7 +593,8 @@ __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int l
       slot[q] = 0;
     }
     __syncwarp();
-    for (j = 0; j + 4 <= n; j += 4) {
+    int j = 0;
+    for (; j + 4 <= n; j += 4) {
       const int4 a = *reinterpret_cast<const int4*>(kc + j);
 #pragma unroll
       for (int q = 0; q < NQ; ++q) slot[q] += (a.x < col[q]) + (a.y < col[q]) + (a.z < col[q]) + (a.w < col[q]);
@@ -580,6 +615,15 @@ __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int l
     }
   }
   __syncwarp();
+#ifdef JK_PHASE_PROFILE
+  if (threadIdx.x == 0) {
+    const int cta = blockIdx.y * gridDim.x + blockIdx.x;
+    if (cta < kTraceCtas) {
+      g_trace[cta][19] += tq1 - tq0;
+      g_trace[cta][20] += clock64() - tq1;
+    }
+  }
+#endif
   return real < k ? real : k;
 }
 
@@ -719,7 +763,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
     const int cta = blockIdx.y * gridDim.x + blockIdx.x;
-    if (cta < kTraceCtas) g_trace[cta][15] = smid;
+    if (cta < kTraceCtas) {
+      g_trace[cta][15] = smid;
+      g_trace[cta][19] = g_trace[cta][20] = g_trace[cta][21] = 0;
+    }
   }
 #endif
 
@@ -1072,6 +1119,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c1 = nsel[rt];
         const int m = c0 + c1;
         const bool runs = failrow[rt] == 0;
+#ifdef JK_PHASE_PROFILE
+        if (threadIdx.x == 0 && blockIdx.y * gridDim.x + blockIdx.x < kTraceCtas)
+          g_trace[blockIdx.y * gridDim.x + blockIdx.x][21] += m;
+#endif
         n = m <= 32   ? warp_rank_select<1>(wv, wi, c0, c1, k, lane, ks, runs, m0)
             : m <= 64 ? warp_rank_select<2>(wv, wi, c0, c1, k, lane, ks, runs, m0)
             : m <= 96 ? warp_rank_select<3>(wv, wi, c0, c1, k, lane, ks, runs, m0)
