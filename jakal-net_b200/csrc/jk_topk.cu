@@ -108,6 +108,7 @@ struct Params {
   int compress;
   int state_dtype, val_dtype, out_dtype;
   int slab_ok;  // tm_val is valid (windowed gather of 16-bit values, dim % 64 == 0)
+  int tma_out;  // tm_out is valid: the tensor-core aggregate stores 16-bit outputs by TMA
   int split3;   // projections are the three-plane bf16 split of f32 values
   // multi-head scorer (heads > 1): head h owns K steps [h * kph, (h + 1) * kph) and its own
   // TMEM plane; the planes are combined (JK_HEADS_*) with head_bias as they are read
@@ -673,7 +674,8 @@ struct Layout {
 template <int KATOMS, int STAGES, int MODE, typename VT, bool MH>
 __global__ void __launch_bounds__(kThreads, 1)
     topk_kernel(const __grid_constant__ CUtensorMap tm_rows, const __grid_constant__ CUtensorMap tm_cols,
-                const __grid_constant__ CUtensorMap tm_val, Params p, uint32_t idesc) {
+                const __grid_constant__ CUtensorMap tm_val, const __grid_constant__ CUtensorMap tm_out, Params p,
+                uint32_t idesc) {
   using L = Layout<KATOMS, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -765,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int cta = blockIdx.y * gridDim.x + blockIdx.x;
     if (cta < kTraceCtas) {
       g_trace[cta][15] = smid;
-      g_trace[cta][19] = g_trace[cta][20] = g_trace[cta][21] = 0;
+      g_trace[cta][19] = g_trace[cta][20] = g_trace[cta][21] = g_trace[cta][22] = g_trace[cta][23] = 0;
     }
   }
 #endif
@@ -874,12 +876,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         JK_STAMP(11);
         for (int kt = 0; kt < nkt && ok; ++kt) {
           const int buf = kt & 1;
-          if (!JK_PHASE_TIME(8, mbar_wait(&e_full[buf], (kt >> 1) & 1)) || *abort_flag) { ok = false; break; }
+#ifdef JK_PHASE_PROFILE
+          const long long tw0 = clock64();
+#endif
+          if (!mbar_wait(&e_full[buf], (kt >> 1) & 1) || *abort_flag) { ok = false; break; }
+#ifdef JK_PHASE_PROFILE
+          g_trace[(blockIdx.y * gridDim.x + blockIdx.x) % kTraceCtas][22] += clock64() - tw0;
+#endif
           tc_fence_after();
           const uint32_t e_col = tmem + kOCols + buf * 64;
           for (int sl = 0; sl < nsl; ++sl) {
             const int pi = kt * nsl + sl, vb = pi % kVBufs;
-            if (!JK_PHASE_TIME(9, mbar_wait(&vb_full[vb], (pi / kVBufs) & 1))) { ok = false; break; }
+#ifdef JK_PHASE_PROFILE
+            const long long tw1 = clock64();
+#endif
+            if (!mbar_wait(&vb_full[vb], (pi / kVBufs) & 1)) { ok = false; break; }
+#ifdef JK_PHASE_PROFILE
+            g_trace[(blockIdx.y * gridDim.x + blockIdx.x) % kTraceCtas][23] += clock64() - tw1;
+#endif
             const int w = static_cast<int>(p.dim) - sl * kVSlice;
             const uint32_t idesc_pv = idesc_f16(kRows, w < kVSlice ? w : kVSlice, kHalfV ? 0u : 1u) | (1u << 16);
             const uint32_t v_addr = smem_u32(vbuf + vb * 16384);
@@ -1284,7 +1298,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           JK_PHASE_MARK(7, t_prev);
-          if (!*abort_flag) {
+          if (!*abort_flag && p.tma_out) {
+            // O -> 16-bit rows staged in the (now free) candidate buffers as 64-column boxes
+            // in the 128-byte-swizzled layout of tm_out, then stored by TMA (rows past
+            // n_rows are clipped). Thread = row, half = which half of the columns.
+            uint8_t* stg = reinterpret_cast<uint8_t*>(bufv);  // 1024-aligned, >= 96 KB
+            const int hcols = static_cast<int>(p.dim / 2);      // multiple of 32
+            const bool obf16 = p.out_dtype == JK_BF16;
+            for (int c0 = 0; c0 < hcols; c0 += 32) {
+              uint32_t v[32];
+              tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * hcols + c0, v);
+              tmem_ld_wait();
+              const int col = half * hcols + c0;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint32_t w4[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  const float a = __uint_as_float(v[8 * q + 2 * u]), c = __uint_as_float(v[8 * q + 2 * u + 1]);
+                  if (obf16) {
+                    __nv_bfloat162 h = __floats2bfloat162_rn(a, c);
+                    w4[u] = *reinterpret_cast<uint32_t*>(&h);
+                  } else {
+                    __half2 h = __floats2half2_rn(a, c);
+                    w4[u] = *reinterpret_cast<uint32_t*>(&h);
+                  }
+                }
+                const int cc = col + 8 * q;
+                const int chunk = (cc & 63) >> 3;
+                *reinterpret_cast<uint4*>(stg + (cc >> 6) * (kRows * 128) + (row >> 3) * 1024 + (row & 7) * 128 +
+                                          ((chunk ^ (row & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+              }
+            }
+            fence_proxy_async_smem();
+            sel_barrier();
+            if (threadIdx.x == 0) {
+              for (int bx = 0; bx < static_cast<int>(p.dim / 64); ++bx)
+                tma_store_3d(&tm_out, stg + bx * (kRows * 128), bx * 64, static_cast<int>(t0), static_cast<int>(b));
+              bulk_commit_group();
+              bulk_wait_group_read0();
+            }
+          } else if (!*abort_flag) {
             // O -> outputs (thread = row; half = which half of the columns)
             const int hcols = static_cast<int>(p.dim / 2);  // multiple of 32
             for (int c0 = 0; c0 < hcols; c0 += 32) {
@@ -1336,7 +1390,8 @@ __global__ void finalize_scatter(const float* acc_state, const float* acc_val, i
 }
 
 template <int KATOMS, int MODE, typename VT>
-int launch_vt(const CUtensorMap& tr, const CUtensorMap& tc, const CUtensorMap& tv, const Params& p, int64_t batch,
+int launch_vt(const CUtensorMap& tr, const CUtensorMap& tc, const CUtensorMap& tv, const CUtensorMap& to,
+              const Params& p, int64_t batch,
               uint32_t idesc, cudaStream_t st) {
   constexpr int STAGES = KATOMS == 1 ? 4 : 1;
   constexpr int sm = Layout<KATOMS, STAGES>::kTotal;
@@ -1347,24 +1402,25 @@ int launch_vt(const CUtensorMap& tr, const CUtensorMap& tc, const CUtensorMap& t
     return JK_ERR_LAUNCH;
   }
   const dim3 grid(static_cast<unsigned>((p.row_count + kRows - 1) / kRows), static_cast<unsigned>(batch));
-  kern<<<grid, kThreads, sm, st>>>(tr, tc, tv, p, idesc);
+  kern<<<grid, kThreads, sm, st>>>(tr, tc, tv, to, p, idesc);
   return launch_status();
 }
 
 template <int KATOMS, int MODE>
-int launch_k(const CUtensorMap& tr, const CUtensorMap& tc, const CUtensorMap& tv, const Params& p, int64_t batch,
+int launch_k(const CUtensorMap& tr, const CUtensorMap& tc, const CUtensorMap& tv, const CUtensorMap& to,
+             const Params& p, int64_t batch,
              uint32_t idesc, cudaStream_t st) {
   switch (p.val_dtype) {
-    case JK_F32: return launch_vt<KATOMS, MODE, float>(tr, tc, tv, p, batch, idesc, st);
-    case JK_BF16: return launch_vt<KATOMS, MODE, __nv_bfloat16>(tr, tc, tv, p, batch, idesc, st);
-    default: return launch_vt<KATOMS, MODE, __half>(tr, tc, tv, p, batch, idesc, st);
+    case JK_F32: return launch_vt<KATOMS, MODE, float>(tr, tc, tv, to, p, batch, idesc, st);
+    case JK_BF16: return launch_vt<KATOMS, MODE, __nv_bfloat16>(tr, tc, tv, to, p, batch, idesc, st);
+    default: return launch_vt<KATOMS, MODE, __half>(tr, tc, tv, to, p, batch, idesc, st);
   }
 }
 
 template <int MODE>
 int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols, int64_t rp,
            int proj_dtype, Params& p, cudaStream_t st) {
-  CUtensorMap tr, tc, tv;
+  CUtensorMap tr, tc, tv, to;
   const bool bf16 = proj_dtype != JK_F16;
   p.split3 = proj_dtype == JK_BF16X3 ? 1 : 0;
   int status = make_tmap_3d_16bit(&tr, row_proj, rp, n_rows, batch, 64, kRows, bf16);
@@ -1377,9 +1433,15 @@ int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_
     if (make_tmap_3d_16bit(&tv, p.col_val, p.dim, n_cols, batch, 64, kEK, p.val_dtype == JK_BF16, true) == JK_OK)
       p.slab_ok = 1;
   }
+  to = tc;  // placeholder when the outputs are not stored by TMA
+  p.tma_out = 0;
+  if (MODE == kGather && p.slab_ok && p.out_dtype != JK_F32 && aligned16(p.out_val)) {
+    if (make_tmap_3d_16bit(&to, p.out_val, p.dim, n_rows, batch, 64, kRows, p.out_dtype == JK_BF16, true) == JK_OK)
+      p.tma_out = 1;
+  }
   const uint32_t idesc = idesc_f16(kRows, kCols, bf16 ? 1u : 0u);
-  if (rp == 64) return launch_k<1, MODE>(tr, tc, tv, p, batch, idesc, st);
-  return launch_k<2, MODE>(tr, tc, tv, p, batch, idesc, st);
+  if (rp == 64) return launch_k<1, MODE>(tr, tc, tv, to, p, batch, idesc, st);
+  return launch_k<2, MODE>(tr, tc, tv, to, p, batch, idesc, st);
 }
 
 int validate_common(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_rows, int64_t n_cols,
