@@ -1154,6 +1154,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- compress (thread per row), fold the sender strength, form the state output
     const SlabRange sr = slab_range<VT>(p, t0);
     const bool tc_agg = MODE == kGather && good && sr.on && ntiles > 0;
+    // The source states of a windowed CTA, staged once (coalesced) in the selection passes'
+    // per-row scratch (s1, s2, pub: 6 x kRows contiguous floats, free from here on).
+    float* st_stage = s1;
+    uint32_t n_stage = 0;
+    if (MODE == kGather && good && sr.on) n_stage = static_cast<uint32_t>(sr.n < 6 * kRows ? sr.n : 6 * kRows);
+    if (n_stage > 0) {
+      for (int i = threadIdx.x; i < static_cast<int>(n_stage); i += kSelWarps * 32)
+        st_stage[i] = ld_elem(p.col_state, b * p.n_cols + sr.s_lo + i, p.state_dtype);
+      sel_barrier();
+    }
     if (half == 0) {
       const Lane F{rv, ri};
       const int n = nsel[row];
@@ -1180,7 +1190,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int u = 0; u < 8; ++u) {
             const bool on = e0 + u < n;
             const int j = on ? F.idx(e0 + u) : 0;
-            st[u] = on ? ld_elem(p.col_state, cb + j, p.state_dtype) : 0.f;
+            const uint32_t js = static_cast<uint32_t>(j - sr.s_lo);
+            st[u] = !on ? 0.f : (js < n_stage ? st_stage[js] : ld_elem(p.col_state, cb + j, p.state_dtype));
             sn[u] = (on && p.col_sender) ? ld_elem(p.col_sender, cb + j, p.state_dtype) : 1.f;
           }
 #pragma unroll
