@@ -1025,6 +1025,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // register counter (no atomics); a row whose stacks meet takes the exact fallback pass.
     {
       const float th = tau[row];
+      const uint32_t rv_s = smem_u32(rv), ri_s = smem_u32(ri);
       int myc = 0;
       for (int it = 0; it < ntiles && ok; ++it) {
         uint32_t v[2][32];
@@ -1034,16 +1035,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
+            // predicated append (no branch): a passing column goes to slot myc of this
+            // half's stack while it has room; myc counts every passing column
             const int col = col0 + c * 32 + e;
             const float x = __uint_as_float(v[c][e]);
-            if (static_cast<uint32_t>(col - lo_t) <= span && x >= th) {
-              if (myc < kCap) {
-                const int slot = half == 0 ? myc : kCap - 1 - myc;
-                rv[slot] = x;
-                ri[slot] = col;
-              }
-              ++myc;
-            }
+            const bool pass = static_cast<uint32_t>(col - lo_t) <= span && x >= th;
+            const uint32_t off = static_cast<uint32_t>(half == 0 ? myc : kCap - 1 - myc) * 4u;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %0, 0;\n\t"
+                "@p st.shared.f32 [%1], %2;\n\t"
+                "@p st.shared.b32 [%3], %4;\n\t}" ::"r"(static_cast<int>(pass && myc < kCap)),
+                "r"(rv_s + off), "f"(x), "r"(ri_s + off), "r"(col)
+                : "memory");
+            myc += pass ? 1 : 0;
           }
       }
       (half == 0 ? cnt : nsel)[row] = myc;
