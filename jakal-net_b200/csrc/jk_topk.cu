@@ -47,7 +47,7 @@ namespace topk {
 // Debug-only timeline: clock64 stamps of the phase boundaries of every CTA, stored by one
 // thread (no atomics, so the timeline is not perturbed). Slot 0 = start, 15 = SM id.
 constexpr int kTraceCtas = 4096;
-__device__ long long g_trace[kTraceCtas][24];
+__device__ long long g_trace[kTraceCtas][32];
 #define JK_STAMP(i)                                                                  \
   do {                                                                               \
     const int _cta = blockIdx.y * gridDim.x + blockIdx.x;                            \
@@ -87,9 +87,10 @@ enum Mode { kGather = 0, kScatter = 1 };
 constexpr int kEK = 64;       // source rows per edge tile (MMA K)
 constexpr int kVSlice = 128;  // value columns per slice (MMA N)
 constexpr int kVBufs = 4;     // value-slice buffers (16 KB each)
-constexpr int kOCols = 384;   // TMEM columns of the aggregate's accumulator O (dim <= 384)
-// Edge tiles live in TMEM behind O: buffer e, plane q (hi / lo) at column
-// kOCols + e * 64 + q * 32; a row's 64 K elements are 32 columns of bf16 / f16 pairs.
+constexpr int kOCols = 512;   // TMEM columns of the aggregate's accumulator O (dim <= 512)
+// Edge tiles: two buffers of 32 KB at the start of region 0, each a hi plane then a lo plane
+// of 128 rows x 64 K elements in the K-major 128-byte-swizzled operand layout.
+constexpr int kETile = 32768;
 
 // Start (in floats, 16-byte aligned) of a row's packed gather table: (weight, column) pairs
 // written over the row's candidate values once the edges are final.
@@ -662,10 +663,11 @@ struct Layout {
   static constexpr int kAtomBytes = kRows * 128;  // 128 rows x 64 (16-bit) elements
   static constexpr int kABytes = KATOMS * kAtomBytes;
   static constexpr int kBBytes = KATOMS * kAtomBytes;
-  // A + ring; reused by the selection scratch, then by the aggregate's value buffers
+  // A + ring; reused by the selection scratch, then by the aggregate's edge tiles
   static constexpr int kRegion0 = kABytes + STAGES * kBBytes;
-  static_assert(kRegion0 >= kVBufs * 16384, "the aggregate's value buffers reuse region 0");
+  static_assert(kRegion0 >= 2 * kETile, "the aggregate's edge tiles reuse region 0");
   static constexpr int kBufBytes = 2 * kRows * kStride * 4;    // candidate values + indices
+  static_assert(kBufBytes / 2 - 1023 >= kVBufs * 16384, "the value slices reuse the candidate-index buffer");
   static constexpr int kRowArrays = 10 * kRows * 4;            // per-row scalars
   static constexpr int kBarBytes = 320;
   static constexpr int kTotal = 1024 + kRegion0 + kBufBytes + kRowArrays + kBarBytes;
@@ -767,7 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int cta = blockIdx.y * gridDim.x + blockIdx.x;
     if (cta < kTraceCtas) {
       g_trace[cta][15] = smid;
-      g_trace[cta][19] = g_trace[cta][20] = g_trace[cta][21] = g_trace[cta][22] = g_trace[cta][23] = 0;
+      for (int z = 19; z < 32; ++z) g_trace[cta][z] = 0;
     }
   }
 #endif
@@ -809,7 +811,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const SlabRange sr = slab_range<VT>(p, t0);
         const int nkt = (sr.n + kEK - 1) / kEK;
         const int nsl = static_cast<int>((p.dim + kVSlice - 1) / kVSlice);
-        uint8_t* vbuf = smem;  // region 0: the score operands are consumed by now
+        // the candidate-index buffer: free once compress packed the survivors into bufv
+        uint8_t* vbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bufi) + 1023) & ~uintptr_t(1023));
         for (int pi = 0; pi < nkt * nsl && ok; ++pi) {
           const int vb = pi % kVBufs;
           if (pi >= kVBufs && !JK_PHASE_TIME(10, mbar_wait(&vb_empty[vb], ((pi - kVBufs) / kVBufs) & 1))) {
@@ -872,7 +875,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const SlabRange sr = slab_range<VT>(p, t0);
         const int nkt = (sr.n + kEK - 1) / kEK;
         const int nsl = static_cast<int>((p.dim + kVSlice - 1) / kVSlice);
-        uint8_t* vbuf = smem;
+        uint8_t* vbuf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bufi) + 1023) & ~uintptr_t(1023));
         JK_STAMP(11);
         for (int kt = 0; kt < nkt && ok; ++kt) {
           const int buf = kt & 1;
@@ -884,7 +887,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           g_trace[(blockIdx.y * gridDim.x + blockIdx.x) % kTraceCtas][22] += clock64() - tw0;
 #endif
           tc_fence_after();
-          const uint32_t e_col = tmem + kOCols + buf * 64;
+          const uint32_t e_addr = smem_u32(smem + buf * kETile);
           for (int sl = 0; sl < nsl; ++sl) {
             const int pi = kt * nsl + sl, vb = pi % kVBufs;
 #ifdef JK_PHASE_PROFILE
@@ -901,7 +904,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int q = 0; q < 2; ++q) {
 #pragma unroll
               for (int kk = 0; kk < kEK / 16; ++kk) {
-                mma_f16_ts(tmem + sl * kVSlice, e_col + q * 32 + kk * 8, sdesc_mnmajor_sw128(v_addr + kk * 2048, 8192),
+                mma_f16_ss(tmem + sl * kVSlice, sdesc_kmajor_sw128(e_addr + q * (kETile / 2) + kk * 32),
+                           sdesc_mnmajor_sw128(v_addr + kk * 2048, 8192),
                            idesc_pv, (kt > 0 || q > 0 || kk > 0) ? 1u : 0u);
               }
             }
@@ -1211,11 +1215,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         st_elem(p.out_state, b * p.n_rows + t, p.out_dtype, acc);
         if (threadIdx.x == 0) JK_STAMP(18);
       }
-      if (tc_agg) {
-        // the tensor-core aggregate reads the weights and columns in place
-      } else if (MODE == kGather) {
-        // Pack (weight, column) pairs for the gather, back to front so that every write
-        // lands on an already consumed candidate slot of the same row.
+      if (MODE == kGather) {
+        // Pack (weight, column) pairs for the aggregate, back to front so that every write
+        // lands on an already consumed candidate slot of the same row (slot order kept).
         float* tab = bufv + gtab_off(row);
         for (int e = n - 1; e >= 0; --e) {
           const float w = F.val(e);
@@ -1240,70 +1242,83 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tc_agg) {
           // Tensor-core aggregate over the CTA's source window. For every 64-row source
           // tile kt the selected edges of the 128 target rows form a sparse 128 x 64 matrix
-          // E (bf16 / f16 hi + lo planes), in TMEM as the MMA's A operand. Tile kt lies in
-          // half kt & 1 of a score tile, so its columns are exactly the candidates the
-          // selection half kt & 1 collected: the four warps of that half build it, from
-          // their rows' run of survivors (ascending columns), into buffer kt & 1 (thread =
-          // TMEM lane = row), and signal e_full; the two halves build alternate tiles. The
-          // MMA warp forms O[128 x dim] += E_hi.V + E_lo.V. The hi + lo planes keep the
-          // edge weights to ~16 bits.
+          // E (bf16 / f16 hi + lo planes), the MMA's A operand in shared memory. Tile kt lies
+          // in half kt & 1 of a score tile, so its columns are exactly the candidates the
+          // selection half kt & 1 collected: the four warps of that half build it -- each
+          // thread zeroes its row and stores the row's edges of the tile, walking its run
+          // of packed (weight, column) survivors -- into buffer kt & 1, and signal e_full;
+          // the two halves build alternate tiles. The MMA warp forms
+          // O[128 x dim] += E_hi.V + E_lo.V in TMEM. The hi + lo planes keep the edge
+          // weights to ~16 bits.
           constexpr bool kHalfV = std::is_same<VT, __half>::value;
           const int nkt = (sr.n + kEK - 1) / kEK;
           const int n = nsel[row];
           const int m0 = cnt[row];
+          const float* tab = bufv + gtab_off(row);
           // rows of the exact fallback pass hold one sorted run, filtered by tile parity
           const bool runs = failrow[row] == 0;
           int cur = runs && half == 1 ? m0 : 0;
           const int end = runs && half == 0 ? m0 : n;
           auto next_rel = [&]() -> int {  // window-relative column of the next entry of this half
             while (cur < end) {
-              const int rel = ri[cur] - sr.s_lo;
+              const int rel = __float_as_int(tab[2 * cur + 1]) - sr.s_lo;
               if (((rel >> 6) & 1) == half) return rel;
               ++cur;
             }
             return INT_MAX;
           };
           int rel = next_rel();
-          const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16) + kOCols + half * 64;
+          const uint32_t rsw = static_cast<uint32_t>(row & 7);
+          const int rbase = (row >> 3) * 1024 + (row & 7) * 128;
           for (int kt = half, use = 0; kt < nkt; kt += 2, ++use) {
+#ifdef JK_PHASE_PROFILE
+            const long long tb0 = clock64();
+#endif
             if (use >= 1 && !mbar_wait(&e_empty[half], (use - 1) & 1)) {
               atomicExch(&g_device_error, JK_ERR_DEVICE_TIMEOUT);
               *abort_flag = 1;
             }
             if (*abort_flag) break;
-            tc_fence_after();
-            uint32_t ehi[32], elo[32];
+#ifdef JK_PHASE_PROFILE
+            const long long tb1 = clock64();
+#endif
+            uint8_t* e_hi = smem + half * kETile + rbase;
+            uint8_t* e_lo = e_hi + kETile / 2;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ehi[i] = elo[i] = 0u;
+            for (int c = 0; c < 8; ++c) {  // through the swizzle: the warp's rows hit distinct banks
+              const int o = (c ^ static_cast<int>(rsw)) << 4;
+              *reinterpret_cast<uint4*>(e_hi + o) = make_uint4(0, 0, 0, 0);
+              *reinterpret_cast<uint4*>(e_lo + o) = make_uint4(0, 0, 0, 0);
+            }
             while ((rel >> 6) == kt) {
-              const float w = rv[cur];
+              const float w = tab[2 * cur];
               const int kin = rel & 63;
-              uint32_t hb, lb;
+              const int off = ((static_cast<uint32_t>(kin >> 3) ^ rsw) << 4) + (kin & 7) * 2;
               if (kHalfV) {
                 const __half h = __float2half_rn(w);
-                hb = __half_as_ushort(h);
-                lb = __half_as_ushort(__float2half_rn(w - __half2float(h)));
+                *reinterpret_cast<__half*>(e_hi + off) = h;
+                *reinterpret_cast<__half*>(e_lo + off) = __float2half_rn(w - __half2float(h));
               } else {
                 const __nv_bfloat16 h = __float2bfloat16_rn(w);
-                hb = __bfloat16_as_ushort(h);
-                lb = __bfloat16_as_ushort(__float2bfloat16_rn(w - __bfloat162float(h)));
-              }
-              const int sh = (kin & 1) * 16;
-              const int r = kin >> 1;
-              hb <<= sh;
-              lb <<= sh;
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                ehi[i] |= (i == r) ? hb : 0u;
-                elo[i] |= (i == r) ? lb : 0u;
+                *reinterpret_cast<__nv_bfloat16*>(e_hi + off) = h;
+                *reinterpret_cast<__nv_bfloat16*>(e_lo + off) = __float2bfloat16_rn(w - __bfloat162float(h));
               }
               ++cur;
               rel = next_rel();
             }
-            tmem_st_32x32b_x32(lane_base, ehi);
-            tmem_st_32x32b_x32(lane_base + 32, elo);
-            tmem_st_wait();
-            tc_fence_before();
+#ifdef JK_PHASE_PROFILE
+            const long long tb2 = clock64();
+#endif
+            fence_proxy_async_smem();  // the MMA (async proxy) reads the tile next
+#ifdef JK_PHASE_PROFILE
+            if (threadIdx.x == 0 || threadIdx.x == 128) {
+              const int tr = (blockIdx.y * gridDim.x + blockIdx.x) % kTraceCtas;
+              const int o = threadIdx.x == 0 ? 24 : 27;
+              g_trace[tr][o] += tb1 - tb0;
+              g_trace[tr][o + 1] += tb2 - tb1;
+              g_trace[tr][o + 2] += clock64() - tb2;
+            }
+#endif
             __syncwarp();
             if (lane == 0) mbar_arrive(&e_full[half]);
           }
@@ -1689,6 +1704,6 @@ extern "C" int jk_transition_pairwise_topk_forward_mh(const void* src_proj, cons
 extern "C" int jk_debug_trace(long long* out, int n_ctas) {
   cudaDeviceSynchronize();
   const int n = n_ctas < jk::topk::kTraceCtas ? n_ctas : jk::topk::kTraceCtas;
-  return cudaMemcpyFromSymbol(out, jk::topk::g_trace, sizeof(long long) * 24 * n) == cudaSuccess ? 0 : -1;
+  return cudaMemcpyFromSymbol(out, jk::topk::g_trace, sizeof(long long) * 32 * n) == cudaSuccess ? 0 : -1;
 }
 #endif

@@ -69,9 +69,9 @@ def run() -> None:
     e1.record()
     torch.cuda.synchronize()
     n = B * N // 128
-    buf = (ctypes.c_longlong * (24 * n))()
+    buf = (ctypes.c_longlong * (32 * n))()
     lib.jk_debug_trace(buf, n)
-    t = np.array(buf, dtype=np.int64).reshape(n, 24)
+    t = np.array(buf, dtype=np.int64).reshape(n, 32)
     rel = t - t[:, :1]
     print(f"traced launch {e0.elapsed_time(e1) * 1e3:.1f} us, {n} CTAs on {len(set(t[:, 15]))} SMs")
     print(f"{'phase end':36s} {'median':>9s} {'max':>9s}  (cycles from CTA start)")
@@ -79,6 +79,9 @@ def run() -> None:
         print(f"{name:36s} {np.median(rel[:, slot]):9.0f} {np.max(rel[:, slot]):9.0f}")
     print(f"select, warp 0 over its 16 rows: rank loop {np.median(t[:, 19]):.0f}, tail {np.median(t[:, 20]):.0f}, "
           f"candidates {np.median(t[:, 21]):.0f}")
+    for h, o in ((0, 24), (1, 27)):
+        print(f"edge builder, half {h} (thread 0 of its first warp): waits {np.median(t[:, o]):.0f}, entries "
+              f"{np.median(t[:, o + 1]):.0f}, TMEM store {np.median(t[:, o + 2]):.0f}")
     print(f"MMA warp waits: edge tiles {np.median(t[:, 22]):.0f}, value slices {np.median(t[:, 23]):.0f}")
 
 
