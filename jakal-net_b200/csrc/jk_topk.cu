@@ -85,8 +85,9 @@ enum Mode { kGather = 0, kScatter = 1 };
 
 // Tensor-core aggregate: 64 source rows per edge tile, value slices of 128 columns.
 constexpr int kEK = 64;       // source rows per edge tile (MMA K)
-constexpr int kVSlice = 128;  // value columns per slice (MMA N)
-constexpr int kVBufs = 4;     // value-slice buffers (16 KB each)
+constexpr int kVSlice = 256;  // value columns per slice (MMA N)
+constexpr int kVBufs = 2;     // value-slice buffers
+constexpr int kVBufBytes = kEK * kVSlice * 2;  // 32 KB: kVSlice / 64 boxes of 64 rows x 64 columns
 constexpr int kOCols = 512;   // TMEM columns of the aggregate's accumulator O (dim <= 512)
 // Edge tiles: two buffers of 32 KB at the start of region 0, each a hi plane then a lo plane
 // of 128 rows x 64 K elements in the K-major 128-byte-swizzled operand layout.
@@ -667,7 +668,7 @@ struct Layout {
   static constexpr int kRegion0 = kABytes + STAGES * kBBytes;
   static_assert(kRegion0 >= 2 * kETile, "the aggregate's edge tiles reuse region 0");
   static constexpr int kBufBytes = 2 * kRows * kStride * 4;    // candidate values + indices
-  static_assert(kBufBytes / 2 - 1023 >= kVBufs * 16384, "the value slices reuse the candidate-index buffer");
+  static_assert(kBufBytes / 2 - 1023 >= kVBufs * kVBufBytes, "the value slices reuse the candidate-index buffer");
   static constexpr int kRowArrays = 10 * kRows * 4;            // per-row scalars
   static constexpr int kBarBytes = 320;
   static constexpr int kTotal = 1024 + kRegion0 + kBufBytes + kRowArrays + kBarBytes;
@@ -825,7 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int nb = (w < kVSlice ? w : kVSlice) / 64;
           mbar_arrive_expect_tx(&vb_full[vb], nb * 8192);
           for (int a = 0; a < nb; ++a)
-            tma_load_3d(vbuf + vb * 16384 + a * 8192, &tm_val, &vb_full[vb], sl * kVSlice + a * 64,
+            tma_load_3d(vbuf + vb * kVBufBytes + a * 8192, &tm_val, &vb_full[vb], sl * kVSlice + a * 64,
                         sr.s_lo + kt * kEK, static_cast<int>(b));
         }
       }
@@ -899,7 +900,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
             const int w = static_cast<int>(p.dim) - sl * kVSlice;
             const uint32_t idesc_pv = idesc_f16(kRows, w < kVSlice ? w : kVSlice, kHalfV ? 0u : 1u) | (1u << 16);
-            const uint32_t v_addr = smem_u32(vbuf + vb * 16384);
+            const uint32_t v_addr = smem_u32(vbuf + vb * kVBufBytes);
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
 #pragma unroll
