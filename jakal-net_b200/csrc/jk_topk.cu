@@ -630,6 +630,86 @@ __device__ int warp_rank_select(float* rv, int* ri, int c0, int c1, int k, int l
   return real < k ? real : k;
 }
 
+// Two rows at once (the latency of one row's loads and compares hides the other's): the
+// 32-bit-score ranking of warp_rank_select for two rows whose stacks hold ascending
+// column runs. A row with exact score ties is left untouched (done[] false) for
+// warp_rank_select; a done row is written back exactly as warp_rank_select writes it.
+template <int NQ>
+__device__ void warp_rank_pair(float* const (&rv)[2], int* const (&ri)[2], const int (&c0)[2], const int (&c1)[2],
+                               int k, int lane, uint32_t* ku, bool (&done)[2], int (&nout)[2], int (&m0)[2]) {
+  int n[2], n4[2];
+  float sc[2][NQ];
+  int col[2][NQ];
+  uint32_t u[2][NQ];
+  int rank[2][NQ];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    n[r] = c0[r] + c1[r];
+    n4[r] = (n[r] + 3) & ~3;
+  }
+  const int nmax = n4[0] > n4[1] ? n4[0] : n4[1];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int i = q * 32 + lane;
+      const int e = i < c0[r] ? i : kCap - 1 - (i - c0[r]);
+      const bool real_i = i < n[r] && ri[r][e] != kSentinel;
+      sc[r][q] = real_i ? rv[r][e] : 0.f;
+      col[r][q] = real_i ? ri[r][e] : 0;
+      u[r][q] = real_i ? static_cast<uint32_t>(make_key(sc[r][q], col[r][q]) >> 32) : 0u;
+      if (i < nmax) ku[r * kCap + i] = u[r][q];  // zero beyond the row: never beats a key
+      rank[r][q] = 0;
+    }
+  }
+  __syncwarp();
+  for (int j = 0; j < nmax; j += 4) {
+    const uint4 a = *reinterpret_cast<const uint4*>(ku + j);
+    const uint4 b = *reinterpret_cast<const uint4*>(ku + kCap + j);
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      rank[0][q] += (a.x > u[0][q]) + (a.y > u[0][q]) + (a.z > u[0][q]) + (a.w > u[0][q]);
+      rank[1][q] += (b.x > u[1][q]) + (b.y > u[1][q]) + (b.z > u[1][q]) + (b.w > u[1][q]);
+    }
+  }
+  const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    int real = 0, rsum = 0;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const bool is_real = u[r][q] != 0u;
+      real += __popc(__ballot_sync(0xffffffffu, is_real));
+      rsum += is_real ? rank[r][q] : 0;
+    }
+    rsum = __reduce_add_sync(0xffffffffu, rsum);
+    done[r] = rsum == real * (real - 1) / 2;
+    if (!done[r]) continue;  // warp-uniform
+    bool keep[NQ];
+    int slot[NQ];
+    int before = 0, in0 = 0;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      keep[q] = u[r][q] != 0u && rank[r][q] < k;
+      const uint32_t bal = __ballot_sync(0xffffffffu, keep[q]);
+      slot[q] = before + __popc(bal & lt);
+      before += __popc(bal);
+      in0 += __popc(__ballot_sync(0xffffffffu, keep[q] && q * 32 + lane < c0[r]));
+    }
+    m0[r] = in0;
+    nout[r] = real < k ? real : k;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      if (keep[q]) {
+        rv[r][slot[q]] = sc[r][q];
+        ri[r][slot[q]] = col[r][q];
+        ri[r][kCap / 2 + slot[q]] = rank[r][q];
+      }
+    }
+  }
+  __syncwarp();
+}
+
 __device__ __forceinline__ void sel_barrier() {
   asm volatile("bar.sync 1, %0;" ::"r"(kSelWarps * 32) : "memory");
 }
@@ -1133,29 +1213,54 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rt0 = warp * (kRows / kSelWarps);
     // Key scratch in the (now idle) operand region: 128 keys per warp.
     unsigned long long* ks = reinterpret_cast<unsigned long long*>(smem) + warp * kCap;
-    for (int r = 0; r < kRows / kSelWarps; ++r) {
-      const int rt = rt0 + r;
-      int n = 0, m0 = 0;
-      if (good && t0 + rt < p.n_rows) {
-        float* wv = bufv + rt * kStride;
-        int* wi = bufi + rt * kStride;
-        const int c0 = cnt[rt];
-        const int c1 = nsel[rt];
-        const int m = c0 + c1;
-        const bool runs = failrow[rt] == 0;
+    for (int r = 0; r < kRows / kSelWarps; r += 2) {
+      // rows rt0 + r and rt0 + r + 1 together; exact-fallback rows and rows with score ties
+      // go through warp_rank_select one at a time
+      float* wv[2];
+      int* wi[2];
+      int c0[2], c1[2], n[2] = {0, 0}, m0[2] = {0, 0};
+      bool live[2], pairable[2], done[2] = {false, false};
+      int mmax = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int rt = rt0 + r + h;
+        wv[h] = bufv + rt * kStride;
+        wi[h] = bufi + rt * kStride;
+        live[h] = good && t0 + rt < p.n_rows;
+        c0[h] = live[h] ? cnt[rt] : 0;
+        c1[h] = live[h] ? nsel[rt] : 0;
+        pairable[h] = live[h] && failrow[rt] == 0;
+        if (pairable[h] && c0[h] + c1[h] > mmax) mmax = c0[h] + c1[h];
 #ifdef JK_PHASE_PROFILE
         if (threadIdx.x == 0 && blockIdx.y * gridDim.x + blockIdx.x < kTraceCtas)
-          g_trace[blockIdx.y * gridDim.x + blockIdx.x][21] += m;
+          g_trace[blockIdx.y * gridDim.x + blockIdx.x][21] += c0[h] + c1[h];
 #endif
-        n = m <= 32   ? warp_rank_select<1>(wv, wi, c0, c1, k, lane, ks, runs, m0)
-            : m <= 64 ? warp_rank_select<2>(wv, wi, c0, c1, k, lane, ks, runs, m0)
-            : m <= 96 ? warp_rank_select<3>(wv, wi, c0, c1, k, lane, ks, runs, m0)
-                      : warp_rank_select<4>(wv, wi, c0, c1, k, lane, ks, runs, m0);
+      }
+      if (pairable[0] && pairable[1]) {
+        uint32_t* ku = reinterpret_cast<uint32_t*>(ks);
+        if (mmax <= 32) warp_rank_pair<1>(wv, wi, c0, c1, k, lane, ku, done, n, m0);
+        else if (mmax <= 64) warp_rank_pair<2>(wv, wi, c0, c1, k, lane, ku, done, n, m0);
+        else if (mmax <= 96) warp_rank_pair<3>(wv, wi, c0, c1, k, lane, ku, done, n, m0);
+        else warp_rank_pair<4>(wv, wi, c0, c1, k, lane, ku, done, n, m0);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (live[h] && !done[h]) {
+          const int m = c0[h] + c1[h];
+          const bool runs = pairable[h];
+          n[h] = m <= 32   ? warp_rank_select<1>(wv[h], wi[h], c0[h], c1[h], k, lane, ks, runs, m0[h])
+                 : m <= 64 ? warp_rank_select<2>(wv[h], wi[h], c0[h], c1[h], k, lane, ks, runs, m0[h])
+                 : m <= 96 ? warp_rank_select<3>(wv[h], wi[h], c0[h], c1[h], k, lane, ks, runs, m0[h])
+                           : warp_rank_select<4>(wv[h], wi[h], c0[h], c1[h], k, lane, ks, runs, m0[h]);
+        }
       }
       __syncwarp();
       if (lane == 0) {
-        nsel[rt] = n;
-        cnt[rt] = m0;  // length of the first ascending column run
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          nsel[rt0 + r + h] = n[h];
+          cnt[rt0 + r + h] = m0[h];  // length of the first ascending column run
+        }
       }
     }
     sel_barrier();
