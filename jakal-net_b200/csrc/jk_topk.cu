@@ -1279,9 +1279,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         st_stage[i] = ld_elem(p.col_state, b * p.n_cols + sr.s_lo + i, p.state_dtype);
       sel_barrier();
     }
+    // Softsign is elementwise: unless the ordered scores are requested, both threads of a
+    // row share its entries (even / odd) and half 1 hands its state partial over in tau.
+    const bool split = p.compress == JK_SOFTSIGN && !(MODE == kGather && (p.out_scores || p.out_index));
+    const Lane F{rv, ri};
+    const int n_row = nsel[row];
+    if (split) {
+      const float bias = p.bias + (p.bias_dev ? __ldg(p.bias_dev) : 0.f);
+      float acc = 0.f;
+      const int64_t cb = b * p.n_cols;
+      for (int e = half; e < n_row; e += 2) {
+        const float x = F.val(e) + bias;
+        float w = x / (1.f + fabsf(x));
+        if (MODE == kGather) {
+          const int j = F.idx(e);
+          const uint32_t js = static_cast<uint32_t>(j - sr.s_lo);
+          if (p.col_sender) w *= ld_elem(p.col_sender, cb + j, p.state_dtype);
+          const float stv = js < n_stage ? st_stage[js] : ld_elem(p.col_state, cb + j, p.state_dtype);
+          acc = fmaf(w, stv, acc);
+        }
+        F.val(e) = w;
+      }
+      if (half == 1) tau[row] = acc;
+      sel_barrier();
+      if (MODE == kGather && half == 0 && row_ok && good)
+        st_elem(p.out_state, b * p.n_rows + t, p.out_dtype, acc + tau[row]);
+    }
     if (half == 0) {
-      const Lane F{rv, ri};
-      const int n = nsel[row];
+      const int n = n_row;
+      if (!split) {
       const float bias = p.bias + (p.bias_dev ? __ldg(p.bias_dev) : 0.f);
       for (int e = 0; e < n; ++e) F.val(e) += bias;
       if (MODE == kGather && row_ok && good && (p.out_scores || p.out_index)) {
@@ -1320,6 +1346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         st_elem(p.out_state, b * p.n_rows + t, p.out_dtype, acc);
         if (threadIdx.x == 0) JK_STAMP(18);
+      }
       }
       if (MODE == kGather) {
         // Pack (weight, column) pairs for the aggregate, back to front so that every write
