@@ -41,7 +41,7 @@ UNIT = "Gpairs/s"
 WORKLOAD = "config2: SparsePropagation causal window 512 intersect top-k 32, B8 N2048 D384 R64, bf16, softsign"
 # dram__bytes_read.sum + dram__bytes_write.sum of one fused-kernel launch on this workload,
 # from the ncu capture summarised in profiles/topk_kernel_config2.md.
-NCU_TRAFFIC_BYTES = 16955392  # 16.96 MB read + 0 B written (outputs stay in L2), one launch
+NCU_TRAFFIC_BYTES = 16975104  # 16.98 MB read + 0 B written (outputs stay in L2), one launch
 
 
 def pairs_per_batch_item(n: int, window: int) -> int:
