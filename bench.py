@@ -151,6 +151,9 @@ def cpu_port_time(seconds: float = 10.0):
     w_s = (torch.randn(R, D, generator=g) / D ** 0.5).bfloat16()
     w_t = (torch.randn(R, D, generator=g) / D ** 0.5).bfloat16()
     core = torch.full((R,), 1.0 / R ** 0.5)
+    pt = cpu_port.lowrank_project_bf16(val, w_t)  # untimed warm-up: first-call overheads
+    ps = cpu_port.lowrank_project_bf16(val, w_s, core)
+    cpu_port.window_topk_propagation(pt, ps, state, val, K_TOP, WINDOW)
     reps = 0
     t0 = time.perf_counter()
     while True:
