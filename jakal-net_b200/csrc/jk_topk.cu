@@ -10,29 +10,32 @@
 //   * per-source transition    native/jakal_net_native_cuda.cu:740-878 (rows = sources,
 //                              softmax over the k picked destinations, scatter-add).
 //
-// Per CTA: 128 rows of one batch item, 9 warps.
-//   warp 8 (producer): TMA-loads the row-side projection tile once and streams the
-//          column-side tiles (128 columns x rp) through a smem ring; issues tcgen05.mma
-//          (M=128 rows, N=128 columns, K=rp) into one of two TMEM accumulators, so the MMA
-//          of one tile overlaps the selection work on the previous one. The column tiles
-//          are streamed once per selection pass (scores are recomputed, never stored).
+// Per CTA: 128 rows of one batch item, 10 warps.
+//   warp 9 (loader): TMA of the row-side projection tile once, the column-side tiles
+//          (128 columns x rp) through a shared-memory ring once per selection pass, and
+//          for the tensor-core aggregate the source window's value slices.
+//   warp 8 (MMA): tcgen05.mma score tiles (M=128 rows, N=128 columns, K=rp) into one of two
+//          TMEM accumulators, so the MMA of one tile overlaps the selection work on the
+//          previous one (scores are recomputed per pass, never stored); later the
+//          aggregate's E.V MMAs.
 //   warps 0-7 (selection): two threads per row (warps w and w+4 read the same TMEM lanes),
 //          each owning 64 of the 128 columns of every tile.
 //     pass A (only when a row sees more than kCap columns): per-row mean and variance of
 //          the visible scores -> a threshold tau expected to pass about k + 3 sqrt(k) + 8
 //          columns (normal quantile).
-//     pass B: every visible column with score >= tau is appended to the row's candidate
-//          buffer (kCap slots in shared memory).
+//     pass B: every visible column with score >= tau is appended (predicated stores) to
+//          the row's candidate stack of its half -- two stacks in ascending column order.
 //     pass C (only if some row of the CTA got fewer than min(k, visible) or more than kCap
 //          candidates -- a row far from normal): those rows redo an exact streaming
 //          selection, each thread keeping a k-entry min-heap in the row's buffer.
-//     select: one warp per row ranks the row's candidates (64-bit keys ordered by score
-//          then lower column; each lane counts the keys that beat its own) and keeps the
-//          best k in descending order.
-//   Then the k survivors are compressed into edges, and all 8 warps aggregate: a windowed
-//   CTA stages its whole source range in shared memory 64 value columns at a time (TMA)
-//   and gathers from there; otherwise 16-byte vector gathers from global memory; the
-//   per-source transition scatters with vector atomics instead.
+//     select: one warp per two rows ranks the candidates (32-bit scores; 64-bit keys
+//          score then lower column for rows with exact ties) and keeps the best k as two
+//          ascending column runs.
+//   Then the k survivors are compressed into edges (sender weighting and the state sum
+//   folded in) and aggregated: a windowed CTA on the tensor cores (sparse 64-row edge
+//   tiles in shared memory times value slices, O in TMEM, TMA-stored outputs); otherwise
+//   16-byte vector gathers from global memory; the per-source transition scatters with
+//   vector atomics instead.
 #include "jk_host.h"
 #include "jk_sm100.cuh"
 
