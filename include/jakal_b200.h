@@ -288,6 +288,35 @@ int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_pr
                                         void* out_val, int out_dtype, jk_stream_t stream);
 
 /*
+ * Select-aggregate over materialised f32 score rows (any k, any score rank):
+ *   scores [B, row_count, n_cols] holds score[b, t, s] for the rows t in
+ *   [row_begin, row_begin + row_count) of an n_rows-row operator (e.g. a plain GEMM of the
+ *   projections). Visibility, selection (ties to the lower column), score_bias / bias_dev,
+ *   compressors and sender weighting are those of jk_propagation_topk_forward, with no limit
+ *   on k or on the rank that produced the scores.
+ *   scatter == 0 (gather): out_state [B, n_rows] / out_val [B, n_rows, dim] (out_dtype) get
+ *     rows row_begin..; state / sender [B, n_cols], val [B, n_cols, dim] are per column.
+ *   scatter == 1 (per-source transition): rows are sources; state / sender [B, n_rows],
+ *     val [B, n_rows, dim]; acc_state [B, n_cols] and acc_val [B, n_cols, dim] (f32, zeroed
+ *     by the caller) receive sum_t w[t, s] * state[t] and sum_t w[t, s] * val[t, :].
+ *   sel_score f32 / sel_index int64 [B, row_count, k] (caller scratch, also a result): the
+ *   selected scores (bias included) and columns in ascending column order, -inf / -1 pad.
+ * One CTA per row: an exact 4-pass radix select over order-preserving keys, block prefix
+ * sums for the survivors, block reductions for the compressor, then the gather or the
+ * scatter. Replaces the blocked top-k paths that take any k:
+ * jakal_net_native.cpp:6390-6447 (propagation_topk), :6916-7087 (transition_pairwise_topk)
+ * and :7089-7246 (transition_query_topk), the path the reference takes when its CUDA kernels
+ * refuse k > 64 (jakal_net_native_cuda.cu:2432-2434, 2557-2559).
+ */
+int jk_select_aggregate_forward(const float* scores, int64_t batch, int64_t n_rows, int64_t n_cols,
+                                int64_t row_begin, int64_t row_count, const void* state,
+                                const void* sender, int state_dtype, const void* val, int64_t dim,
+                                int val_dtype, int64_t k, int64_t window, float score_bias,
+                                const float* bias_dev, int compress, int scatter, void* out_state,
+                                void* out_val, int out_dtype, float* acc_state, float* acc_val,
+                                float* sel_score, int64_t* sel_index, jk_stream_t stream);
+
+/*
  * Allocation-free per-source sparse transition. No counterpart in the reference: it exists
  * for callers that cannot allocate device memory at call time -- plain-C / FFI hosts with no
  * device allocator of their own, and latency-critical loops that must not call cudaMalloc /
@@ -295,8 +324,9 @@ int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_pr
  * jk_transition_pairwise_topk_forward without the `accum` argument: the f32 scratch is a
  * fixed 16 MiB device array inside the library (held on every GPU that loads it until exit),
  * so B * n_dst * (dim + 1) must not exceed jk_transition_pairwise_topk_noalloc_capacity()
- * floats, else JK_ERR_BAD_SHAPE. The first call on a device resolves the array's address
- * (make it before any stream capture). Calls share the array: calls that overlap on the GPU
+ * floats, else JK_ERR_BAD_SHAPE. Every call looks up the array's address on the current
+ * device (so it stays valid after a device reset or from another context); the first call
+ * on a device also loads the library's module there, so make it before any stream capture. Calls share the array: calls that overlap on the GPU
  * race; serialise them on one stream. The scratch is zeroed on the stream by every call.
  */
 int jk_transition_pairwise_topk_forward_noalloc(const void* src_proj, const void* dst_proj,

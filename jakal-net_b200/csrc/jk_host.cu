@@ -94,13 +94,15 @@ int jk_device_status(jk_stream_t stream, int* device_status) {
     cudaGetLastError();
     return JK_ERR_LAUNCH;
   }
-  int value = 0, zero = 0;
-  if (cudaMemcpyFromSymbol(&value, jk::g_device_error, sizeof(int)) != cudaSuccess ||
-      cudaMemcpyToSymbol(jk::g_device_error, &zero, sizeof(int)) != cudaSuccess) {
-    cudaGetLastError();
-    return JK_ERR_LAUNCH;
+  int (*readers[])(int*) = {jk::read_error_project, jk::read_error_topk, jk::read_error_window};
+  int combined = JK_OK;
+  for (auto read : readers) {
+    int value = JK_OK;
+    const int st = read(&value);
+    if (st != JK_OK) return st;
+    if (value != JK_OK) combined = value;
   }
-  *device_status = value;
+  *device_status = combined;
   return JK_OK;
 }
 

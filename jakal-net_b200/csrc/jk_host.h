@@ -12,9 +12,28 @@
 namespace jk {
 
 // Device-side error word (JK_OK or JK_ERR_DEVICE_TIMEOUT), written by kernels whose
-// bounded wait gave up; read and cleared by jk_device_status. The library is built as a
-// single translation unit (jk_lib.cu), so the definition lives here.
-__device__ int g_device_error = 0;
+// bounded wait gave up. The library is built from several translation units without
+// relocatable device code, so every unit that includes this header has its own copy;
+// JK_ERROR_READER defines the unit's host function that reads and clears its copy, and
+// jk_device_status combines them.
+static __device__ int g_device_error = 0;
+
+#define JK_ERROR_READER(name)                                                             \
+  int name(int* value) {                                                                \
+    int zero = 0;                                                                       \
+    if (cudaMemcpyFromSymbol(value, g_device_error, sizeof(int)) != cudaSuccess ||      \
+        cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)) != cudaSuccess) {        \
+      cudaGetLastError();                                                               \
+      return JK_ERR_LAUNCH;                                                             \
+    }                                                                                   \
+    return JK_OK;                                                                       \
+  }
+
+// Readers of the units that launch kernels with bounded waits (jk_project.cu, jk_topk.cu,
+// jk_window.cu).
+int read_error_project(int* value);
+int read_error_topk(int* value);
+int read_error_window(int* value);
 
 // Returns JK_OK when the current device is sm_100 (cached per device ordinal).
 int check_device();

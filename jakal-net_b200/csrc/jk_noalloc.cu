@@ -8,14 +8,13 @@
 // scratch in a fixed file-scope device array -- every GPU that loads the library holds it
 // until the process exits -- and offers one more entry point that allocates nothing.
 //
-// The first call on a device resolves the array's device address (cudaGetSymbolAddress
-// with that device current); make that first call before any stream capture. All calls on
+// Every call resolves the array's device address on the current device
+// (cudaGetSymbolAddress with that device current); the first call on a device also loads the
+// module there, so make it before any stream capture. All calls on
 // a device share the one array, so calls whose kernels overlap on the GPU (different
 // streams, or different host threads) race and corrupt each other's results; serialise
 // them on one stream.
 #include "jk_host.h"
-
-#include <mutex>
 
 namespace jk {
 namespace noalloc {
@@ -25,27 +24,17 @@ constexpr int64_t kScratchFloats = int64_t(1) << 22;
 
 static __device__ __align__(256) float g_transition_scratch[kScratchFloats];
 
-// Device address of g_transition_scratch per device ordinal, resolved once per device with
-// that device current (the symbol's host-side name is only a stand-in, not an address).
+// Device address of g_transition_scratch on the current device. It is looked up on every
+// call, with the caller's device current, instead of being cached: a cached address would go
+// stale after a device reset or when a driver-API host calls from another context on the
+// same device. (The symbol's host-side name is only a stand-in, not a device address.)
 int scratch_address(float** out) {
-  constexpr int kMaxDev = 64;
-  static float* addr[kMaxDev] = {};
-  static std::mutex mu;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_transition_scratch) != cudaSuccess || p == nullptr) {
     cudaGetLastError();
-    return JK_ERR_UNSUPPORTED_DEVICE;
+    return JK_ERR_LAUNCH;
   }
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_transition_scratch) != cudaSuccess || p == nullptr) {
-      cudaGetLastError();
-      return JK_ERR_LAUNCH;
-    }
-    addr[dev] = static_cast<float*>(p);
-  }
-  *out = addr[dev];
+  *out = static_cast<float*>(p);
   return JK_OK;
 }
 

@@ -345,3 +345,7 @@ extern "C" int jk_debug_ptrace(long long* out, int n) {
   return cudaMemcpyFromSymbol(out, jk::proj::g_ptrace, sizeof(long long) * 16 * (n < 1024 ? n : 1024)) == cudaSuccess ? 0 : -1;
 }
 #endif
+
+namespace jk {
+JK_ERROR_READER(read_error_project)
+}  // namespace jk

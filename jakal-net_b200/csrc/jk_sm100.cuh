@@ -365,6 +365,27 @@ __device__ __forceinline__ void st_elem(void* p, long long i, int dtype, float v
   }
 }
 
+// Stores 8 f32 values at base[elem ..] in dtype (f32: two 16-byte stores, 16-bit: one).
+__device__ __forceinline__ void store8(void* base, int64_t elem, int dtype, const float (&f)[8]) {
+  if (dtype == JK_F32) {
+    float4* q = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + elem);
+    q[0] = make_float4(f[0], f[1], f[2], f[3]);
+    q[1] = make_float4(f[4], f[5], f[6], f[7]);
+  } else if (dtype == JK_BF16) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + elem) = u;
+  } else {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(base) + elem) = u;
+  }
+}
+
 // softplus as torch.nn.functional.softplus (beta=1, threshold=20).
 __device__ __forceinline__ float softplus_f(float x) {
   return x > 20.f ? x : log1pf(expf(x));

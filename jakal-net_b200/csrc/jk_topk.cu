@@ -306,26 +306,6 @@ __device__ __forceinline__ float2 widen2<float>(uint32_t) {
   return make_float2(0.f, 0.f);
 }
 
-__device__ __forceinline__ void store8(void* base, int64_t elem, int dtype, const float (&f)[8]) {
-  if (dtype == JK_F32) {
-    float4* q = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + elem);
-    q[0] = make_float4(f[0], f[1], f[2], f[3]);
-    q[1] = make_float4(f[4], f[5], f[6], f[7]);
-  } else if (dtype == JK_BF16) {
-    uint4 u;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + elem) = u;
-  } else {
-    uint4 u;
-    __half2* h = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-    *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(base) + elem) = u;
-  }
-}
-
 __device__ __forceinline__ void store2(void* base, int64_t elem, int dtype, float a, float b) {
   if (dtype == JK_F32) {
     *reinterpret_cast<float2*>(reinterpret_cast<float*>(base) + elem) = make_float2(a, b);
@@ -1843,3 +1823,7 @@ extern "C" int jk_debug_trace(long long* out, int n_ctas) {
   return cudaMemcpyFromSymbol(out, jk::topk::g_trace, sizeof(long long) * 32 * n) == cudaSuccess ? 0 : -1;
 }
 #endif
+
+namespace jk {
+JK_ERROR_READER(read_error_topk)
+}  // namespace jk

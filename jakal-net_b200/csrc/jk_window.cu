@@ -587,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float f[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) f[u] = __uint_as_float(v[e + u]);
-            topk::store8(p.out_val, base + e, p.out_dtype, f);
+            store8(p.out_val, base + e, p.out_dtype, f);
           }
         }
       }
@@ -812,3 +812,7 @@ extern "C" int jk_transition_pairwise_dense_forward_mh(const void* src_proj, con
                                            state_dtype, src_val, src_val_lo, dim, score_bias, bias_dev, compress,
                                            stats, out_state, out_val, out_dtype, heads, stream);
 }
+
+namespace jk {
+JK_ERROR_READER(read_error_window)
+}  // namespace jk

@@ -8,12 +8,30 @@ imports the module named by ``JAKAL_NET_NATIVE_MODULE``; with
 below positionally, exactly as it calls ``jakal_net_native`` (native_backend.py:5359-6021).
 
 Every op runs on the GPU through ``libjakal_b200.so`` (C ABI in include/jakal_b200.h).
-There is no CPU path: CPU tensors, unsupported kinds or dtypes raise instead of falling
-back to another implementation.
+There is no CPU path: CPU tensors and unsupported compressors raise ``RuntimeError``;
+scorer / route kinds this backend does not implement raise ``TypeError`` (the error the
+reference's own dispatch treats as "not supported here", transition.py:620-623).
+
+Two kernel families serve every op:
+  * the fused kernels (tcgen05 score tiles kept on chip, streaming top-k, aggregate) for
+    k <= 64 and single-head scorers of padded rank <= 128 with 16-bit projections, or f32
+    projections of rank <= 32 (three-plane split), and multi-head scorers within the kernel
+    head limits;
+  * the select-aggregate kernel (jk_select_aggregate_forward) over materialised f32 score
+    blocks -- a plain GEMM of the projections -- for everything else the reference accepts:
+    any k, any score rank, f32 projections of any rank, diagonal / full bilinear scorers of
+    any width. It is exact (radix select) and reproduces the reference's blocked paths that
+    take any k (jakal_net_native.cpp:6390-6447, 6916-7087, 7089-7246).
+Under CUDA autocast the scorer inputs are cast to the autocast dtype before the projection
+GEMMs, as the reference's at::matmul inside its extension is (jakal_net_native.cpp:6236-6239
+runs within the caller's autocast region); values, states and outputs keep their dtypes.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import functools
+import threading
 from typing import Optional
 
 import torch
@@ -53,7 +71,10 @@ _ROUTE_CODE = {
     "signed_abs_softmax": _lib.JK_SIGNED_ABS_SOFTMAX,
     "signed_entmax15": _lib.JK_SIGNED_ENTMAX15,
 }
-_MAX_K = 64
+_MAX_K = 64  # fused kernels; larger k takes the select-aggregate kernel
+# f32 score elements per materialised block of the select-aggregate path (256 MiB)
+_SCORE_BUDGET = 1 << 26
+_TLS = threading.local()
 # MultiHeadPairwise aggregate -> jk_heads_t.combine (kernel_common.py:151-178 spec kinds
 # multihead_{max,smoothmax,signed_smoothmax}_low_rank_bilinear)
 _HEAD_COMBINE = {
@@ -90,6 +111,47 @@ def backend_name() -> str:
 
 
 # ----------------------------------------------------------------------------- helpers
+def _entry(fn):
+    """Op entry: records the caller's CUDA autocast dtype (the scorer inputs follow it, see
+    the module docstring), then runs the op with autocast and autograd off -- the module's
+    own torch calls are plain library work on already-decided dtypes, and its outputs are
+    fresh tensors like the reference extension's (no autograd graph)."""
+
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        prev = getattr(_TLS, "autocast", None)
+        _TLS.autocast = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else None
+        try:
+            with torch.autocast("cuda", enabled=False), torch.no_grad():
+                return fn(*args, **kwargs)
+        finally:
+            _TLS.autocast = prev
+
+    return wrapper
+
+
+def _scorer_input(x: Tensor) -> Tensor:
+    """The scorer (projection GEMM) input in the dtype the reference's at::matmul would use:
+    f32 inputs are cast to the caller's autocast dtype when an op was called under CUDA
+    autocast."""
+    ac = getattr(_TLS, "autocast", None)
+    if ac is not None and x.dtype == torch.float32:
+        return x.to(ac)
+    return x
+
+
+@contextlib.contextmanager
+def _exact_f32_matmul():
+    """f32 GEMMs in full f32 (TF32 off) for the duration of the block: the projections and
+    score blocks of f32 inputs follow the reference's f32 torch::matmul."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        yield
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def _ptr(t: Optional[Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
@@ -131,10 +193,21 @@ def _flatten_state(t: Tensor) -> Tensor:
     return t.reshape(-1, t.shape[-1]).contiguous()
 
 
+def _pad_dim8(x2: Tensor, w: Tensor) -> tuple[Tensor, Tensor]:
+    """Zero-pads the contraction dim of a projection to a multiple of 8 (16-byte TMA rows);
+    the padded columns add exact zeros to every dot product."""
+    pad = (-x2.shape[-1]) % 8
+    if pad:
+        x2 = torch.nn.functional.pad(x2, (0, pad))
+        w = torch.nn.functional.pad(w, (0, pad))
+    return x2.contiguous(), w.contiguous()
+
+
 def lowrank_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None,
                     temperature: float = 1.0) -> Tensor:
     """round(x @ weight^T) [* core] [/ temperature] in x's dtype, padded to a multiple of
     64 columns (jakal_net_native.cpp:6236-6239, 6977-6986). x [..., D] -> [..., rp].
+    16-bit x: rank <= 128, any D (zero-padded to a multiple of 8).
 
     f32 inputs (rank <= 32): the f32 projection (a plain f32 GEMM, like the reference's
     torch::matmul) is returned as three bf16 planes [h | m | l | 0] (rp = 128) whose six
@@ -146,26 +219,23 @@ def lowrank_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None,
     x2 = x.reshape(-1, dim).contiguous()
     if x.dtype == torch.float32:
         if rank > 32:
-            raise RuntimeError(f"b200_sm100a f32 scoring supports score rank <= 32 (got {rank}).")
-        proj = torch.matmul(x2, weight.detach().to(device=x.device, dtype=torch.float32).t())
-        if core is not None:
-            proj = proj * core.detach().reshape(-1).to(device=x.device, dtype=torch.float32)
-        if float(temperature) != 1.0:
-            proj = proj / float(temperature)
-        proj = proj.contiguous()
+            raise RuntimeError(f"b200_sm100a three-plane f32 scoring supports score rank <= 32 (got {rank}).")
+        proj = _generic_project(x2, weight, core, temperature)
         out = torch.empty((x2.shape[0], 128), device=x.device, dtype=torch.bfloat16)
         with torch.cuda.device(x.device):
             check(_LIBRARY.jk_split3_bf16(proj.data_ptr(), x2.shape[0], rank, out.data_ptr(), _stream(x.device)),
                   "jk_split3_bf16")
         return out.reshape(*x.shape[:-1], 128)
     code = _proj_dtype(x)
-    w = weight.detach().to(device=x.device, dtype=x.dtype).contiguous()
+    if rank > 128:
+        raise RuntimeError(f"b200_sm100a fused projections support score rank <= 128 (got {rank}).")
+    x2, w = _pad_dim8(x2, weight.detach().to(device=x.device, dtype=x.dtype))
     c = None if core is None else core.detach().reshape(-1).to(device=x.device, dtype=x.dtype).contiguous()
     rp = int(_LIBRARY.jk_padded_rank(rank))
     out = torch.empty((x2.shape[0], rp), device=x.device, dtype=x.dtype)
     with torch.cuda.device(x.device):
         check(
-            _LIBRARY.jk_lowrank_project(x2.data_ptr(), x2.shape[0], dim, w.data_ptr(), rank, _ptr(c),
+            _LIBRARY.jk_lowrank_project(x2.data_ptr(), x2.shape[0], x2.shape[1], w.data_ptr(), rank, _ptr(c),
                                         float(temperature), code, out.data_ptr(), rp, _stream(x.device)),
             "jk_lowrank_project",
         )
@@ -181,20 +251,33 @@ def lowrank_project_pair(x: Tensor, weight: Tensor, weight2: Tensor, core: Optio
     rank, dim = weight.shape
     if (x.dtype == torch.float32 or rank > 64 or tuple(weight2.shape) != (rank, dim) or x.shape[-1] != dim):
         return lowrank_project(x, weight), lowrank_project(x, weight2, core=core, temperature=temperature)
-    x2 = x.reshape(-1, dim).contiguous()
-    w = weight.detach().to(device=x.device, dtype=x.dtype).contiguous()
-    w2 = weight2.detach().to(device=x.device, dtype=x.dtype).contiguous()
+    x2, w = _pad_dim8(x.reshape(-1, dim), weight.detach().to(device=x.device, dtype=x.dtype))
+    _, w2 = _pad_dim8(x2[:0, :dim], weight2.detach().to(device=x.device, dtype=x.dtype))
     c = None if core is None else core.detach().reshape(-1).to(device=x.device, dtype=x.dtype).contiguous()
     out = torch.empty((x2.shape[0], 64), device=x.device, dtype=x.dtype)
     out2 = torch.empty((x2.shape[0], 64), device=x.device, dtype=x.dtype)
     with torch.cuda.device(x.device):
         check(
-            _LIBRARY.jk_lowrank_project_pair(x2.data_ptr(), x2.shape[0], dim, w.data_ptr(), w2.data_ptr(), rank, _ptr(c),
-                                             float(temperature), _proj_dtype(x), out.data_ptr(), out2.data_ptr(),
-                                             _stream(x.device)),
+            _LIBRARY.jk_lowrank_project_pair(x2.data_ptr(), x2.shape[0], x2.shape[1], w.data_ptr(), w2.data_ptr(),
+                                             rank, _ptr(c), float(temperature), _proj_dtype(x), out.data_ptr(),
+                                             out2.data_ptr(), _stream(x.device)),
             "jk_lowrank_project_pair",
         )
     return out.reshape(*x.shape[:-1], 64), out2.reshape(*x.shape[:-1], 64)
+
+
+def _generic_project(x2: Tensor, weight: Optional[Tensor], core: Optional[Tensor] = None,
+                     temperature: float = 1.0) -> Tensor:
+    """Projection for the select-aggregate path, with the reference's rounding points
+    (jakal_net_native.cpp:6236-6239, 6977-6986): p = x @ weight^T (weight None: the
+    identity), then * core, then / temperature, each in x's dtype; returned as f32."""
+    with _exact_f32_matmul():
+        p = x2 if weight is None else torch.matmul(x2, weight.detach().to(device=x2.device, dtype=x2.dtype).t())
+    if core is not None:
+        p = p * core.detach().reshape(-1).to(device=x2.device, dtype=x2.dtype)
+    if float(temperature) != 1.0:
+        p = p / float(temperature)
+    return p.float().contiguous()
 
 
 def _bias_tensor(bias: Optional[Tensor], device: torch.device, scale: float = 1.0) -> Optional[Tensor]:
@@ -226,11 +309,11 @@ def _multihead_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None,
     projection row: head h at columns [16 kph h, 16 kph h + R), zeros elsewhere. weight
     [H, R, D], core [H, R]. Returns (proj [..., rp], kph)."""
     if x.dtype == torch.float32:
-        raise RuntimeError("b200_sm100a multi-head scorers take bf16 / f16 inputs.")
+        raise TypeError("b200_sm100a multi-head scorers take bf16 / f16 inputs.")
     H, R, D = weight.shape
     rb = -(-R // 16) * 16
     if H * rb > 128:
-        raise RuntimeError(f"b200_sm100a multi-head scorers need heads * roundup16(rank) <= 128 (got {H} x {R}).")
+        raise TypeError(f"b200_sm100a multi-head scorers need heads * roundup16(rank) <= 128 (got {H} x {R}).")
     w = weight.detach().new_zeros((H, rb, D))
     w[:, :R] = weight.detach()
     c = None
@@ -254,51 +337,134 @@ def _head_bias(bias: Optional[Tensor], heads: int, device: torch.device, scale: 
     return (b / scale).contiguous()
 
 
-def _diagonal_projections(target_val: Tensor, source_val: Tensor, w_hat: Tensor, temperature: float = 1.0):
-    """Diagonal bilinear scorer (modules.py:37-53, 385-412): score = target . (source * w_hat).
-    The projections are identity / diag(w_hat) GEMMs through jk_lowrank_project: one exact
-    product per output, rounded once -- the reference's elementwise multiply."""
-    D = target_val.shape[-1]
-    if source_val.shape[-1] != D or w_hat.numel() != D:
-        raise RuntimeError("diagonal bilinear scorer needs matching dims.")
-    eye = torch.eye(D, device=target_val.device, dtype=torch.float32)
-    row_proj = lowrank_project(target_val, eye)
-    col_proj = lowrank_project(source_val, eye, core=w_hat, temperature=temperature)
-    return row_proj, col_proj
+# ----------------------------------------------------------------------------- scorers
+class Scorer:
+    """Projections of one call. fused: 16-bit (or three-plane f32) padded projections for
+    the fused kernels, with `heads` for multi-head scorers; otherwise f32 projections
+    [B, rows, R] for the select-aggregate path. `bias` is the scalar device bias or None."""
+
+    def __init__(self, row: Tensor, col: Tensor, bias: Optional[Tensor], fused: bool,
+                 heads: Optional[Heads] = None, split3: bool = False):
+        self.row, self.col, self.bias, self.fused, self.heads, self.split3 = row, col, bias, fused, heads, split3
+
+
+def _fused_rank_ok(x: Tensor, rank: int) -> bool:
+    if x.dtype == torch.float32:
+        return rank <= 32
+    return x.dtype in (torch.bfloat16, torch.float16) and rank <= 128
+
+
+def _single_scorer(tx: Tensor, sx: Tensor, t_weight: Optional[Tensor], s_weight: Optional[Tensor],
+                   core: Optional[Tensor], temperature: float, bias: Optional[Tensor], rank: int,
+                   fused: bool, pair: bool = False) -> Scorer:
+    """Single-head low-rank form shared by every single-head kind: row = tx @ t_weight^T,
+    col = (sx @ s_weight^T) * core / temperature (a weight of None is the identity).
+
+    f32 inputs whose whole score matrix fits one materialised block take the
+    select-aggregate path even when the fused three-plane form would apply: it scores,
+    compresses and aggregates in plain f32 like the reference's f32 kernels."""
+    pairs = (tx.numel() // max(1, tx.shape[-1])) * sx.shape[-2]
+    if tx.dtype == torch.float32 and pairs <= _SCORE_BUDGET:
+        fused = False
+    if fused and _fused_rank_ok(tx, rank):
+        dim = tx.shape[-1]
+        eye = None
+        if t_weight is None or s_weight is None:
+            eye = torch.eye(dim, device=tx.device, dtype=torch.float32)
+        tw = eye if t_weight is None else t_weight
+        sw = eye if s_weight is None else s_weight
+        if pair and tw.shape == sw.shape:
+            row, col = lowrank_project_pair(tx, tw, sw, core=core, temperature=temperature)
+        else:
+            row = lowrank_project(tx, tw)
+            col = lowrank_project(sx, sw, core=core, temperature=temperature)
+        return Scorer(row, col, bias, True, split3=tx.dtype == torch.float32)
+    row = _generic_project(tx.reshape(-1, tx.shape[-1]), t_weight).reshape(*tx.shape[:-1], -1)
+    col = _generic_project(sx.reshape(-1, sx.shape[-1]), s_weight, core, temperature).reshape(*sx.shape[:-1], -1)
+    return Scorer(row, col, bias, False)
 
 
 def _pair_scorer(kind: str, weight: Tensor, bias, in_weight, in_bias, out_weight, out_bias, target_val: Tensor,
-                 source_val: Tensor):
-    """Projections of a pairwise spec (kernel_common.py:151-192): low_rank_bilinear,
-    diagonal_bilinear (dim <= 128) or multihead_{max,smoothmax,signed_smoothmax}_low_rank_bilinear.
-    Returns (row_proj [target], col_proj [source, * core], scalar bias tensor or None, Heads or None)."""
+                 source_val: Tensor, fused: bool = True) -> Scorer:
+    """Projections of a pairwise spec (kernel_common.py:151-212): low_rank_bilinear,
+    diagonal_bilinear, bilinear (full D x D: score = t . (W s), modules.py:56-72) or
+    multihead_{max,smoothmax,signed_smoothmax}_low_rank_bilinear. `fused` False forces the
+    select-aggregate form (e.g. k > 64). Other kinds raise TypeError."""
+    tx, sx = _scorer_input(target_val), _scorer_input(source_val)
+    if tx.dtype != sx.dtype:
+        raise RuntimeError("target and source values must share a dtype.")
+    dev = target_val.device
     if kind == "diagonal_bilinear":
-        row_proj, col_proj = _diagonal_projections(target_val, source_val, weight)
-        return row_proj, col_proj, _bias_tensor(bias, target_val.device), None
-    if in_weight is None or out_weight is None:
-        raise RuntimeError("Low-rank bilinear pairwise kernel is missing projection weights.")
-    if in_bias is not None or out_bias is not None:
-        raise RuntimeError("Low-rank bilinear projections take no bias.")
+        dim = tx.shape[-1]
+        if weight is None or weight.numel() != dim:
+            raise RuntimeError("diagonal bilinear scorer needs a weight of the value dim.")
+        return _single_scorer(tx, sx, None, None, weight, 1.0, _bias_tensor(bias, dev), dim, fused)
+    if kind == "bilinear":
+        dim = tx.shape[-1]
+        if weight is None or tuple(weight.shape) != (dim, dim):
+            raise RuntimeError("bilinear scorer needs a [dim, dim] weight.")
+        return _single_scorer(tx, sx, None, weight, None, 1.0, _bias_tensor(bias, dev), dim, fused)
     if kind == "low_rank_bilinear":
-        if target_val is source_val:  # propagation: both projections in one pass over the values
-            row_proj, col_proj = lowrank_project_pair(target_val, out_weight, in_weight, core=weight)
-        else:
-            row_proj = lowrank_project(target_val, out_weight)                # target side
-            col_proj = lowrank_project(source_val, in_weight, core=weight)    # source side, * w_hat
-        return row_proj, col_proj, _bias_tensor(bias, target_val.device), None
+        if in_weight is None or out_weight is None:
+            raise RuntimeError("Low-rank bilinear pairwise kernel is missing projection weights.")
+        if in_bias is not None or out_bias is not None:
+            raise TypeError("Low-rank bilinear projections take no bias.")
+        return _single_scorer(tx, sx, out_weight, in_weight, weight, 1.0, _bias_tensor(bias, dev),
+                              out_weight.shape[0], fused, pair=target_val is source_val)
     prefix, base = "multihead_", "_low_rank_bilinear"
     agg = kind[len(prefix):-len(base)] if kind.startswith(prefix) and kind.endswith(base) else None
     if agg not in _HEAD_COMBINE:
-        raise RuntimeError(f"Unsupported pairwise kernel kind for b200_sm100a: {kind}")
-    if in_weight.dim() != 3 or out_weight.dim() != 3:
+        raise TypeError(f"Unsupported pairwise kernel kind for b200_sm100a: {kind}")
+    if not fused:
+        raise TypeError("b200_sm100a multi-head scorers run in the fused kernels only (k <= 64).")
+    if in_weight is None or out_weight is None or in_weight.dim() != 3 or out_weight.dim() != 3:
         raise RuntimeError("multi-head projection weights must be [heads, rank, dim].")
     H = in_weight.shape[0]
-    row_proj, kph = _multihead_project(target_val, out_weight)
-    col_proj, _ = _multihead_project(source_val, in_weight, core=weight)
-    heads = Heads(H, kph, _HEAD_COMBINE[agg], _head_bias(bias, H, target_val.device))
-    return row_proj, col_proj, None, heads
+    row, kph = _multihead_project(tx, out_weight)
+    col, _ = _multihead_project(sx, in_weight, core=weight)
+    return Scorer(row, col, None, True, heads=Heads(H, kph, _HEAD_COMBINE[agg], _head_bias(bias, H, dev)))
 
 
+def _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                       hidden_weight, hidden_bias, out_weight, out_bias, temperature, src_val, dst_val,
+                       fused: bool = True) -> Scorer:
+    """Route projections (kernel_common.py:238-295): low_rank_bilinear_route,
+    diagonal_bilinear_route or multihead_max_low_rank_bilinear_route; logits =
+    (ps . pd + b) / T. Returns a Scorer whose row side is the source (src_proj / T) and
+    column side the destination. Other route kinds raise TypeError."""
+    if route_kind not in ("low_rank_bilinear_route", "multihead_max_low_rank_bilinear_route",
+                          "diagonal_bilinear_route"):
+        raise TypeError(f"Unsupported pairwise route kind for b200_sm100a: {route_kind}")
+    temperature = float(temperature)
+    if temperature <= 0.0:
+        raise RuntimeError("route temperature must be positive.")
+    sx, dx = _scorer_input(src_val), _scorer_input(dst_val)
+    dev = src_val.device
+    if route_kind == "diagonal_bilinear_route":
+        if any(t is not None for t in (source_weight, source_bias, target_weight, target_bias, hidden_weight,
+                                       hidden_bias, out_weight, out_bias)):
+            raise TypeError("Diagonal routes take no projection / hidden layers.")
+        sc = _single_scorer(dx, sx, None, None, core_weight, temperature, None, dx.shape[-1], fused)
+        return Scorer(sc.col, sc.row, _bias_tensor(bias, dev, temperature), sc.fused, split3=sc.split3)
+    if source_weight is None or target_weight is None:
+        raise RuntimeError("Low-rank route kernel is missing projection weights.")
+    if any(t is not None for t in (source_bias, target_bias, hidden_weight, hidden_bias, out_weight, out_bias)):
+        raise TypeError("Low-rank route projections take no bias / hidden layers.")
+    if route_kind == "multihead_max_low_rank_bilinear_route":
+        if not fused:
+            raise TypeError("b200_sm100a multi-head routes run in the fused kernels only (k <= 64).")
+        # max_h(l_h) / T == max_h(l_h / T): every head's source projection and bias take the 1 / T
+        H = source_weight.shape[0]
+        src_proj, kph = _multihead_project(sx, source_weight, core=core_weight, temperature=temperature)
+        dst_proj, _ = _multihead_project(dx, target_weight)
+        return Scorer(src_proj, dst_proj, None, True,
+                      heads=Heads(H, kph, _lib.JK_HEADS_MAX, _head_bias(bias, H, dev, temperature)))
+    sc = _single_scorer(dx, sx, target_weight, source_weight, core_weight, temperature, None,
+                        source_weight.shape[0], fused)
+    return Scorer(sc.col, sc.row, _bias_tensor(bias, dev, temperature), sc.fused, split3=sc.split3)
+
+
+# ----------------------------------------------------------------------------- raw kernels
 def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, k: int, *,
                    window: int = -1, compress: int = _lib.JK_SOFTSIGN, col_sender: Optional[Tensor] = None,
                    bias: Optional[Tensor] = None, score_bias: float = 0.0,
@@ -349,252 +515,64 @@ def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_va
     return out_state, out_val
 
 
-def _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
-                           layer_val, projected_state, projected_val, topk: int, window: int):
-    if edge_compress_name not in _EDGE_CODE:
-        raise RuntimeError(
-            "Only edge_compress_name in {softsign, signed_abs_softmax, signed_entmax15} is supported by the native backend."
-        )
-    if topk <= 0:
-        raise RuntimeError("topk must be positive.")
-    for name, t in (("layer_val", layer_val), ("projected_state", projected_state), ("projected_val", projected_val)):
+def select_aggregate(row_f: Tensor, col_f: Tensor, state: Tensor, val: Tensor, k: int, *, window: int = -1,
+                     compress: int = _lib.JK_SOFTSIGN, sender: Optional[Tensor] = None,
+                     bias: Optional[Tensor] = None, scatter: bool = False, out_dtype: Optional[torch.dtype] = None,
+                     return_selection: bool = False, budget: int = _SCORE_BUDGET):
+    """Select-aggregate over materialised score blocks (jk_select_aggregate_forward): any k,
+    any rank. row_f [B, T, R] and col_f [B, S, R] are f32 projections; every block of rows
+    gets its f32 scores from one GEMM (TF32 off) and then the exact select / compress /
+    aggregate kernel.
+
+    gather (scatter False): state / sender [B, S], val [B, S, D] per column; returns
+    (state [B, T], val [B, T, D]) in out_dtype. scatter True (per-source transition): rows
+    are sources with state / sender [B, T], val [B, T, D]; returns the f32 destination sums
+    (state [B, S], val [B, S, D]). With return_selection the selected scores (bias
+    included) and columns [B, T, min(k, S)] follow, in ascending column order per row."""
+    for name, t in (("row_f", row_f), ("col_f", col_f), ("state", state), ("val", val)):
         _require_cuda(name, t)
-    batch_shape = layer_val.shape[:-2]
-    n = layer_val.shape[-2]
-    out_dim = projected_val.shape[-1]
-    val = _flatten_val(layer_val)
-    pstate = _flatten_state(projected_state)
-    pval = _flatten_val(projected_val)
-    k = min(int(topk), n)
-    if k > _MAX_K:
-        raise RuntimeError(f"b200_sm100a top-k supports k <= {_MAX_K} (got {k}).")
-    row_proj, col_proj, bias_t, heads = _pair_scorer(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
-                                                     val, val)
-    same = projected_state.dtype == projected_val.dtype
-    out_dtype = projected_val.dtype if same else torch.float32
-    state, out = topk_aggregate(row_proj, col_proj, pstate, pval, k, window=window,
-                                compress=_EDGE_CODE[edge_compress_name], bias=bias_t, out_dtype=out_dtype,
-                                split3=val.dtype == torch.float32, heads=heads)
-    state = state.to(projected_state.dtype).reshape(*batch_shape, n)
-    out = out.to(projected_val.dtype).reshape(*batch_shape, n, out_dim)
-    return state, out
-
-
-def propagation_topk(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
-                     layer_val, projected_state, projected_val, topk, target_block_size, source_block_size):
-    """SparsePropagation(sparse_type="topk") forward: per target, top-k over every source
-    (no causal mask), edges over the k, aggregate. Reference op: jakal_net_native.cpp:6305-6447
-    (CUDA fast path :6355-6389). Block sizes are accepted for signature parity; the fused
-    kernel tiles internally."""
-    return _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
-                                  edge_compress_name, layer_val, projected_state, projected_val, topk, -1)
-
-
-def propagation_window_topk(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
-                            layer_val, projected_state, projected_val, window, topk, target_block_size=0,
-                            source_block_size=0):
-    """Window-intersect-top-k propagation: causal window mask (kernel_common.py:443-456),
-    then top-k among the visible sources (rows with fewer visible sources use all of them),
-    edges over the survivors (propagation.py:67-88). Not a reference op; the benchmark
-    configurations that combine a causal window with top-k use it."""
-    if window < 0:
-        raise RuntimeError("window must be non-negative.")
-    return _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
-                                  edge_compress_name, layer_val, projected_state, projected_val, topk, int(window))
-
-
-def _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
-                       hidden_weight, hidden_bias, out_weight, out_bias, temperature, src_val, dst_val):
-    """Route projections (kernel_common.py:238-295): low_rank_bilinear_route,
-    diagonal_bilinear_route (dim <= 128) or multihead_max_low_rank_bilinear_route;
-    logits = (ps . pd + b) / T. Returns (src_proj / T, dst_proj, scalar bias / T or None,
-    Heads or None)."""
-    if route_kind not in ("low_rank_bilinear_route", "multihead_max_low_rank_bilinear_route",
-                          "diagonal_bilinear_route"):
-        raise TypeError(f"Unsupported pairwise route kind for b200_sm100a: {route_kind}")
-    temperature = float(temperature)
-    if temperature <= 0.0:
-        raise RuntimeError("route temperature must be positive.")
-    if route_kind == "diagonal_bilinear_route":
-        if any(t is not None for t in (source_weight, source_bias, target_weight, target_bias, hidden_weight,
-                                       hidden_bias, out_weight, out_bias)):
-            raise TypeError("Diagonal routes take no projection / hidden layers.")
-        dst_proj, src_proj = _diagonal_projections(dst_val, src_val, core_weight, temperature)
-        return src_proj, dst_proj, _bias_tensor(bias, src_val.device, temperature), None
-    if source_weight is None or target_weight is None:
-        raise RuntimeError("Low-rank route kernel is missing projection weights.")
-    if any(t is not None for t in (source_bias, target_bias, hidden_weight, hidden_bias, out_weight, out_bias)):
-        raise TypeError("Low-rank route projections take no bias / hidden layers.")
-    if route_kind == "multihead_max_low_rank_bilinear_route":
-        # max_h(l_h) / T == max_h(l_h / T): every head's source projection and bias take the 1 / T
-        H = source_weight.shape[0]
-        src_proj, kph = _multihead_project(src_val, source_weight, core=core_weight, temperature=temperature)
-        dst_proj, _ = _multihead_project(dst_val, target_weight)
-        heads = Heads(H, kph, _lib.JK_HEADS_MAX, _head_bias(bias, H, src_val.device, temperature))
-        return src_proj, dst_proj, None, heads
-    src_proj = lowrank_project(src_val, source_weight, core=core_weight, temperature=temperature)
-    dst_proj = lowrank_project(dst_val, target_weight)
-    return src_proj, dst_proj, _bias_tensor(bias, src_val.device, temperature), None
-
-
-def transition_query_topk(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
-                          hidden_weight, hidden_bias, out_weight, out_bias, temperature, sender_strength, src_val,
-                          query_val, projected_state, projected_val, topk, query_block_size, source_block_size,
-                          use_cuda_reduce=True):
-    """Per-query transition (jakal_net_native.cpp:7089-7246): each query slot takes its
-    top-k sources by route logit, softmax over the k, sender-weighted gather."""
-    for name, t in (("sender_strength", sender_strength), ("src_val", src_val), ("query_val", query_val),
-                    ("projected_state", projected_state), ("projected_val", projected_val)):
-        _require_cuda(name, t)
-    if topk <= 0:
-        raise RuntimeError("topk must be positive.")
-    batch_shape = query_val.shape[:-2]
-    n_query = query_val.shape[-2]
-    n_src = src_val.shape[-2]
-    out_dim = projected_val.shape[-1]
-    sv = _flatten_val(src_val)
-    qv = _flatten_val(query_val)
-    k = min(int(topk), n_src)
-    if k > _MAX_K:
-        raise RuntimeError(f"b200_sm100a top-k supports k <= {_MAX_K} (got {k}).")
-    src_proj, q_proj, bias_t, heads = _route_projections(route_kind, source_weight, source_bias, target_weight,
-                                                         target_bias, core_weight, bias, hidden_weight, hidden_bias,
-                                                         out_weight, out_bias, temperature, sv, qv)
-    pstate = _flatten_state(projected_state)
-    sender = _flatten_state(sender_strength).to(pstate.dtype)
-    pval = _flatten_val(projected_val)
-    same = projected_state.dtype == projected_val.dtype
-    out_dtype = projected_val.dtype if same else torch.float32
-    state, out = topk_aggregate(q_proj, src_proj, pstate, pval, k, window=-1, compress=_lib.JK_SOFTMAX,
-                                col_sender=sender, bias=bias_t, out_dtype=out_dtype, split3=sv.dtype == torch.float32,
-                                heads=heads)
-    return (state.to(projected_state.dtype).reshape(*batch_shape, n_query),
-            out.to(projected_val.dtype).reshape(*batch_shape, n_query, out_dim))
-
-
-def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
-                             hidden_weight, hidden_bias, out_weight, out_bias, temperature, sender_strength, src_val,
-                             dst_val, projected_state, projected_val, topk, src_block_size, dst_block_size,
-                             route_compress_name="softmax"):
-    """SparseTransition forward (jakal_net_native.cpp:6916-7087): each source takes its
-    top-k destinations by route logit, routes compressed over the k, sender-weighted
-    scatter-add into the destinations."""
-    for name, t in (("sender_strength", sender_strength), ("src_val", src_val), ("dst_val", dst_val),
-                    ("projected_state", projected_state), ("projected_val", projected_val)):
-        _require_cuda(name, t)
-    if topk <= 0:
-        raise RuntimeError("topk must be positive.")
-    if route_compress_name not in _ROUTE_CODE:
-        raise RuntimeError(f"Unsupported route compress {route_compress_name!r}")
-    batch_shape = src_val.shape[:-2]
-    n_src = src_val.shape[-2]
-    n_dst = dst_val.shape[-2]
-    out_dim = projected_val.shape[-1]
-    sv = _flatten_val(src_val)
-    dv = _flatten_val(dst_val)
-    k = min(int(topk), n_dst)
-    if k > _MAX_K:
-        raise RuntimeError(f"b200_sm100a top-k supports k <= {_MAX_K} (got {k}).")
-    src_proj, dst_proj, bias_t, heads = _route_projections(route_kind, source_weight, source_bias, target_weight,
-                                                           target_bias, core_weight, bias, hidden_weight,
-                                                           hidden_bias, out_weight, out_bias, temperature, sv, dv)
-    pstate = _flatten_state(projected_state)
-    sender = _flatten_state(sender_strength).to(pstate.dtype)
-    pval = _flatten_val(projected_val)
-    B = sv.shape[0]
-    dev = sv.device
-    same = projected_state.dtype == projected_val.dtype
-    out_dtype = projected_val.dtype if same else torch.float32
-    accum = torch.empty(B * n_dst * (out_dim + 1) + 4, device=dev, dtype=torch.float32)
-    out_state = torch.empty((B, n_dst), device=dev, dtype=out_dtype)
-    out_val = torch.empty((B, n_dst, out_dim), device=dev, dtype=out_dtype)
-    args = (src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1],
-            _proj_dtype(src_proj, sv.dtype == torch.float32),
-            pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
-            pval.data_ptr(), out_dim, _dtype_code("val", pval),
-            k, 0.0, _ptr(bias_t), _ROUTE_CODE[route_compress_name], accum.data_ptr(),
-            out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
+    B, T, _ = row_f.shape
+    S = col_f.shape[1]
+    D = val.shape[-1]
+    dev = val.device
+    kk = max(1, min(int(k), S))
+    state = state.contiguous()
+    val = val.contiguous()
+    snd = None if sender is None else sender.to(state.dtype).contiguous()
+    out_dtype = out_dtype or val.dtype
+    if scatter:
+        acc_state = torch.zeros((B, S), device=dev, dtype=torch.float32)
+        acc_val = torch.zeros((B, S, D), device=dev, dtype=torch.float32)
+        out_state = out_val = None
+    else:
+        out_state = torch.empty((B, T), device=dev, dtype=out_dtype)
+        out_val = torch.empty((B, T, D), device=dev, dtype=out_dtype)
+        acc_state = acc_val = None
+    chunk = max(1, min(T, budget // max(1, B * (S + 3 * kk))))
+    if return_selection:
+        all_s = torch.empty((B, T, kk), device=dev, dtype=torch.float32)
+        all_i = torch.empty((B, T, kk), device=dev, dtype=torch.int64)
+    sel_s = torch.empty((B, chunk, kk), device=dev, dtype=torch.float32)
+    sel_i = torch.empty((B, chunk, kk), device=dev, dtype=torch.int64)
+    col_t = col_f.transpose(1, 2)
     with torch.cuda.device(dev):
-        if heads is None:
-            check(_LIBRARY.jk_transition_pairwise_topk_forward(*args, _stream(dev)),
-                  "jk_transition_pairwise_topk_forward")
-        else:
-            check(_LIBRARY.jk_transition_pairwise_topk_forward_mh(*args, heads.ref(), _stream(dev)),
-                  "jk_transition_pairwise_topk_forward_mh")
-    return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
-            out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))
-
-
-def _value_planes(pval: Tensor, proj_dtype: torch.dtype):
-    """Values for the window-kernel value GEMM: padded to 64 columns; f32 values become bf16
-    hi + lo planes (both multiplied by the hi + lo edge planes). Returns (val, val_lo, pad)."""
-    out_dim = pval.shape[-1]
-    pad = (-out_dim) % 64
-    if pad:
-        pval = torch.nn.functional.pad(pval, (0, pad))
-    pval_lo = None
-    if proj_dtype == torch.float32:
-        pval = pval.float().contiguous()
-        hi = torch.empty(pval.shape, device=pval.device, dtype=torch.bfloat16)
-        pval_lo = torch.empty_like(hi)
-        with torch.cuda.device(pval.device):
-            check(_LIBRARY.jk_split2_bf16(pval.data_ptr(), pval.numel(), hi.data_ptr(), pval_lo.data_ptr(),
-                                          _stream(pval.device)), "jk_split2_bf16")
-        pval = hi
-    elif pval.dtype != proj_dtype:
-        pval = pval.to(proj_dtype)
-    return pval.contiguous(), pval_lo, pad
-
-
-def transition_pairwise_dense(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
-                              hidden_weight, hidden_bias, out_weight, out_bias, route_compress_name, temperature,
-                              sender_strength, src_val, dst_val, projected_state, projected_val, src_block_size,
-                              dst_block_size):
-    """Dense pairwise Transition forward (jakal_net_native.cpp:6705-6914; transition.py:238-254):
-    routes of every source compressed over all destinations, sender-weighted, accumulated into
-    the destinations. Two fused launches: per-source route statistics, then the per-destination
-    aggregate with per-column normalisation."""
-    for name, t in (("sender_strength", sender_strength), ("src_val", src_val), ("dst_val", dst_val),
-                    ("projected_state", projected_state), ("projected_val", projected_val)):
-        _require_cuda(name, t)
-    if route_compress_name not in _ROUTE_CODE:
-        raise RuntimeError(f"Unsupported route compress {route_compress_name!r}")
-    batch_shape = src_val.shape[:-2]
-    n_src = src_val.shape[-2]
-    n_dst = dst_val.shape[-2]
-    out_dim = projected_val.shape[-1]
-    sv = _flatten_val(src_val)
-    dv = _flatten_val(dst_val)
-    src_proj, dst_proj, bias_t, heads = _route_projections(route_kind, source_weight, source_bias, target_weight,
-                                                           target_bias, core_weight, bias, hidden_weight,
-                                                           hidden_bias, out_weight, out_bias, temperature, sv, dv)
-    pstate = _flatten_state(projected_state)
-    sender = _flatten_state(sender_strength).to(pstate.dtype).contiguous()
-    pval, pval_lo, pad = _value_planes(_flatten_val(projected_val), sv.dtype)
-    B = sv.shape[0]
-    dev = sv.device
-    same = projected_state.dtype == projected_val.dtype
-    out_dtype = projected_val.dtype if same else torch.float32
-    stats = torch.empty(B * n_src * 3, device=dev, dtype=torch.float32)
-    out_state = torch.empty((B, n_dst), device=dev, dtype=out_dtype)
-    out_val = torch.empty((B, n_dst, pval.shape[-1]), device=dev, dtype=out_dtype)
-    args = (src_proj.data_ptr(), dst_proj.data_ptr(), B, n_src, n_dst, src_proj.shape[-1],
-            _proj_dtype(src_proj, sv.dtype == torch.float32),
-            pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
-            pval.data_ptr(), _ptr(pval_lo), pval.shape[-1],
-            0.0, _ptr(bias_t), _ROUTE_CODE[route_compress_name], stats.data_ptr(),
-            out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
-    with torch.cuda.device(dev):
-        if heads is None:
-            check(_LIBRARY.jk_transition_pairwise_dense_forward(*args, _stream(dev)),
-                  "jk_transition_pairwise_dense_forward")
-        else:
-            check(_LIBRARY.jk_transition_pairwise_dense_forward_mh(*args, heads.ref(), _stream(dev)),
-                  "jk_transition_pairwise_dense_forward_mh")
-    if pad:
-        out_val = out_val[..., :out_dim]
-    return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
-            out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))
+        for r0 in range(0, T, chunk):
+            rc = min(chunk, T - r0)
+            with _exact_f32_matmul():
+                sc = torch.bmm(row_f[:, r0:r0 + rc], col_t).contiguous()
+            check(_LIBRARY.jk_select_aggregate_forward(
+                sc.data_ptr(), B, T, S, r0, rc, state.data_ptr(), _ptr(snd), _dtype_code("state", state),
+                val.data_ptr(), D, _dtype_code("val", val), kk, int(window), 0.0, _ptr(bias), compress,
+                1 if scatter else 0, _ptr(out_state), _ptr(out_val), _dtype_code("out", out_state if out_state is not None else val),
+                _ptr(acc_state), _ptr(acc_val), sel_s.data_ptr(), sel_i.data_ptr(), _stream(dev)),
+                "jk_select_aggregate_forward")
+            if return_selection:
+                all_s[:, r0:r0 + rc] = sel_s.view(-1)[:B * rc * kk].view(B, rc, kk)
+                all_i[:, r0:r0 + rc] = sel_i.view(-1)[:B * rc * kk].view(B, rc, kk)
+    res = (acc_state, acc_val) if scatter else (out_state, out_val)
+    if return_selection:
+        return (*res, all_s, all_i)
+    return res
 
 
 def masked_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, *, window: int = -1,
@@ -626,20 +604,256 @@ def masked_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_
     return out_state, out_val
 
 
-def _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, target_val,
-                 source_val, projected_state, projected_val, window: int, source_state=None):
+def _value_planes(pval: Tensor, proj_dtype: torch.dtype):
+    """Values for the window-kernel value GEMM: padded to 64 columns. f32 values become bf16
+    hi + lo planes (both multiplied by the hi + lo edge planes, ~16 significant bits) unless
+    the projections are f16, where they are rounded to f16; 16-bit values are cast to the
+    projections' 16-bit type. proj_dtype: torch.float32 for three-plane f32 projections.
+    Returns (val, val_lo, pad)."""
+    out_dim = pval.shape[-1]
+    pad = (-out_dim) % 64
+    if pad:
+        pval = torch.nn.functional.pad(pval, (0, pad))
+    pval_lo = None
+    if pval.dtype == torch.float32 and proj_dtype != torch.float16:
+        pval = pval.contiguous()
+        hi = torch.empty(pval.shape, device=pval.device, dtype=torch.bfloat16)
+        pval_lo = torch.empty_like(hi)
+        with torch.cuda.device(pval.device):
+            check(_LIBRARY.jk_split2_bf16(pval.data_ptr(), pval.numel(), hi.data_ptr(), pval_lo.data_ptr(),
+                                          _stream(pval.device)), "jk_split2_bf16")
+        pval = hi
+    else:
+        target = torch.bfloat16 if proj_dtype == torch.float32 else proj_dtype
+        if pval.dtype != target:
+            pval = pval.to(target)
+    return pval.contiguous(), pval_lo, pad
+
+
+# ----------------------------------------------------------------------------- ops
+def _check_edge(edge_compress_name: str) -> int:
     if edge_compress_name not in _EDGE_CODE:
         raise RuntimeError(
             "Only edge_compress_name in {softsign, signed_abs_softmax, signed_entmax15} is supported by the native backend."
         )
+    return _EDGE_CODE[edge_compress_name]
+
+
+def _out_dtype(projected_state: Tensor, projected_val: Tensor) -> torch.dtype:
+    return projected_val.dtype if projected_state.dtype == projected_val.dtype else torch.float32
+
+
+def _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
+                           layer_val, projected_state, projected_val, topk: int, window: int):
+    compress = _check_edge(edge_compress_name)
+    if topk <= 0:
+        raise RuntimeError("topk must be positive.")
+    for name, t in (("layer_val", layer_val), ("projected_state", projected_state), ("projected_val", projected_val)):
+        _require_cuda(name, t)
+    n = layer_val.shape[-2]
+    k = min(int(topk), n)
+    if window < 0 and k >= n:
+        # every source survives: the dense propagation (same edges, same sums)
+        return _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
+                            layer_val, layer_val, projected_state, projected_val, -1)
+    batch_shape = layer_val.shape[:-2]
+    out_dim = projected_val.shape[-1]
+    val = _flatten_val(layer_val)
+    pstate = _flatten_state(projected_state)
+    pval = _flatten_val(projected_val)
+    out_dtype = _out_dtype(projected_state, projected_val)
+    sc = _pair_scorer(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, val, val, fused=k <= _MAX_K)
+    if sc.fused:
+        state, out = topk_aggregate(sc.row, sc.col, pstate, pval, k, window=window, compress=compress, bias=sc.bias,
+                                    out_dtype=out_dtype, split3=sc.split3, heads=sc.heads)
+    else:
+        state, out = select_aggregate(sc.row, sc.col, pstate, pval, k, window=window, compress=compress,
+                                      bias=sc.bias, out_dtype=out_dtype)
+    return (state.to(projected_state.dtype).reshape(*batch_shape, n),
+            out.to(projected_val.dtype).reshape(*batch_shape, n, out_dim))
+
+
+@_entry
+def propagation_topk(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
+                     layer_val, projected_state, projected_val, topk, target_block_size, source_block_size):
+    """SparsePropagation(sparse_type="topk") forward: per target, top-k over every source
+    (no causal mask), edges over the k, aggregate. Reference op: jakal_net_native.cpp:6305-6447
+    (CUDA fast path :6355-6389, blocked path for any k :6390-6447). Block sizes are accepted
+    for signature parity; the kernels tile internally."""
+    return _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
+                                  edge_compress_name, layer_val, projected_state, projected_val, topk, -1)
+
+
+@_entry
+def propagation_window_topk(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
+                            layer_val, projected_state, projected_val, window, topk, target_block_size=0,
+                            source_block_size=0):
+    """Window-intersect-top-k propagation: causal window mask (kernel_common.py:443-456),
+    then top-k among the visible sources (rows with fewer visible sources use all of them),
+    edges over the survivors (propagation.py:67-88). Not a reference op; the benchmark
+    configurations that combine a causal window with top-k use it."""
+    if window < 0:
+        raise RuntimeError("window must be non-negative.")
+    return _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
+                                  edge_compress_name, layer_val, projected_state, projected_val, topk, int(window))
+
+
+def _transition_inputs(sender_strength, src_val, other_val, projected_state, projected_val):
+    for name, t in (("sender_strength", sender_strength), ("src_val", src_val), ("dst/query_val", other_val),
+                    ("projected_state", projected_state), ("projected_val", projected_val)):
+        _require_cuda(name, t)
+    pstate = _flatten_state(projected_state)
+    sender = _flatten_state(sender_strength).to(pstate.dtype)
+    return _flatten_val(src_val), _flatten_val(other_val), pstate, sender, _flatten_val(projected_val)
+
+
+@_entry
+def transition_query_topk(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                          hidden_weight, hidden_bias, out_weight, out_bias, temperature, sender_strength, src_val,
+                          query_val, projected_state, projected_val, topk, query_block_size, source_block_size,
+                          use_cuda_reduce=True):
+    """Per-query transition (jakal_net_native.cpp:7089-7246): each query slot takes its
+    top-k sources by route logit, softmax over the k, sender-weighted gather."""
+    if topk <= 0:
+        raise RuntimeError("topk must be positive.")
+    sv, qv, pstate, sender, pval = _transition_inputs(sender_strength, src_val, query_val, projected_state,
+                                                      projected_val)
+    batch_shape = query_val.shape[:-2]
+    n_query = query_val.shape[-2]
+    n_src = src_val.shape[-2]
+    out_dim = projected_val.shape[-1]
+    k = min(int(topk), n_src)
+    sc = _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                            hidden_weight, hidden_bias, out_weight, out_bias, temperature, sv, qv,
+                            fused=k <= _MAX_K)
+    out_dtype = _out_dtype(projected_state, projected_val)
+    # rows = query slots (the route's destination side), columns = sources
+    if sc.fused:
+        state, out = topk_aggregate(sc.col, sc.row, pstate, pval, k, window=-1, compress=_lib.JK_SOFTMAX,
+                                    col_sender=sender, bias=sc.bias, out_dtype=out_dtype, split3=sc.split3,
+                                    heads=sc.heads)
+    else:
+        state, out = select_aggregate(sc.col, sc.row, pstate, pval, k, compress=_lib.JK_SOFTMAX, sender=sender,
+                                      bias=sc.bias, out_dtype=out_dtype)
+    return (state.to(projected_state.dtype).reshape(*batch_shape, n_query),
+            out.to(projected_val.dtype).reshape(*batch_shape, n_query, out_dim))
+
+
+@_entry
+def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                             hidden_weight, hidden_bias, out_weight, out_bias, temperature, sender_strength, src_val,
+                             dst_val, projected_state, projected_val, topk, src_block_size, dst_block_size,
+                             route_compress_name="softmax"):
+    """SparseTransition forward (jakal_net_native.cpp:6916-7087): each source takes its
+    top-k destinations by route logit, routes compressed over the k, sender-weighted
+    scatter-add into the destinations."""
+    if topk <= 0:
+        raise RuntimeError("topk must be positive.")
+    if route_compress_name not in _ROUTE_CODE:
+        raise RuntimeError(f"Unsupported route compress {route_compress_name!r}")
+    sv, dv, pstate, sender, pval = _transition_inputs(sender_strength, src_val, dst_val, projected_state,
+                                                      projected_val)
+    batch_shape = src_val.shape[:-2]
+    n_dst = dst_val.shape[-2]
+    out_dim = projected_val.shape[-1]
+    k = min(int(topk), n_dst)
+    sc = _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                            hidden_weight, hidden_bias, out_weight, out_bias, temperature, sv, dv,
+                            fused=k <= _MAX_K)
+    compress = _ROUTE_CODE[route_compress_name]
+    B = sv.shape[0]
+    dev = sv.device
+    out_dtype = _out_dtype(projected_state, projected_val)
+    if sc.fused:
+        accum = torch.empty(B * n_dst * (out_dim + 1) + 4, device=dev, dtype=torch.float32)
+        out_state = torch.empty((B, n_dst), device=dev, dtype=out_dtype)
+        out_val = torch.empty((B, n_dst, out_dim), device=dev, dtype=out_dtype)
+        args = (sc.row.data_ptr(), sc.col.data_ptr(), B, sv.shape[1], n_dst, sc.row.shape[-1],
+                _proj_dtype(sc.row, sc.split3),
+                pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
+                pval.data_ptr(), out_dim, _dtype_code("val", pval),
+                k, 0.0, _ptr(sc.bias), compress, accum.data_ptr(),
+                out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
+        with torch.cuda.device(dev):
+            if sc.heads is None:
+                check(_LIBRARY.jk_transition_pairwise_topk_forward(*args, _stream(dev)),
+                      "jk_transition_pairwise_topk_forward")
+            else:
+                check(_LIBRARY.jk_transition_pairwise_topk_forward_mh(*args, sc.heads.ref(), _stream(dev)),
+                      "jk_transition_pairwise_topk_forward_mh")
+    else:
+        out_state, out_val = select_aggregate(sc.row, sc.col, pstate, pval, k, compress=compress, sender=sender,
+                                              bias=sc.bias, scatter=True)
+    return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
+            out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))
+
+
+@_entry
+def transition_pairwise_dense(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                              hidden_weight, hidden_bias, out_weight, out_bias, route_compress_name, temperature,
+                              sender_strength, src_val, dst_val, projected_state, projected_val, src_block_size,
+                              dst_block_size):
+    """Dense pairwise Transition forward (jakal_net_native.cpp:6705-6914; transition.py:238-254):
+    routes of every source compressed over all destinations, sender-weighted, accumulated into
+    the destinations. Fused: two launches (per-source route statistics, then the
+    per-destination aggregate with per-column normalisation); otherwise the select-aggregate
+    kernel's scatter with every destination selected."""
+    if route_compress_name not in _ROUTE_CODE:
+        raise RuntimeError(f"Unsupported route compress {route_compress_name!r}")
+    sv, dv, pstate, sender, pval0 = _transition_inputs(sender_strength, src_val, dst_val, projected_state,
+                                                       projected_val)
+    batch_shape = src_val.shape[:-2]
+    n_src = src_val.shape[-2]
+    n_dst = dst_val.shape[-2]
+    out_dim = projected_val.shape[-1]
+    sc = _route_projections(route_kind, source_weight, source_bias, target_weight, target_bias, core_weight, bias,
+                            hidden_weight, hidden_bias, out_weight, out_bias, temperature, sv, dv)
+    compress = _ROUTE_CODE[route_compress_name]
+    if sc.heads is not None and sc.heads.struct.heads > 2:
+        raise TypeError("b200_sm100a dense multi-head routes support 2 heads.")
+    out_dtype = _out_dtype(projected_state, projected_val)
+    if not sc.fused:
+        out_state, out_val = select_aggregate(sc.row, sc.col, pstate, pval0, n_dst, compress=compress,
+                                              sender=sender, bias=sc.bias, scatter=True)
+        return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
+                out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))
+    pval, pval_lo, pad = _value_planes(pval0, torch.float32 if sc.split3 else sc.row.dtype)
+    B = sv.shape[0]
+    dev = sv.device
+    stats = torch.empty(B * n_src * 3, device=dev, dtype=torch.float32)
+    out_state = torch.empty((B, n_dst), device=dev, dtype=out_dtype)
+    out_val = torch.empty((B, n_dst, pval.shape[-1]), device=dev, dtype=out_dtype)
+    args = (sc.row.data_ptr(), sc.col.data_ptr(), B, n_src, n_dst, sc.row.shape[-1],
+            _proj_dtype(sc.row, sc.split3),
+            pstate.data_ptr(), sender.data_ptr(), _dtype_code("state", pstate),
+            pval.data_ptr(), _ptr(pval_lo), pval.shape[-1],
+            0.0, _ptr(sc.bias), compress, stats.data_ptr(),
+            out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
+    with torch.cuda.device(dev):
+        if sc.heads is None:
+            check(_LIBRARY.jk_transition_pairwise_dense_forward(*args, _stream(dev)),
+                  "jk_transition_pairwise_dense_forward")
+        else:
+            check(_LIBRARY.jk_transition_pairwise_dense_forward_mh(*args, sc.heads.ref(), _stream(dev)),
+                  "jk_transition_pairwise_dense_forward_mh")
+    if pad:
+        out_val = out_val[..., :out_dim]
+    return (out_state.to(projected_state.dtype).reshape(*batch_shape, n_dst),
+            out_val.to(projected_val.dtype).reshape(*batch_shape, n_dst, out_dim))
+
+
+def _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, target_val,
+                 source_val, projected_state, projected_val, window: int, source_state=None):
+    compress = _check_edge(edge_compress_name)
     for name, t in (("target_val", target_val), ("source_val", source_val), ("projected_state", projected_state),
                     ("projected_val", projected_val)):
         _require_cuda(name, t)
     batch_shape = target_val.shape[:-2]
     n_t = target_val.shape[-2]
+    n_s = source_val.shape[-2]
     out_dim = projected_val.shape[-1]
     tv = _flatten_val(target_val)
-    sv = _flatten_val(source_val)
+    sv = tv if source_val is target_val else _flatten_val(source_val)
     pstate = _flatten_state(projected_state)
     pval = _flatten_val(projected_val)
     if source_state is not None and source_state.numel() != 0:
@@ -648,21 +862,24 @@ def _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, e
         ss = _flatten_state(source_state).float()
         pstate = (pstate.float() * ss).to(pstate.dtype)
         pval = (pval.float() * ss[..., None]).to(pval.dtype)
-    f32 = tv.dtype == torch.float32
-    pval, pval_lo, pad = _value_planes(pval, tv.dtype)
-    row_proj, col_proj, bias_t, heads = _pair_scorer(kind, weight, bias, in_weight, in_bias, out_weight, out_bias,
-                                                     tv, sv)
-    same = projected_state.dtype == projected_val.dtype
-    out_dtype = projected_val.dtype if same else torch.float32
-    st, out = masked_aggregate(row_proj, col_proj, pstate, pval, window=window,
-                               compress=_EDGE_CODE[edge_compress_name], bias=bias_t,
-                               out_dtype=out_dtype, split3=f32, col_val_lo=pval_lo, heads=heads)
-    if pad:
-        out = out[..., :out_dim]
+    sc = _pair_scorer(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, tv, sv)
+    if sc.heads is not None and sc.heads.struct.heads > 2:
+        raise TypeError("b200_sm100a window / dense multi-head scorers support 2 heads.")
+    out_dtype = _out_dtype(projected_state, projected_val)
+    if sc.fused:
+        pv, pval_lo, pad = _value_planes(pval, torch.float32 if sc.split3 else sc.row.dtype)
+        st, out = masked_aggregate(sc.row, sc.col, pstate, pv, window=window, compress=compress, bias=sc.bias,
+                                   out_dtype=out_dtype, split3=sc.split3, col_val_lo=pval_lo, heads=sc.heads)
+        if pad:
+            out = out[..., :out_dim]
+    else:
+        st, out = select_aggregate(sc.row, sc.col, pstate, pval, n_s, window=window, compress=compress,
+                                   bias=sc.bias, out_dtype=out_dtype)
     return (st.to(projected_state.dtype).reshape(*batch_shape, n_t),
             out.to(projected_val.dtype).reshape(*batch_shape, n_t, out_dim))
 
 
+@_entry
 def propagation_window(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, layer_val,
                        projected_state, projected_val, window, target_block_size, source_block_size):
     """SparsePropagation(sparse_type="window") forward: causal window [t - window, t], edges
@@ -674,6 +891,7 @@ def propagation_window(kind, weight, bias, in_weight, in_bias, out_weight, out_b
                         layer_val, projected_state, projected_val, int(window))
 
 
+@_entry
 def propagation_dense(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, layer_val,
                       projected_state, projected_val, source_state, target_block_size, source_block_size):
     """Dense Propagation forward: every (target, source) pair (jakal_net_native.cpp:5962-6076;
@@ -682,6 +900,7 @@ def propagation_dense(kind, weight, bias, in_weight, in_bias, out_weight, out_bi
                         layer_val, projected_state, projected_val, -1, source_state)
 
 
+@_entry
 def propagation_query_dense(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name,
                             query_val, source_val, projected_state, projected_val, query_block_size,
                             source_block_size):

@@ -98,6 +98,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _p, _p, _i32, _p],
     ),
     "jk_transition_pairwise_topk_noalloc_capacity": (_i64, []),
+    "jk_select_aggregate_forward": (
+        _i32,
+        [_p, _i64, _i64, _i64, _i64, _i64,      # scores, B, n_rows, n_cols, row_begin, row_count
+         _p, _p, _i32, _p, _i64, _i32,          # state, sender, state_dtype, val, dim, val_dtype
+         _i64, _i64, _f32, _p, _i32, _i32,      # k, window, score_bias, bias_dev, compress, scatter
+         _p, _p, _i32, _p, _p,                  # out_state, out_val, out_dtype, acc_state, acc_val
+         _p, _p, _p],                           # sel_score, sel_index, stream
+    ),
 }
 _args = SIGNATURES["jk_propagation_topk_forward"][1]
 SIGNATURES["jk_propagation_topk_rows_forward"] = (_i32, _args[:4] + [_i64, _i64] + _args[4:])  # + row block

@@ -45,7 +45,10 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", type=Path, required=True, help="Jakal-Net checkout (contains src/jakal_net)")
     args = ap.parse_args()
-    import reference_shim
+    import sys
+
+    sys.path.insert(0, str(HERE.parent.parent / "baseline"))
+    import reference_shim  # baseline/reference_shim.py
 
     jn = reference_shim.import_reference(args.reference / "src")
     from jakal_net.kernel_common import build_topk_mask, causal_window_mask
