@@ -1,0 +1,99 @@
+"""Builds the reference's own native extension from its sources into oracle/_ref/ (checker only).
+
+    python oracle/build_ref.py [--cpu] [--cuda] [--src PATH_TO_REFERENCE_CHECKOUT]
+
+Test and baseline infrastructure: nothing in the product package imports what this builds.
+
+* --cpu: ``native/jakal_net_native.cpp`` compiled CPU-only with torch.utils.cpp_extension,
+  plus a two-function stub. The .cpp calls two availability probes that only the .cu defines
+  (``jakal_net_low_rank_dense_scores_tf32_cuda_available`` and
+  ``jakal_net_low_rank_propagation_dense_tf32_forward_cuda_available``, referenced outside its
+  ``#ifdef WITH_CUDA``); the stub answers ``false`` for both, which is what a CPU-only build
+  means. Module name ``jakal_net_native`` (backend "aten_cpp_cpu"). Its per-query transition
+  (jakal_net_native.cpp:7089-7246) generates the fixtures that pin the oracle's
+  transition_query_topk (tests/golden/make_golden_native.py).
+* --cuda: the same .cpp plus ``native/jakal_net_native_cuda.cu`` with ``-DWITH_CUDA`` for
+  sm_100 (the reference's own build recipe, scripts/build_native_extension.py, with the
+  architecture fixed). Module name ``jakal_net_native`` too, in its own folder. nvcc cross-
+  compiles it here; on the GPU host it is the same-box GPU reference (bench.py
+  --impl reference-gpu) and the pin of the bf16 rounding chain of the CUDA fast paths.
+
+Nothing in the reference tree is modified; outputs go to oracle/_ref/{cpu,cuda}/ only
+(git-ignored, shipped with the tree to the GPU host like the product library).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.machinery
+import importlib.util
+import os
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+REF_OUT = HERE / "_ref"
+DEFAULT_SRC = Path("/root/reference")
+STUB = """// CPU-only build of the reference extension: the two CUDA availability probes the .cpp
+// references outside its WITH_CUDA guard answer "not available".
+bool jakal_net_low_rank_dense_scores_tf32_cuda_available() { return false; }
+bool jakal_net_low_rank_propagation_dense_tf32_forward_cuda_available() { return false; }
+"""
+
+
+def build(kind: str, src: Path = DEFAULT_SRC, verbose: bool = False) -> Path:
+    from torch.utils.cpp_extension import load
+
+    native = src / "native"
+    out = REF_OUT / kind
+    out.mkdir(parents=True, exist_ok=True)
+    sources = [str(native / "jakal_net_native.cpp")]
+    cflags = ["-std=c++17", "-O3"]
+    if kind == "cpu":
+        stub = out / "cuda_probe_stub.cpp"
+        stub.write_text(STUB)
+        sources.append(str(stub))
+        with_cuda = False
+        cuda_flags = None
+    else:
+        sources.append(str(native / "jakal_net_native_cuda.cu"))
+        cflags.append("-DWITH_CUDA")
+        with_cuda = True
+        cuda_flags = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a"]
+        os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
+    load(name="jakal_net_native", sources=sources, build_directory=str(out), verbose=verbose, with_cuda=with_cuda,
+         extra_include_paths=[str(native)], extra_cflags=cflags, extra_cuda_cflags=cuda_flags)
+    return out / "jakal_net_native.so"
+
+
+def load_built(kind: str):
+    """Imports a module built by build() (no compiler, no reference checkout needed)."""
+    import torch  # noqa: F401  (the extension links against torch's libraries)
+
+    path = REF_OUT / kind / "jakal_net_native.so"
+    if not path.exists():
+        raise ImportError(f"{path} not built (python oracle/build_ref.py --{kind})")
+    name = "jakal_net_native"
+    if name in sys.modules and getattr(sys.modules[name], "__file__", "") == str(path):
+        return sys.modules[name]
+    loader = importlib.machinery.ExtensionFileLoader(name, str(path))
+    spec = importlib.util.spec_from_loader(name, loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    sys.modules[name] = mod
+    return mod
+
+
+def available(kind: str) -> bool:
+    return (REF_OUT / kind / "jakal_net_native.so").exists()
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--cpu", action="store_true")
+    ap.add_argument("--cuda", action="store_true")
+    ap.add_argument("--src", type=Path, default=DEFAULT_SRC)
+    ap.add_argument("--verbose", action="store_true")
+    a = ap.parse_args()
+    kinds = [k for k, on in (("cpu", a.cpu), ("cuda", a.cuda)) if on] or ["cpu"]
+    for k in kinds:
+        print(build(k, a.src, a.verbose))

@@ -197,3 +197,24 @@ def test_diagonal_route_transition_matches_reference():
                                                    int(g["k"]), compress_name="softmax")
     _close(st, g["out_state"])
     _close(val, g["out_val"])
+
+
+@pytest.mark.parametrize("name", ["query_topk_low_rank", "query_topk_low_rank_k_all", "query_topk_diagonal"])
+def test_transition_query_topk_matches_reference_native_build(name):
+    """Per-query transition pinned to the reference's own native op (CPU build of
+    jakal_net_native.cpp:7089-7246; fixtures from tests/golden/make_golden_native.py):
+    logits route(src, query)^T / T + b / T, top-k sources per query, softmax over the k,
+    sender-weighted gather."""
+    g = _load(name)
+    T = float(g["temperature"])
+    if str(g["kind"]) == "low_rank_bilinear_route":
+        sp = oracle.lowrank_project(g["src_val"], g["w_s"], g["core"], T, "f32")
+        qp = oracle.lowrank_project(g["query_val"], g["w_t"], None, 1.0, "f32")
+    else:
+        sp = oracle.lowrank_project(g["src_val"], np.eye(g["src_val"].shape[-1]), g["core"], T, "f32")
+        qp = g["query_val"].astype(np.float64)
+    k = min(int(g["k"]), g["src_val"].shape[1])
+    st, val, _, _ = oracle.transition_query_topk(qp, sp, g["state"], g["val"], g["sender"], k,
+                                                 bias=float(g["bias"]) / T)
+    _close(st, g["out_state"])
+    _close(val, g["out_val"])
