@@ -409,6 +409,209 @@ def run_config5(args, rank, world, device):
     print(json.dumps(line), flush=True)
 
 
+C4 = dict(B=32, P=1024, D=512, VOCAB=16384, LAYERS=6, EXPAND=256, COMPRESS=64, WINDOW=512, TOPK=32, HIDDEN=64,
+          TARGET=128, SEED=3)
+C4_METRIC = "Progressive-B fwd tokens/s"
+C4_WORKLOAD = ("config4: ProgressiveBExampleLM.forward_query_block, B32 prefix 1024 dim 512 vocab 16384, 6 joint "
+               "blocks (expanded 256 / compressed 64), s_window 512, top-k 32, rank 64, 128 query slots, bf16 autocast")
+C4_OPS = ("propagation_window", "propagation_topk", "transition_pairwise_topk", "propagation_dense",
+          "transition_pairwise_dense", "propagation_query_dense", "transition_query_topk")
+
+
+def _progressive_b(pb, implementation, batch_hint=None):
+    c = C4
+    torch.manual_seed(c["SEED"])
+    specs = pb.build_progressive_b_stage_specs(c["P"], lite_layers=c["LAYERS"], mid_layers=0, full_layers=0,
+                                               lite_expand_ratio=c["EXPAND"] / c["P"],
+                                               lite_compress_ratio=c["COMPRESS"] / c["P"])
+    return pb.ProgressiveBExampleLM(
+        vocab_size=c["VOCAB"], dim=c["D"], seq_nodes=c["P"], stage_specs=specs, s_window=c["WINDOW"],
+        route_topk=c["TOPK"], expanded_topk=c["TOPK"], compressed_topk=c["TOPK"], query_topk=c["TOPK"],
+        route_kind="low_rank_bilinear", pairwise_kind="low_rank_bilinear", route_hidden_dim=c["HIDDEN"],
+        pairwise_hidden_dim=c["HIDDEN"], implementation=implementation).eval()
+
+
+def _import_reference_model():
+    """The reference's Progressive-B model script and package, staged by
+    baseline/stage_reference.py (None when not staged)."""
+    sys.path.insert(0, str(ROOT / "baseline"))
+    import reference_shim
+
+    if not reference_shim.available():
+        return None, None
+    os.environ["JAKAL_NET_NATIVE_MODULE"] = "jakal_net_b200"
+    jn = reference_shim.import_reference()
+    return jn, reference_shim.import_progressive_b()
+
+
+def cpu_progressive_b(seconds: float = 15.0, batch: int = 2):
+    """The reference's own CPU forward (implementation="reference", the Python/ATen path on
+    all host threads) of config 4's model on a bounded batch; tokens/s, sample text, threads."""
+    jn, pb = _import_reference_model()
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = _progressive_b(pb, "reference")
+    ids = torch.randint(0, C4["VOCAB"], (batch, C4["P"]), generator=torch.Generator().manual_seed(C4["SEED"]))
+    times = []
+    with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
+        model.forward_query_block(ids, target_len=C4["TARGET"])  # untimed warm-up
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end or len(times) < 3:
+            t0 = time.perf_counter()
+            model.forward_query_block(ids, target_len=C4["TARGET"])
+            times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    sample = (f"median of {len(times)} forwards of batch {batch} (prefix 1024, config-4 model), "
+              f"implementation=reference, bf16 CPU autocast, torch threads {torch.get_num_threads()}, {_cpu_model()}")
+    return batch * C4["P"] / med, sample, threads
+
+
+def run_config4(args, rank, world, device):
+    jn, pb = _import_reference_model()
+    if pb is None:
+        if rank == 0:
+            print(json.dumps({"metric": C4_METRIC, "unavailable": "reference model not staged (baseline/_ref)"}))
+        return
+    import jakal_net_b200 as jk
+
+    status = jn.native_status(force_reload=True)
+    assert status.available and status.backend_name == jk.backend_name(), status
+    model = _progressive_b(pb, "native").to(device)
+    b, p = C4["B"], C4["P"]
+    h_ids = torch.randint(0, C4["VOCAB"], (b, p), generator=torch.Generator().manual_seed(C4["SEED"] + rank))
+    ids = h_ids.to(device)
+    h_ids = h_ids.pin_memory()
+
+    def forward(x):
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return model.forward_query_block(x, target_len=C4["TARGET"])
+
+    for _ in range(args.warmup):
+        forward(ids)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    steps = max(1, min(args.steps, 20))
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            forward(ids)
+        e1.record()
+        torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / steps
+
+    # per-op device time: every backend op the model calls, bracketed by CUDA events
+    per_op, calls, launches = {}, {}, {}
+    originals = {n: getattr(jk, n) for n in C4_OPS}
+
+    def wrap(name, fn):
+        def timed_op(*a, **kw):
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            out = fn(*a, **kw)
+            s1.record()
+            per_op.setdefault(name, []).append((s0, s1))
+            return out
+        return timed_op
+
+    for n, f in originals.items():
+        setattr(jk, n, wrap(n, f))
+    try:
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        forward(ids)
+        f1.record()
+        torch.cuda.synchronize(device)
+    finally:
+        for n, f in originals.items():
+            setattr(jk, n, f)
+    fwd_ms = f0.elapsed_time(f1)
+    op_ms = {n: sum(a.elapsed_time(z) for a, z in evs) for n, evs in per_op.items()}
+    calls = {n: len(evs) for n, evs in per_op.items()}
+
+    # end to end: token ids from pinned host memory in, logits back to pinned host memory
+    h_logits = torch.empty((b, C4["TARGET"], C4["VOCAB"]), dtype=torch.bfloat16).pin_memory()
+
+    def e2e():
+        d = h_ids.to(device, non_blocking=True)
+        h_logits.copy_(forward(d), non_blocking=True)
+
+    e2e()
+    torch.cuda.synchronize(device)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(steps, 5))
+    g0.record()
+    for _ in range(e2e_steps):
+        e2e()
+    g1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = g0.elapsed_time(g1) / e2e_steps
+
+    # the reference's own torch implementation of the same model on this GPU (informative)
+    ref_ms = None
+    if not args.no_reference_gpu:
+        ref_model = _progressive_b(pb, "reference").to(device)
+        ref_model.load_state_dict(model.state_dict())
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            ref_model.forward_query_block(ids, target_len=C4["TARGET"])
+            torch.cuda.synchronize(device)
+            r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            r0.record()
+            for _ in range(3):
+                ref_model.forward_query_block(ids, target_len=C4["TARGET"])
+            r1.record()
+            torch.cuda.synchronize(device)
+        ref_ms = r0.elapsed_time(r1) / 3
+        del ref_model
+
+    def max_over_ranks(x):
+        if world == 1 or x is None:
+            return x
+        t = torch.tensor([x], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    ms, e2e_ms, ref_ms = max_over_ranks(ms), max_over_ranks(e2e_ms), max_over_ranks(ref_ms)
+    if rank != 0:
+        return
+    tokens = world * b * p
+    line = {
+        "metric": C4_METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (uniform token ids, random-init weights of the config-4 architecture)",
+        "config": {"workload": C4_WORKLOAD, "batch_per_gpu": b, "prefix": p, "dim": C4["D"],
+                   "backend": "JAKAL_NET_NATIVE_MODULE=jakal_net_b200, implementation=native",
+                   "l2": "per-step working set (weights + activations) far above L2",
+                   "timing": "eager forward (the reference forces its torch path under graph capture), "
+                             "CUDA events, max over ranks",
+                   "parallelism": f"batch-sharded x{world}, no collective on the data path"},
+        "clocks": clk.summary(),
+        "per_op": {"forward_ms": fwd_ms, "ops_ms": op_ms, "calls": calls,
+                   "ops_share": {n: v / fwd_ms for n, v in op_ms.items()}},
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h_ids.numel() * 8, "d2h_bytes_per_step": h_logits.numel() * 2},
+    }
+    if ref_ms is not None:
+        line["reference_torch_gpu"] = {"value": tokens / (ref_ms * 1e-3), "unit": "tokens/s", "ms_per_step": ref_ms,
+                                       "what": "the same model with implementation=reference on this GPU"}
+    if world == 1 and not args.no_cpu_baseline:
+        v, sample, threads = cpu_progressive_b()
+        line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                                "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+def _cpu_model() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown CPU"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -416,7 +619,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[2, 5], default=2)
+    ap.add_argument("--config", type=int, choices=[2, 4, 5], default=2)
+    ap.add_argument("--no-reference-gpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -430,7 +634,7 @@ def main():
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=device)
     try:
-        (run_config5 if args.config == 5 else run_b200)(args, rank, world, device)
+        {2: run_b200, 4: run_config4, 5: run_config5}[args.config](args, rank, world, device)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

@@ -62,9 +62,18 @@ def _val_proj(val):
     return val * 0.5 + 0.25
 
 
-def _signed_abs(scores):
+def signed_abs_softmax_edges(scores):
+    """sign(s) * softmax(|s|); the reference's dispatch recognises the edge compressor by
+    this function name (propagation.py:56-64)."""
     clean = torch.nan_to_num(scores)
     return torch.sign(clean) * torch.softmax(clean.abs(), dim=-1)
+
+
+def signed_entmax15(scores):
+    """The reference's signed_entmax15 edges (kernels.py:155-236), recognised by name."""
+    from jakal_net.kernels import signed_entmax15 as ref_entmax
+
+    return ref_entmax(scores, dim=-1)
 
 
 def _close(a, b, atol=1e-5, rtol=1e-5):
@@ -100,7 +109,7 @@ def test_dense_propagation_diagonal(jn, module):
 def test_dense_propagation_low_rank_signed_abs_state_weighted(jn, module):
     layer = _layer(jn, 6, 4, 302)
     pw = jn.LowRankBilinearPairwise(dim=4, rank=3).cuda()
-    ref, nat = _pair(lambda **kw: jn.Propagation(pairwise_fn=pw, edge_compress_fn=_signed_abs,
+    ref, nat = _pair(lambda **kw: jn.Propagation(pairwise_fn=pw, edge_compress_fn=signed_abs_softmax_edges,
                                                  state_proj_fn=_state_proj, val_proj_fn=_val_proj,
                                                  state_weight_edges=True, **kw))
     with mock.patch.object(module, "propagation_dense", wraps=module.propagation_dense) as w:
@@ -128,14 +137,15 @@ def test_sparse_propagation_window_and_topk(jn, module):
     _close(ref.compute_delta(layer), got)
 
 
-@pytest.mark.parametrize("edge", ["softsign", "signed_abs"])
+@pytest.mark.parametrize("edge", ["softsign", "signed_abs", "signed_entmax15"])
 @pytest.mark.parametrize("k", [3, 65, 200])
 def test_sparse_propagation_topk_any_k(jn, module, edge, k):
     """k beyond the reference CUDA kernels' 64 (they fall back to the blocked path,
     jakal_net_native.cpp:6390-6447); here the select-aggregate kernel takes it."""
     layer = _layer(jn, 300, 24, 40 + k)
     pw = jn.LowRankBilinearPairwise(dim=24, rank=16).cuda()
-    kw = {} if edge == "softsign" else {"edge_compress_fn": _signed_abs}
+    kw = {"softsign": {}, "signed_abs": {"edge_compress_fn": signed_abs_softmax_edges},
+          "signed_entmax15": {"edge_compress_fn": signed_entmax15}}[edge]
     ref, nat = _pair(lambda **a: jn.SparsePropagation(pairwise_fn=pw, sparse_type="topk", topk=k, **kw, **a))
     with mock.patch.object(module, "propagation_topk", wraps=module.propagation_topk) as w:
         got = nat.compute_delta(layer)
@@ -277,3 +287,26 @@ def test_progressive_b_query_block_bf16_autocast(jn, module):
     rel = ((got - want).norm() / want.norm()).item()
     print(f"bf16 autocast logits: relative L2 difference native vs reference {rel:.3e}; calls {calls}")
     assert rel < 0.1, rel
+
+
+@pytest.mark.parametrize("edge", ["softsign", "signed_abs"])
+def test_config1_causal_dense_against_reference(jn, module, edge):
+    """Config 1's shape and inputs (B2 N256 D128 R32 f32, causal window 255 = causal dense,
+    val / state ~ N(0, 1), W ~ N(0, 1/sqrt(D)), w = ones, b = 0, seed 0) through the
+    reference's SparsePropagation, native against reference."""
+    torch.manual_seed(0)
+    B, N, D, R = 2, 256, 128, 32
+    g = torch.Generator().manual_seed(0)
+    layer = jn.Layer(dim=D, num_nodes=N, state=torch.randn(B, N, generator=g).cuda(),
+                     val=torch.randn(B, N, D, generator=g).cuda())
+    pw = jn.LowRankBilinearPairwise(dim=D, rank=R)
+    with torch.no_grad():
+        pw.source_proj.weight.copy_(torch.randn(R, D, generator=g) / D ** 0.5)
+        pw.target_proj.weight.copy_(torch.randn(R, D, generator=g) / D ** 0.5)
+    pw = pw.cuda()
+    kw = {} if edge == "softsign" else {"edge_compress_fn": signed_abs_softmax_edges}
+    ref, nat = _pair(lambda **a: jn.SparsePropagation(pairwise_fn=pw, sparse_type="window", window=N - 1, **kw, **a))
+    with mock.patch.object(module, "propagation_window", wraps=module.propagation_window) as w:
+        got = nat.compute_delta(layer)
+    assert w.call_count > 0
+    _close(ref.compute_delta(layer), got, atol=1e-5, rtol=1e-5)
