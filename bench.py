@@ -40,8 +40,40 @@ METRIC = "fused propagation Gpairs/s"
 UNIT = "Gpairs/s"
 WORKLOAD = "config2: SparsePropagation causal window 512 intersect top-k 32, B8 N2048 D384 R64, bf16, softsign"
 # dram__bytes_read.sum + dram__bytes_write.sum of one fused-kernel launch on this workload,
-# from the ncu capture summarised in profiles/topk_kernel_config2.md.
+# from an ncu capture of this bench's kernel (a recorded constant, not measured per run).
 NCU_TRAFFIC_BYTES = 16975104  # 16.98 MB read + 0 B written (outputs stay in L2), one launch
+
+# Kernels each C-ABI entry point launches (the library's own kernels only).
+KERNELS_PER_CALL = {
+    "jk_lowrank_project": 1, "jk_lowrank_project_pair": 1, "jk_propagation_topk_forward": 1,
+    "jk_propagation_topk_forward_mh": 1, "jk_propagation_topk_rows_forward": 1,
+    "jk_propagation_window_forward": 1, "jk_propagation_window_forward_mh": 1, "jk_select_aggregate_forward": 1,
+    "jk_split3_bf16": 1, "jk_split2_bf16": 1,
+}
+
+
+def count_launches(fn) -> int:
+    """Runs fn once and counts the library kernels it launches, from the C-ABI calls it makes."""
+    import jakal_net_b200 as jk
+
+    lib = jk._LIBRARY
+    counts = {}
+    saved = {}
+    for name in KERNELS_PER_CALL:
+        f = getattr(lib, name)
+        saved[name] = f
+
+        def wrapped(*a, _f=f, _n=name):
+            counts[_n] = counts.get(_n, 0) + 1
+            return _f(*a)
+
+        setattr(lib, name, wrapped)
+    try:
+        fn()
+    finally:
+        for name, f in saved.items():
+            setattr(lib, name, f)
+    return sum(KERNELS_PER_CALL[n] * c for n, c in counts.items())
 
 
 def pairs_per_batch_item(n: int, window: int) -> int:
@@ -169,19 +201,118 @@ def cpu_port_time(seconds: float = 10.0):
     return pairs / el / 1e9, sample, threads
 
 
+def _median_rate(run, work, seconds: float, min_reps: int = 3):
+    """Times run() until `seconds` have passed and at least min_reps runs were made (after
+    an untimed warm-up run); returns (work / median run time, number of runs)."""
+    run()
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < min_reps:
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    return work / statistics.median(times), len(times)
+
+
+def cpu_reference_config2(seconds: float = 10.0):
+    """The reference's own CPU code on config 2 (one batch item per run, all host threads):
+    window-intersect-top-k is not a single reference op, so it is composed from the
+    reference's primitives exactly as its Python path would run them -- the
+    LowRankBilinearPairwise scores (modules.py:93-100), causal_window_mask and build_topk_mask
+    (kernel_common.py:433-456), _compress_edges (propagation.py:67-88) and the einsum
+    aggregate (propagation.py:215-219) -- in f32 (the reference's CPU precision).
+    Returns (Gpairs/s, sample text, threads) or None when the reference is not staged."""
+    jn, _ = _import_reference_model()
+    if jn is None:
+        return None
+    from jakal_net.kernel_common import build_topk_mask, causal_window_mask
+    from jakal_net.propagation import _compress_edges
+    from torch.nn import functional as F
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(SEED)
+    val = torch.randn(1, N, D, generator=g)
+    state = torch.randn(1, N, generator=g)
+    torch.manual_seed(SEED)
+    pw = jn.LowRankBilinearPairwise(dim=D, rank=R)
+    win = causal_window_mask(0, N, 0, N, WINDOW).view(1, N, N)
+
+    @torch.no_grad()
+    def run():
+        scores = pw(val, val)
+        masked = scores.masked_fill(~win, float("-inf"))
+        keep = build_topk_mask(masked, K_TOP) & win
+        e = _compress_edges(scores, F.softsign, mask=keep)
+        return torch.einsum("bij,bj->bi", e, state), torch.einsum("bij,bjd->bid", e, val)
+
+    rate, reps = _median_rate(run, pairs_per_batch_item(N, WINDOW), seconds)
+    sample = (f"median of {reps} runs of 1 of the 8 batch items (N=2048, window 512, k 32, f32) through the "
+              f"reference's own primitives; torch threads {torch.get_num_threads()}, {_cpu_model()}")
+    return rate / 1e9, sample, threads
+
+
+def cpu_port_time(seconds: float = 10.0):
+    """The CPU port (oracle/cpu_port.py, the reference's blocked algorithm restated in torch
+    CPU ops) on one batch item; returns (Gpairs/s, sample text, threads)."""
+    from oracle import cpu_port
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(SEED)
+    val = torch.randn(1, N, D, generator=g).bfloat16().float()
+    state = torch.randn(1, N, generator=g).bfloat16().float()
+    w_s = (torch.randn(R, D, generator=g) / D ** 0.5).bfloat16()
+    w_t = (torch.randn(R, D, generator=g) / D ** 0.5).bfloat16()
+    core = torch.full((R,), 1.0 / R ** 0.5)
+
+    def run():
+        pt = cpu_port.lowrank_project_bf16(val, w_t)
+        ps = cpu_port.lowrank_project_bf16(val, w_s, core)
+        cpu_port.window_topk_propagation(pt, ps, state, val, K_TOP, WINDOW)
+
+    rate, reps = _median_rate(run, pairs_per_batch_item(N, WINDOW), seconds)
+    sample = (f"median of {reps} runs of 1 of the 8 batch items (N=2048, window 512, k 32), blocked torch CPU "
+              f"port; torch threads {torch.get_num_threads()}, {_cpu_model()}")
+    return rate / 1e9, sample, threads
+
+
+def cpu_baseline_config2(seconds: float = 10.0):
+    """The reference's own code when staged (kind "reference"), else the port (kind "port")."""
+    ref = cpu_reference_config2(seconds)
+    if ref is not None:
+        return (*ref, "reference")
+    return (*cpu_port_time(seconds), "port")
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
-    value, sample, threads = cpu_port_time(max(5.0, min(30.0, 0.05 * args.steps)))
+    if args.config == 4:
+        jn, _ = _import_reference_model()
+        if jn is None:
+            print(json.dumps({"impl": "reference", "unavailable": "reference model not staged (baseline/_ref)"}))
+            return
+        value, sample, threads = cpu_progressive_b(max(10.0, min(30.0, 0.1 * args.steps)))
+        metric, unit, cfg, dtype = C4_METRIC, "tokens/s", C4_WORKLOAD, "bf16"
+        ms = C4["P"] * 2 / value * 1e3
+        kind = "reference"
+    elif args.config == 2:
+        value, sample, threads, kind = cpu_baseline_config2(max(5.0, min(30.0, 0.05 * args.steps)))
+        metric, unit, cfg, dtype = METRIC, UNIT, WORKLOAD, "f32"
+        ms = PAIRS_PER_STEP / (value * 1e9) * 1e3
+    else:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference arm covers configs 2 and 4"}))
+        return
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": PAIRS_PER_STEP / (value * 1e9) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,1) inputs of the config shape)",
-        "config": {"workload": WORKLOAD, "implementation": "CPU port of the reference blocked path (oracle/cpu_port.py)"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic (seeded inputs of the config shape)",
+        "config": {"workload": cfg, "implementation": "the reference's own CPU code on the host cores" if
+                   kind == "reference" else "CPU port of the reference blocked path (oracle/cpu_port.py)"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -196,6 +327,7 @@ def run_b200(args, rank, world, device):
         return jk.propagation_window_topk("low_rank_bilinear", inp["core"], inp["bias"], inp["w_s"], None,
                                           inp["w_t"], None, "softsign", val, state, val, WINDOW, K_TOP, 128, 128)
 
+    launches_per_step = count_launches(lambda: api_step(inp["val"], inp["state"]))
     # CUDA graph of one step (projections + fused kernel) on the resident inputs.
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
@@ -246,37 +378,67 @@ def run_b200(args, rank, world, device):
         kgraph.replay()
     kernel_ms = timed(kgraph.replay, args.steps) / args.steps
 
-    # End to end through the public API with host buffers (H2D inputs, D2H outputs).
+    # End to end through the public API with host buffers: every step copies its inputs in
+    # from pinned host memory and its outputs back. Steps are pipelined over three streams
+    # (host-to-device copy, compute, device-to-host copy) with two buffer sets, so step
+    # i + 1's upload and step i - 1's download overlap step i's compute (PCIe is full duplex).
     h_val = inp["val"].cpu().pin_memory()
     h_state = inp["state"].cpu().pin_memory()
-    d_val = torch.empty_like(inp["val"])
-    d_state = torch.empty_like(inp["state"])
-    h_out_state = torch.empty(B, N, dtype=torch.bfloat16).pin_memory()
-    h_out_val = torch.empty(B, N, D, dtype=torch.bfloat16).pin_memory()
+    nbuf = 2
+    d_val = [torch.empty_like(inp["val"]) for _ in range(nbuf)]
+    d_state = [torch.empty_like(inp["state"]) for _ in range(nbuf)]
+    h_out_state = [torch.empty(B, N, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
+    h_out_val = [torch.empty(B, N, D, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
+    s_in, s_cmp, s_out = (torch.cuda.Stream(device) for _ in range(3))
+    ev_in = [torch.cuda.Event() for _ in range(nbuf)]
+    ev_cmp = [torch.cuda.Event() for _ in range(nbuf)]
+    ev_out = [torch.cuda.Event() for _ in range(nbuf)]
     e2e_steps = max(3, min(args.steps, 50))
 
-    def e2e_once():
-        d_val.copy_(h_val, non_blocking=True)
-        d_state.copy_(h_state, non_blocking=True)
-        st, vv = api_step(d_val, d_state)
-        h_out_state.copy_(st, non_blocking=True)
-        h_out_val.copy_(vv, non_blocking=True)
+    def e2e_run(steps):
+        for i in range(steps):
+            j = i % nbuf
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(ev_cmp[j])  # the compute that last read buffer set j is done
+                d_val[j].copy_(h_val, non_blocking=True)
+                d_state[j].copy_(h_state, non_blocking=True)
+                ev_in[j].record(s_in)
+            with torch.cuda.stream(s_cmp):
+                s_cmp.wait_event(ev_in[j])
+                s_cmp.wait_event(ev_out[j])  # the download of this buffer set's last outputs is done
+                st, vv = api_step(d_val[j], d_state[j])
+                ev_cmp[j].record(s_cmp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_cmp[j])
+                h_out_state[j].copy_(st, non_blocking=True)
+                h_out_val[j].copy_(vv, non_blocking=True)
+                st.record_stream(s_out)
+                vv.record_stream(s_out)
+                ev_out[j].record(s_out)
 
-    for _ in range(3):
-        e2e_once()
+    e2e_run(3)
     torch.cuda.synchronize(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_once()
-    e1.record()
+    t0 = time.perf_counter()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s_in)
+    s_cmp.wait_event(e0)
+    e2e_run(e2e_steps)
+    s_in.wait_stream(s_out)
+    e1.record(s_in)
     torch.cuda.synchronize(device)
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    e2e_wall_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
     if world > 1:
         t = torch.tensor([e2e_ms, kernel_ms], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_ms, kernel_ms = (float(x) for x in t.tolist())
 
+    c5 = None
+    if not args.no_config5:
+        if world > 1:
+            torch.distributed.barrier()
+        c5 = measure_config5(5, 3, rank, world, device)
     if rank != 0:
         return
     value = world * PAIRS_PER_STEP / (ms_per_step * 1e-3) / 1e9
@@ -293,18 +455,33 @@ def run_b200(args, rank, world, device):
                    "l2": "flushed between timed steps (256 MiB write, outside the timed events)",
                    "timing": "CUDA graph replay of the step, CUDA events per step, max over ranks",
                    "parallelism": f"batch-sharded x{world}, no collective on the data path"},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": (h_val.numel() + h_state.numel()) * 2,
-                "d2h_bytes_per_step": (h_out_val.numel() + h_out_state.numel()) * 2, "ms_per_step": e2e_ms},
+                "d2h_bytes_per_step": (h_out_val[0].numel() + h_out_state[0].numel()) * 2, "ms_per_step": e2e_ms,
+                "wall_ms_per_step": e2e_wall_ms,
+                "how": "public op per step, pinned host inputs copied in and outputs copied out every step; "
+                       "steps pipelined over copy-in / compute / copy-out streams (2 buffer sets)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst)",
                      "kernel": "jk::topk::topk_kernel (fused score / top-k / aggregate)",
-                     "kernel_ms": kernel_ms, "algorithmic_bytes": fused_kernel_bytes(), "traffic": traffic},
+                     "kernel_ms": kernel_ms, "algorithmic_bytes": fused_kernel_bytes(), "traffic": traffic,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
+                                       "kernel on this workload (recorded constant, not measured in this run)"},
     }
+    if c5 is not None:
+        line["config5_row_sharded"] = {
+            "what": "config 5 (B4 N32768 D512 R64, window 4096, top-k 64) split by query-row blocks over the "
+                    f"{world} GPU(s) of this run: strong scaling, total work fixed",
+            "compute": {"value": c5["pairs"] / (c5["compute_ms"] * 1e-3) / 1e9, "unit": UNIT,
+                        "ms_per_step": c5["compute_ms"], "note": "outputs left row-sharded"},
+            "with_allgather": {"value": c5["pairs"] / (c5["sharded_ms"] * 1e-3) / 1e9, "unit": UNIT,
+                               "ms_per_step": c5["sharded_ms"], "note": "NCCL all-gather of the outputs"},
+            "e2e": {"value": c5["pairs"] / (c5["e2e_ms"] * 1e-3) / 1e9, "unit": UNIT, "ms_per_step": c5["e2e_ms"]},
+        }
     if world == 1 and not args.no_cpu_baseline:
-        v, sample, threads = cpu_port_time(10.0)
-        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+        v, sample, threads, kind = cpu_baseline_config2(10.0)
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample}
     print(json.dumps(line), flush=True)
 
 
@@ -312,7 +489,11 @@ C5 = dict(B=4, N=32768, D=512, R=64, K=64, W=4096, SEED=4)
 C5_WORKLOAD = "config5: causal window 4096 intersect top-k 64, B4 N32768 D512 R64, bf16, softsign, row-sharded"
 
 
-def run_config5(args, rank, world, device):
+def measure_config5(steps, warmup, rank, world, device):
+    """Config 5 (B4 N32768 D512 R64, window 4096, top-k 64) partitioned by query-row blocks
+    over the ranks: block compute alone (outputs left row-sharded) and with the all-gather
+    that assembles them on every rank, plus the end-to-end time with host copies. Every
+    time is the max over ranks. Returns a dict on every rank."""
     import jakal_net_b200 as jk
     from jakal_net_b200 import sharding
 
@@ -365,17 +546,18 @@ def run_config5(args, rank, world, device):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
+    launches_per_step = count_launches(lambda: compute(val, state))
+    for _ in range(warmup):
         compute(val, state)
         gather()
     torch.cuda.synchronize(device)
     if world > 1:
         torch.distributed.barrier()
     with ClockSampler(device.index if device.index is not None else 0) as clk:
-        compute_ms = max_over_ranks(timed(lambda: compute(val, state), args.steps))
+        compute_ms = max_over_ranks(timed(lambda: compute(val, state), steps))
         if world > 1:
             torch.distributed.barrier()
-        sharded_ms = max_over_ranks(timed(lambda: (compute(val, state), gather()), args.steps))
+        sharded_ms = max_over_ranks(timed(lambda: (compute(val, state), gather()), steps))
     h_out_val = torch.empty(b, count, d, dtype=torch.bfloat16).pin_memory()
 
     def e2e():
@@ -387,7 +569,16 @@ def run_config5(args, rank, world, device):
 
     if world > 1:
         torch.distributed.barrier()
-    e2e_ms = max_over_ranks(timed(e2e, max(3, min(args.steps, 20))))
+    e2e_ms = max_over_ranks(timed(e2e, max(3, min(steps, 20))))
+    return dict(pairs=pairs, compute_ms=compute_ms, sharded_ms=sharded_ms, e2e_ms=e2e_ms,
+                launches_per_step=launches_per_step, clocks=clk.summary(),
+                h2d=(h_val.numel() + h_state.numel()) * 2, d2h=h_out_val.numel() * 2)
+
+
+def run_config5(args, rank, world, device):
+    m = measure_config5(args.steps, args.warmup, rank, world, device)
+    b, n, d, r, k, w = C5["B"], C5["N"], C5["D"], C5["R"], C5["K"], C5["W"]
+    pairs, compute_ms, sharded_ms, e2e_ms = m["pairs"], m["compute_ms"], m["sharded_ms"], m["e2e_ms"]
     if rank != 0:
         return
     line = {
@@ -399,12 +590,11 @@ def run_config5(args, rank, world, device):
                    "pairs_per_step": pairs, "l2": "inputs (134 MB values) larger than L2",
                    "timing": "CUDA events per step, max over ranks",
                    "parallelism": f"query-row blocks x{world}; value = block compute, outputs left row-sharded"},
-        "gpu_launches": 3 * args.steps,
-        "clocks": clk.summary(),
+        "gpu_launches": m["launches_per_step"] * args.steps,
+        "clocks": m["clocks"],
         "with_allgather": {"ms_per_step": sharded_ms, "value": pairs / (sharded_ms * 1e-3) / 1e9, "unit": UNIT},
         "e2e": {"value": pairs / (e2e_ms * 1e-3) / 1e9, "unit": UNIT, "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": (h_val.numel() + h_state.numel()) * 2,
-                "d2h_bytes_per_step": h_out_val.numel() * 2},
+                "h2d_bytes_per_step": m["h2d"], "d2h_bytes_per_step": m["d2h"]},
     }
     print(json.dumps(line), flush=True)
 
@@ -621,6 +811,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", type=int, choices=[2, 4, 5], default=2)
     ap.add_argument("--no-reference-gpu", action="store_true")
+    ap.add_argument("--no-config5", action="store_true", help="skip the config-5 row-sharded record of the default run")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

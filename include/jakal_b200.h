@@ -288,6 +288,32 @@ int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_pr
                                         void* out_val, int out_dtype, jk_stream_t stream);
 
 /*
+ * Routes form of the per-source sparse transition (deterministic, no atomics):
+ *   routes[b, s, d] = compress(logit[b, s, :] over sel(s))[d] * (src_sender ? src_sender[b, s] : 1)
+ * for the k selected destinations d of every source s (selection, bias and compressors as
+ * jk_transition_pairwise_topk_forward); every other entry is left untouched, so the caller
+ * zeroes routes (f32 [B, n_src, n_dst]) first. The aggregate
+ *   out_state[b, d] = sum_s routes[b, s, d] * src_state[b, s],
+ *   out_val[b, d, :] = sum_s routes[b, s, d] * src_val[b, s, :]
+ * is then a plain GEMM (routes^T x values), with no atomics and a fixed summation order.
+ * Same sizes and limits as jk_transition_pairwise_topk_forward (1 <= k <= 64, rp <= 128).
+ * Replaces the scatter of low_rank_pairwise_topk_forward_cuda (jakal_net_native_cuda.cu:
+ * 740-878, atomicAdd at :862-873) and of the blocked path jakal_net_native.cpp:6916-7087.
+ */
+int jk_transition_pairwise_topk_routes(const void* src_proj, const void* dst_proj, int64_t batch,
+                                       int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                       const void* src_sender, int state_dtype, int64_t k,
+                                       float score_bias, const float* bias_dev, int compress,
+                                       float* routes, jk_stream_t stream);
+
+/* Multi-head (jk_heads_t) variant of jk_transition_pairwise_topk_routes. */
+int jk_transition_pairwise_topk_routes_mh(const void* src_proj, const void* dst_proj, int64_t batch,
+                                          int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                          const void* src_sender, int state_dtype, int64_t k,
+                                          float score_bias, const float* bias_dev, int compress,
+                                          float* routes, const jk_heads_t* heads, jk_stream_t stream);
+
+/*
  * Select-aggregate over materialised f32 score rows (any k, any score rank):
  *   scores [B, row_count, n_cols] holds score[b, t, s] for the rows t in
  *   [row_begin, row_begin + row_count) of an n_rows-row operator (e.g. a plain GEMM of the

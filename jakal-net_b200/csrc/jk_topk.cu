@@ -131,6 +131,10 @@ struct Params {
   // state / value / sender (col_state / col_val / col_sender are indexed by the row).
   float* acc_state;
   float* acc_val;
+  // scatter, routes form: the compressed, sender-weighted route of every selected
+  // (source row, destination column) is written to routes [B, n_rows, n_cols] (f32, zeroed
+  // by the caller) instead of being scatter-added; the aggregate is then a plain GEMM.
+  float* routes;
 };
 
 __device__ __forceinline__ bool worse(float av, int ai, float bv, int bi) {
@@ -418,6 +422,11 @@ __device__ void scatter_row(const Lane& f, int n, int64_t b, int64_t src, const 
   const int64_t D = p.dim;
   float sender = 1.f;
   if (p.col_sender) sender = ld_elem(p.col_sender, src, p.state_dtype);
+  if (p.routes != nullptr) {  // routes form: one plain store per selected destination
+    float* rrow = p.routes + src * p.n_cols;
+    for (int e = lane; e < n; e += 32) rrow[f.idx(e)] = f.val(e) * sender;
+    return;
+  }
   const float sstate = ld_elem(p.col_state, src, p.state_dtype);
   const bool vec = (D % 8) == 0 && D <= 1024 && sizeof(VT) == 2;
   const int nch = static_cast<int>(D / 8);
@@ -1669,6 +1678,46 @@ int gather_forward(const void* row_proj, const void* col_proj, int64_t batch, in
                          reinterpret_cast<cudaStream_t>(stream));
 }
 
+int routes_forward(const void* src_proj, const void* dst_proj, int64_t batch, int64_t n_src, int64_t n_dst,
+                   int64_t rp, int proj_dtype, const void* src_sender, int state_dtype, int64_t k, float score_bias,
+                   const float* bias_dev, int compress, float* routes, const jk_heads_t* heads, jk_stream_t stream) {
+  // the value / state arguments of the shared checks are not read in the routes form
+  int st = validate_common(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, routes, JK_F32, routes, 1, JK_F32,
+                           k, compress, JK_F32);
+  if (st != JK_OK) return st;
+  if (routes == nullptr) return JK_ERR_BAD_ARG;
+  if (src_sender != nullptr && (state_dtype < JK_F32 || state_dtype > JK_F16)) return JK_ERR_BAD_DTYPE;
+  Heads hd;
+  st = read_heads(heads, rp, proj_dtype, 4, hd);
+  if (st != JK_OK) return st;
+  st = check_device();
+  if (st != JK_OK) return st;
+  Params p{};
+  p.n_rows = n_src;
+  p.row_count = n_src;
+  p.n_cols = n_dst;
+  p.rp = rp;
+  p.dim = 1;
+  p.k = static_cast<int>(k);
+  p.window = -1;
+  p.bias = score_bias;
+  p.bias_dev = bias_dev;
+  p.compress = compress;
+  p.state_dtype = state_dtype;
+  p.val_dtype = JK_F32;
+  p.out_dtype = JK_F32;
+  p.col_state = routes;
+  p.col_val = routes;
+  p.col_sender = src_sender;
+  p.routes = routes;
+  p.heads = hd.heads;
+  p.kph = hd.kph;
+  p.combine = hd.combine;
+  p.head_bias = hd.bias;
+  return launch<kScatter>(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, p,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
 int scatter_forward(const void* src_proj, const void* dst_proj, int64_t batch, int64_t n_src, int64_t n_dst,
                     int64_t rp, int proj_dtype, const void* src_state, const void* src_sender, int state_dtype,
                     const void* src_val, int64_t dim, int val_dtype, int64_t k, float score_bias,
@@ -1823,6 +1872,26 @@ extern "C" int jk_debug_trace(long long* out, int n_ctas) {
   return cudaMemcpyFromSymbol(out, jk::topk::g_trace, sizeof(long long) * 32 * n) == cudaSuccess ? 0 : -1;
 }
 #endif
+
+
+extern "C" int jk_transition_pairwise_topk_routes(const void* src_proj, const void* dst_proj, int64_t batch,
+                                                  int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                                  const void* src_sender, int state_dtype, int64_t k,
+                                                  float score_bias, const float* bias_dev, int compress,
+                                                  float* routes, jk_stream_t stream) {
+  return jk::topk::routes_forward(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_sender, state_dtype, k,
+                                  score_bias, bias_dev, compress, routes, nullptr, stream);
+}
+
+extern "C" int jk_transition_pairwise_topk_routes_mh(const void* src_proj, const void* dst_proj, int64_t batch,
+                                                     int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
+                                                     const void* src_sender, int state_dtype, int64_t k,
+                                                     float score_bias, const float* bias_dev, int compress,
+                                                     float* routes, const jk_heads_t* heads, jk_stream_t stream) {
+  if (heads == nullptr) return JK_ERR_BAD_ARG;
+  return jk::topk::routes_forward(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_sender, state_dtype, k,
+                                  score_bias, bias_dev, compress, routes, heads, stream);
+}
 
 namespace jk {
 JK_ERROR_READER(read_error_topk)

@@ -24,7 +24,9 @@ Two kernel families serve every op:
     take any k (jakal_net_native.cpp:6390-6447, 6916-7087, 7089-7246).
 Under CUDA autocast the scorer inputs are cast to the autocast dtype before the projection
 GEMMs, as the reference's at::matmul inside its extension is (jakal_net_native.cpp:6236-6239
-runs within the caller's autocast region); values, states and outputs keep their dtypes.
+runs within the caller's autocast region), and the aggregated values / states are cast to it
+as autocast casts the reference's own einsum / bmm aggregates; accumulation is f32 and the
+outputs keep the dtypes of the projected inputs.
 """
 from __future__ import annotations
 
@@ -134,6 +136,18 @@ def _scorer_input(x: Tensor) -> Tensor:
     """The scorer (projection GEMM) input in the dtype the reference's at::matmul would use:
     f32 inputs are cast to the caller's autocast dtype when an op was called under CUDA
     autocast."""
+    ac = getattr(_TLS, "autocast", None)
+    if ac is not None and x.dtype == torch.float32:
+        return x.to(ac)
+    return x
+
+
+def _aggregate_input(x: Tensor) -> Tensor:
+    """An aggregated operand (projected state / value, sender strength) in the dtype the
+    caller's autocast gives the reference's own aggregate: under CUDA autocast its einsum /
+    bmm aggregates (propagation.py:215-219, transition.py:246-254) run in the autocast dtype,
+    so f32 operands are cast to it; accumulation stays f32 and the outputs keep the dtype of
+    the projected inputs."""
     ac = getattr(_TLS, "autocast", None)
     if ac is not None and x.dtype == torch.float32:
         return x.to(ac)
@@ -630,6 +644,24 @@ def _value_planes(pval: Tensor, proj_dtype: torch.dtype):
     return pval.contiguous(), pval_lo, pad
 
 
+def routes_aggregate(routes: Tensor, state: Tensor, val: Tensor) -> tuple[Tensor, Tensor]:
+    """Aggregate of a dense route matrix: out_state[b, d] = sum_s routes[b, s, d] state[b, s],
+    out_val[b, d] = sum_s routes[b, s, d] val[b, s] (f32 results). 16-bit values take two
+    tensor-core GEMMs against the routes split into hi + lo planes of the values' dtype
+    (f32 accumulation and output, ~16-bit route weights); f32 values one f32 GEMM."""
+    rt = routes.transpose(1, 2)
+    with _exact_f32_matmul():
+        out_state = torch.bmm(rt, state.float().unsqueeze(-1)).squeeze(-1)
+        if val.dtype in (torch.bfloat16, torch.float16):
+            hi = routes.to(val.dtype)
+            lo = (routes - hi.float()).to(val.dtype)
+            out_val = torch.bmm(hi.transpose(1, 2), val, out_dtype=torch.float32)
+            out_val += torch.bmm(lo.transpose(1, 2), val, out_dtype=torch.float32)
+        else:
+            out_val = torch.bmm(rt, val.float())
+    return out_state, out_val
+
+
 # ----------------------------------------------------------------------------- ops
 def _check_edge(edge_compress_name: str) -> int:
     if edge_compress_name not in _EDGE_CODE:
@@ -659,8 +691,8 @@ def _propagation_topk_impl(kind, weight, bias, in_weight, in_bias, out_weight, o
     batch_shape = layer_val.shape[:-2]
     out_dim = projected_val.shape[-1]
     val = _flatten_val(layer_val)
-    pstate = _flatten_state(projected_state)
-    pval = _flatten_val(projected_val)
+    pstate = _aggregate_input(_flatten_state(projected_state))
+    pval = _aggregate_input(_flatten_val(projected_val))
     out_dtype = _out_dtype(projected_state, projected_val)
     sc = _pair_scorer(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, val, val, fused=k <= _MAX_K)
     if sc.fused:
@@ -702,9 +734,9 @@ def _transition_inputs(sender_strength, src_val, other_val, projected_state, pro
     for name, t in (("sender_strength", sender_strength), ("src_val", src_val), ("dst/query_val", other_val),
                     ("projected_state", projected_state), ("projected_val", projected_val)):
         _require_cuda(name, t)
-    pstate = _flatten_state(projected_state)
+    pstate = _aggregate_input(_flatten_state(projected_state))
     sender = _flatten_state(sender_strength).to(pstate.dtype)
-    return _flatten_val(src_val), _flatten_val(other_val), pstate, sender, _flatten_val(projected_val)
+    return _flatten_val(src_val), _flatten_val(other_val), pstate, sender, _aggregate_input(_flatten_val(projected_val))
 
 
 @_entry
@@ -764,7 +796,22 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
     B = sv.shape[0]
     dev = sv.device
     out_dtype = _out_dtype(projected_state, projected_val)
-    if sc.fused:
+    if sc.fused and B * sv.shape[1] * n_dst <= _SCORE_BUDGET:
+        # routes form: the fused kernel writes the dense route matrix (k non-zeros per source),
+        # the aggregate is a GEMM -- no atomics, a fixed summation order
+        routes = torch.zeros((B, sv.shape[1], n_dst), device=dev, dtype=torch.float32)
+        args = (sc.row.data_ptr(), sc.col.data_ptr(), B, sv.shape[1], n_dst, sc.row.shape[-1],
+                _proj_dtype(sc.row, sc.split3), sender.data_ptr(), _dtype_code("sender", sender), k, 0.0,
+                _ptr(sc.bias), compress, routes.data_ptr())
+        with torch.cuda.device(dev):
+            if sc.heads is None:
+                check(_LIBRARY.jk_transition_pairwise_topk_routes(*args, _stream(dev)),
+                      "jk_transition_pairwise_topk_routes")
+            else:
+                check(_LIBRARY.jk_transition_pairwise_topk_routes_mh(*args, sc.heads.ref(), _stream(dev)),
+                      "jk_transition_pairwise_topk_routes_mh")
+        out_state, out_val = routes_aggregate(routes, pstate, pval)
+    elif sc.fused:
         accum = torch.empty(B * n_dst * (out_dim + 1) + 4, device=dev, dtype=torch.float32)
         out_state = torch.empty((B, n_dst), device=dev, dtype=out_dtype)
         out_val = torch.empty((B, n_dst, out_dim), device=dev, dtype=out_dtype)
@@ -862,6 +909,7 @@ def _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, e
         ss = _flatten_state(source_state).float()
         pstate = (pstate.float() * ss).to(pstate.dtype)
         pval = (pval.float() * ss[..., None]).to(pval.dtype)
+    pstate, pval = _aggregate_input(pstate), _aggregate_input(pval)
     sc = _pair_scorer(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, tv, sv)
     if sc.heads is not None and sc.heads.struct.heads > 2:
         raise TypeError("b200_sm100a window / dense multi-head scorers support 2 heads.")

@@ -98,6 +98,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _p, _p, _i32, _p],
     ),
     "jk_transition_pairwise_topk_noalloc_capacity": (_i64, []),
+    "jk_transition_pairwise_topk_routes": (
+        _i32,
+        [_p, _p, _i64, _i64, _i64, _i64, _i32,  # src_proj, dst_proj, B, n_src, n_dst, rp, proj_dtype
+         _p, _i32, _i64, _f32, _p, _i32,        # src_sender, state_dtype, k, score_bias, bias_dev, compress
+         _p, _p],                               # routes, stream
+    ),
     "jk_select_aggregate_forward": (
         _i32,
         [_p, _i64, _i64, _i64, _i64, _i64,      # scores, B, n_rows, n_cols, row_begin, row_count
@@ -112,7 +118,8 @@ SIGNATURES["jk_propagation_topk_rows_forward"] = (_i32, _args[:4] + [_i64, _i64]
 # The multi-head variants take the same arguments plus a jk_heads_t* before the stream.
 _HP = ctypes.POINTER(JkHeads)
 for _name in ("jk_propagation_topk_forward", "jk_transition_query_topk_forward", "jk_transition_pairwise_topk_forward",
-              "jk_propagation_window_forward", "jk_transition_pairwise_dense_forward"):
+              "jk_propagation_window_forward", "jk_transition_pairwise_dense_forward",
+              "jk_transition_pairwise_topk_routes"):
     _res, _args = SIGNATURES[_name]
     SIGNATURES[_name + "_mh"] = (_res, _args[:-1] + [_HP, _p])
 

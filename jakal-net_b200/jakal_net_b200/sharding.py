@@ -63,31 +63,41 @@ def _kernel_block(row_proj, col_proj, col_state, col_val, k, window, begin, coun
         )
 
 
-def gather_row_blocks(out_state: Tensor, out_val: Tensor, blocks: list[tuple[int, int]], group=None):
+def gather_row_blocks(out_state: Tensor, out_val: Tensor, blocks: list[tuple[int, int]], group=None,
+                      stream: Optional[torch.cuda.Stream] = None):
     """Assembles the row blocks every rank wrote into its own out_state [B, N] / out_val
-    [B, N, D] so that every rank holds the full outputs. Equal blocks that tile N exactly:
-    one in-place all-gather per batch item (a rank's block is the rank-th chunk of out[b]);
-    otherwise the blocks go through a padded [world, B, blk, ...] exchange buffer."""
+    [B, N, D] so that every rank holds the full outputs: one rank-major all-gather per
+    tensor (the rank's block of every batch item packed into a [B, blk, ...] buffer,
+    gathered into [world, B, blk, ...]) -- two collectives whatever the batch size -- then
+    the blocks are copied into place. With `stream` the exchange runs on that stream
+    (ordered after the current stream's work), so a caller can overlap it with compute."""
     world = len(blocks)
-    blk = blocks[0][1]
-    B, N = out_state.shape
-    if blk * world == N:
-        for b in range(B):
-            for full in (out_state[b], out_val[b]):
-                mine = full[blocks[dist.get_rank(group)][0]:][:blk]
-                dist.all_gather_into_tensor(full, mine, group=group)
-        return out_state, out_val
     rank = dist.get_rank(group)
+    blk = max(c for _, c in blocks)
+    B = out_state.shape[0]
     begin, count = blocks[rank]
-    for full in (out_state, out_val):
-        send = full.new_zeros((B, blk) + tuple(full.shape[2:]))
-        send[:, :count] = full[:, begin:begin + count]
-        recv = full.new_empty((world * B,) + tuple(send.shape[1:]))  # rank-major concatenation
-        dist.all_gather_into_tensor(recv, send, group=group)
-        recv = recv.view((world,) + tuple(send.shape))
-        for r, (b0, c) in enumerate(blocks):
-            full[:, b0:b0 + c] = recv[r, :, :c]
+    ctx = torch.cuda.stream(stream) if stream is not None else _nullcontext()
+    if stream is not None:
+        stream.wait_stream(torch.cuda.current_stream(out_val.device))
+    with ctx:
+        for full in (out_state, out_val):
+            send = full.new_zeros((B, blk) + tuple(full.shape[2:]))
+            send[:, :count] = full[:, begin:begin + count]
+            recv = full.new_empty((world * B,) + tuple(send.shape[1:]))  # rank-major concatenation
+            dist.all_gather_into_tensor(recv, send, group=group)
+            recv = recv.view((world,) + tuple(send.shape))
+            for r, (b0, c) in enumerate(blocks):
+                if c:
+                    full[:, b0:b0 + c] = recv[r, :, :c]
     return out_state, out_val
+
+
+class _nullcontext:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
 
 
 def propagation_window_topk_rows(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_val: Tensor, k: int,

@@ -1,10 +1,10 @@
-"""Builds the reference's own native extension from its sources into oracle/_ref/ (checker only).
+"""Builds the reference's own native extension (CPU) from its sources into oracle/_ref/cpu/.
 
-    python oracle/build_ref.py [--cpu] [--cuda] [--src PATH_TO_REFERENCE_CHECKOUT]
+    python oracle/build_ref.py [--src PATH_TO_REFERENCE_CHECKOUT]
 
-Test and baseline infrastructure: nothing in the product package imports what this builds.
+Test infrastructure (a checker): nothing in the product package imports what this builds.
 
-* --cpu: ``native/jakal_net_native.cpp`` compiled CPU-only with torch.utils.cpp_extension,
+* ``native/jakal_net_native.cpp`` compiled CPU-only with torch.utils.cpp_extension,
   plus a two-function stub. The .cpp calls two availability probes that only the .cu defines
   (``jakal_net_low_rank_dense_scores_tf32_cuda_available`` and
   ``jakal_net_low_rank_propagation_dense_tf32_forward_cuda_available``, referenced outside its
@@ -12,21 +12,15 @@ Test and baseline infrastructure: nothing in the product package imports what th
   means. Module name ``jakal_net_native`` (backend "aten_cpp_cpu"). Its per-query transition
   (jakal_net_native.cpp:7089-7246) generates the fixtures that pin the oracle's
   transition_query_topk (tests/golden/make_golden_native.py).
-* --cuda: the same .cpp plus ``native/jakal_net_native_cuda.cu`` with ``-DWITH_CUDA`` for
-  sm_100 (the reference's own build recipe, scripts/build_native_extension.py, with the
-  architecture fixed). Module name ``jakal_net_native`` too, in its own folder. nvcc cross-
-  compiles it here; on the GPU host it is the same-box GPU reference (bench.py
-  --impl reference-gpu) and the pin of the bf16 rounding chain of the CUDA fast paths.
-
-Nothing in the reference tree is modified; outputs go to oracle/_ref/{cpu,cuda}/ only
-(git-ignored, shipped with the tree to the GPU host like the product library).
+Nothing in the reference tree is modified; outputs go to oracle/_ref/cpu/ only (git-ignored,
+shipped with the tree to the GPU host like the product library). The reference's CUDA build
+is baseline/build_reference_cuda.py.
 """
 from __future__ import annotations
 
 import argparse
 import importlib.machinery
 import importlib.util
-import os
 import sys
 from pathlib import Path
 
@@ -40,28 +34,17 @@ bool jakal_net_low_rank_propagation_dense_tf32_forward_cuda_available() { return
 """
 
 
-def build(kind: str, src: Path = DEFAULT_SRC, verbose: bool = False) -> Path:
+def build(kind: str = "cpu", src: Path = DEFAULT_SRC, verbose: bool = False) -> Path:
     from torch.utils.cpp_extension import load
 
     native = src / "native"
     out = REF_OUT / kind
     out.mkdir(parents=True, exist_ok=True)
-    sources = [str(native / "jakal_net_native.cpp")]
-    cflags = ["-std=c++17", "-O3"]
-    if kind == "cpu":
-        stub = out / "cuda_probe_stub.cpp"
-        stub.write_text(STUB)
-        sources.append(str(stub))
-        with_cuda = False
-        cuda_flags = None
-    else:
-        sources.append(str(native / "jakal_net_native_cuda.cu"))
-        cflags.append("-DWITH_CUDA")
-        with_cuda = True
-        cuda_flags = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a"]
-        os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0")
-    load(name="jakal_net_native", sources=sources, build_directory=str(out), verbose=verbose, with_cuda=with_cuda,
-         extra_include_paths=[str(native)], extra_cflags=cflags, extra_cuda_cflags=cuda_flags)
+    stub = out / "cuda_probe_stub.cpp"
+    stub.write_text(STUB)
+    load(name="jakal_net_native", sources=[str(native / "jakal_net_native.cpp"), str(stub)],
+         build_directory=str(out), verbose=verbose, with_cuda=False, extra_include_paths=[str(native)],
+         extra_cflags=["-std=c++17", "-O3"])
     return out / "jakal_net_native.so"
 
 
@@ -89,11 +72,7 @@ def available(kind: str) -> bool:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--cpu", action="store_true")
-    ap.add_argument("--cuda", action="store_true")
     ap.add_argument("--src", type=Path, default=DEFAULT_SRC)
     ap.add_argument("--verbose", action="store_true")
     a = ap.parse_args()
-    kinds = [k for k, on in (("cpu", a.cpu), ("cuda", a.cuda)) if on] or ["cpu"]
-    for k in kinds:
-        print(build(k, a.src, a.verbose))
+    print(build("cpu", a.src, a.verbose))
