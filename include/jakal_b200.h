@@ -342,6 +342,52 @@ int jk_select_aggregate_forward(const float* scores, int64_t batch, int64_t n_ro
                                 void* out_val, int out_dtype, float* acc_state, float* acc_val,
                                 float* sel_score, int64_t* sel_index, jk_stream_t stream);
 
+/* ---- backward (training) kernels --------------------------------------------------
+ * The row-wise pieces of the top-k operators' backward, behind the reference's autograd
+ * Functions (native_backend.py:4408-4601 uses softmax_backward_cuda and the reduce
+ * backward; the kernels replaced are jakal_net_native_cuda.cu:2112-2320). `dtype` applies to
+ * every tensor argument of a call (JK_F32, JK_BF16, JK_F16); accumulation is f32.
+ */
+
+/* grad_scores[r, j] = routes[r, j] * (grad_routes[r, j] - sum_j' routes[r, j'] grad_routes[r, j'])
+ * for rows x n row-major tensors (the softmax backward; jakal_net_native.cpp:408-416). */
+int jk_softmax_backward(const void* routes, const void* grad_routes, void* grad_scores, int64_t rows,
+                        int64_t n, int dtype, jk_stream_t stream);
+
+/* grad_scores[i] = grad_edges[i] / (1 + |scores[i]|)^2 over n elements (softsign backward;
+ * jakal_net_native.cpp:398-406). */
+int jk_softsign_backward(const void* scores, const void* grad_edges, void* grad_scores, int64_t n,
+                         int dtype, jk_stream_t stream);
+
+/* Gather half of the backward of a top-k reduce (out[b, q] = sum_e edges[b, q, e] *
+ * x[b, indices[b, q, e]]; jakal_net_native.cpp:152-166):
+ *   grad_edges[b, q, e] = grad_state[b, q] * state[b, idx] + grad_val[b, q, :] . val[b, idx, :]
+ * indices int64 [B, n_rows, k] (-1: no edge, gradient 0), state [B, n_src], val
+ * [B, n_src, dim], grad_state [B, n_rows], grad_val [B, n_rows, dim] in dtype; grad_edges
+ * [B, n_rows, k] in out_dtype. The scatter half (the gradients of state and val) is a GEMM of
+ * the dense edge matrix (jk_topk_to_dense). */
+int jk_topk_reduce_backward_edges(const int64_t* indices, const void* state, const void* val,
+                                  const void* grad_state, const void* grad_val, void* grad_edges,
+                                  int64_t batch, int64_t n_rows, int64_t n_src, int64_t k, int64_t dim,
+                                  int dtype, int out_dtype, jk_stream_t stream);
+
+/* dense[r, indices[r, e]] = w[r, e] for rows x k selections (f32 w, int64 indices, -1
+ * skipped); dense f32 [rows, n_cols] zeroed by the caller. Turns the scatters of the
+ * backward into GEMMs with a fixed summation order. */
+int jk_topk_to_dense(const float* w, const int64_t* indices, float* dense, int64_t rows, int64_t k,
+                     int64_t n_cols, jk_stream_t stream);
+
+/* Failure-path test entry (no reference counterpart): jk_propagation_window_forward
+ * (softsign, no bias) with a producer warp that issues no load and no MMA, so every consumer
+ * wait runs into its bound (about 2 s): the kernel sets the device error word, releases its
+ * TMEM and returns; jk_device_status then reports JK_ERR_DEVICE_TIMEOUT and the context stays
+ * usable. Outputs are zeros. For tests of that path only. */
+int jk_debug_window_stalled_producer(const void* row_proj, const void* col_proj, int64_t batch,
+                                     int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
+                                     const void* col_state, int state_dtype, const void* col_val,
+                                     int64_t dim, int64_t window, void* out_state, void* out_val,
+                                     int out_dtype, jk_stream_t stream);
+
 /*
  * Allocation-free per-source sparse transition. No counterpart in the reference: it exists
  * for callers that cannot allocate device memory at call time -- plain-C / FFI hosts with no

@@ -70,6 +70,9 @@ struct Params {
   // combined as they are read (JK_HEADS_*); heads == 1 keeps two 128-column buffers
   int heads, kph, combine;
   const float* head_bias;
+  // Failure-path test only (jk_debug_window_stalled_producer): the producer warp issues no
+  // load and no MMA, so every consumer wait runs into its bound and the kernel unwinds.
+  int debug_stall;
 };
 
 // One edge from a score and the (max, scale / normaliser, tau) of its normalisation set.
@@ -214,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kSelWarps) {
     // ------------------------------------------------------------ producer / MMA issuer
-    if (lane == 0 && ntiles > 0) {
+    if (lane == 0 && ntiles > 0 && !p.debug_stall) {
       prefetch_tmap(&tm_rows);
       prefetch_tmap(&tm_cols);
       prefetch_tmap(&tm_val);
@@ -721,7 +724,7 @@ int window_forward(const void* row_proj, const void* col_proj, int64_t batch, in
                    int64_t rp, int proj_dtype, const void* col_state, int state_dtype, const void* col_val,
                    const void* col_val_lo, int64_t dim, int64_t window, float score_bias, const float* bias_dev,
                    int compress, void* out_state, void* out_val, int out_dtype, const jk_heads_t* heads,
-                   jk_stream_t stream) {
+                   jk_stream_t stream, int debug_stall = 0) {
   if (compress != JK_SOFTSIGN && compress != JK_SIGNED_ABS_SOFTMAX && compress != JK_SIGNED_ENTMAX15)
     return JK_ERR_UNSUPPORTED_KIND;
   if (window < -1) return JK_ERR_BAD_ARG;
@@ -730,6 +733,7 @@ int window_forward(const void* row_proj, const void* col_proj, int64_t batch, in
                          col_val_lo, dim, score_bias, bias_dev, compress, out_state, out_val, out_dtype, heads, p);
   if (st != JK_OK) return st;
   p.window = window;
+  p.debug_stall = debug_stall;
   return run(row_proj, col_proj, col_val, col_val_lo, batch, n_rows, n_cols, rp, proj_dtype, p, stream);
 }
 
@@ -763,6 +767,20 @@ int transition_dense_forward(const void* src_proj, const void* dst_proj, int64_t
 
 }  // namespace win
 }  // namespace jk
+
+// Failure-path test entry: jk_propagation_window_forward with a producer warp that issues
+// nothing. Every consumer wait gives up after its bound (about 2 s), sets the device error
+// word, releases TMEM and returns; jk_device_status then reports JK_ERR_DEVICE_TIMEOUT and
+// the context stays usable. Outputs are zeros. Only for tests of that path.
+extern "C" int jk_debug_window_stalled_producer(const void* row_proj, const void* col_proj, int64_t batch,
+                                                int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,
+                                                const void* col_state, int state_dtype, const void* col_val,
+                                                int64_t dim, int64_t window, void* out_state, void* out_val,
+                                                int out_dtype, jk_stream_t stream) {
+  return jk::win::window_forward(row_proj, col_proj, batch, n_rows, n_cols, rp, proj_dtype, col_state, state_dtype,
+                                 col_val, nullptr, dim, window, 0.f, nullptr, JK_SOFTSIGN, out_state, out_val,
+                                 out_dtype, nullptr, stream, 1);
+}
 
 extern "C" int jk_propagation_window_forward(const void* row_proj, const void* col_proj, int64_t batch,
                                              int64_t n_rows, int64_t n_cols, int64_t rp, int proj_dtype,

@@ -93,14 +93,21 @@ _SUPPORTED_OPS = (
     "transition_pairwise_dense",
     "transition_pairwise_topk",
     "transition_query_topk",
+    # training: the per-source sparse transition's autograd route (native_backend.py:5962-5975)
+    "low_rank_pairwise_topk_forward_cuda",
+    "low_rank_pairwise_topk_backward_cuda",
+    "query_topk_reduce_backward_cuda",
+    "softsign_backward_cuda",
+    "softmax_backward_cuda",
 )
 
 
 def supported_ops() -> list[str]:
-    """Ops this module implements (jakal_net_native.cpp:5863-5912 contract). The
-    ``*_cuda`` autograd entry points are deliberately not advertised: this backend is
-    forward-only, and advertising them would route training through them
-    (native_backend.py:659-667)."""
+    """Ops this module implements (jakal_net_native.cpp:5863-5912 contract), including the
+    CUDA entry points of the per-source sparse transition's autograd route
+    (native_backend.py:659-667, 4408-4601, 5962-5975). The propagation autograd routes stay
+    on the reference: they are behind its experimental-training switch and need entry
+    points this module does not export (low_rank_propagation_*_forward_cuda)."""
     return list(_SUPPORTED_OPS)
 
 
@@ -532,11 +539,11 @@ def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_va
 def select_aggregate(row_f: Tensor, col_f: Tensor, state: Tensor, val: Tensor, k: int, *, window: int = -1,
                      compress: int = _lib.JK_SOFTSIGN, sender: Optional[Tensor] = None,
                      bias: Optional[Tensor] = None, scatter: bool = False, out_dtype: Optional[torch.dtype] = None,
-                     return_selection: bool = False, budget: int = _SCORE_BUDGET):
+                     return_selection: bool = False, budget: int = _SCORE_BUDGET, score_bias: float = 0.0):
     """Select-aggregate over materialised score blocks (jk_select_aggregate_forward): any k,
-    any rank. row_f [B, T, R] and col_f [B, S, R] are f32 projections; every block of rows
-    gets its f32 scores from one GEMM (TF32 off) and then the exact select / compress /
-    aggregate kernel.
+    any rank. row_f [B, T, R] and col_f [B, S, R] are the projections (f32, or bf16 / f16
+    whose products are exact in f32); every block of rows gets its f32 scores from one GEMM
+    (f32 accumulation, TF32 off) and then the exact select / compress / aggregate kernel.
 
     gather (scatter False): state / sender [B, S], val [B, S, D] per column; returns
     (state [B, T], val [B, T, D]) in out_dtype. scatter True (per-source transition): rows
@@ -572,11 +579,15 @@ def select_aggregate(row_f: Tensor, col_f: Tensor, state: Tensor, val: Tensor, k
     with torch.cuda.device(dev):
         for r0 in range(0, T, chunk):
             rc = min(chunk, T - r0)
-            with _exact_f32_matmul():
-                sc = torch.bmm(row_f[:, r0:r0 + rc], col_t).contiguous()
+            if row_f.dtype in (torch.bfloat16, torch.float16):
+                # exact products of 16-bit projections, f32 accumulation and output
+                sc = torch.bmm(row_f[:, r0:r0 + rc], col_t, out_dtype=torch.float32).contiguous()
+            else:
+                with _exact_f32_matmul():
+                    sc = torch.bmm(row_f[:, r0:r0 + rc], col_t).contiguous()
             check(_LIBRARY.jk_select_aggregate_forward(
                 sc.data_ptr(), B, T, S, r0, rc, state.data_ptr(), _ptr(snd), _dtype_code("state", state),
-                val.data_ptr(), D, _dtype_code("val", val), kk, int(window), 0.0, _ptr(bias), compress,
+                val.data_ptr(), D, _dtype_code("val", val), kk, int(window), float(score_bias), _ptr(bias), compress,
                 1 if scatter else 0, _ptr(out_state), _ptr(out_val), _dtype_code("out", out_state if out_state is not None else val),
                 _ptr(acc_state), _ptr(acc_val), sel_s.data_ptr(), sel_i.data_ptr(), _stream(dev)),
                 "jk_select_aggregate_forward")
@@ -955,3 +966,152 @@ def propagation_query_dense(kind, weight, bias, in_weight, in_bias, out_weight, 
     """Dense query propagation: query rows score every source row (jakal_net_native.cpp:6078-6188)."""
     return _masked_impl(kind, weight, bias, in_weight, in_bias, out_weight, out_bias, edge_compress_name, query_val,
                         source_val, projected_state, projected_val, -1)
+
+
+# ----------------------------------------------------------------------------- training ops
+# The CUDA entry points the reference's autograd Functions call from the native module
+# (native_backend.py:659-667 gates on their names; _LowRankTransitionPairwiseTopK,
+# native_backend.py:4408-4601, uses them for the per-source sparse transition, forward and
+# backward). Positional signatures and return tuples follow jakal_net_native.cpp:152-190,
+# 398-416, 450-478.
+_PAIRWISE_TOPK_COMPRESS = {0: _lib.JK_SOFTMAX, 1: _lib.JK_SIGNED_ABS_SOFTMAX, 2: _lib.JK_SIGNED_ENTMAX15}
+
+
+def _cuda_contig(name: str, t: Tensor) -> Tensor:
+    _require_cuda(name, t)
+    return t.contiguous()
+
+
+@_entry
+def low_rank_pairwise_topk_forward_cuda(weighted_projected_source, projected_target, weighted_projected_state,
+                                        weighted_projected_val, topk, score_bias, compress_kind):
+    """Per-source top-k transition over given projections (jakal_net_native_cuda.cu:2420-2542
+    contract): logits[b, s, d] = wps[b, s] . pt[b, d] + score_bias; every source keeps its
+    top-k destinations, routes = compress_kind (0 softmax, 1 signed_abs_softmax,
+    2 signed_entmax15) over the k, and scatters routes * wstate / routes * wval.
+    Returns (delta_state f32 [B, D], delta_val f32 [B, D, V], topk_scores f32 [B, S, k]
+    (score + bias), topk_indices int64 [B, S, k]); the selection is listed in ascending
+    destination order (the backward only needs the (score, index) pairs)."""
+    if weighted_projected_source.dim() != 3:
+        raise TypeError("b200_sm100a low_rank_pairwise_topk_forward_cuda takes single-head [B, S, R] projections.")
+    if int(compress_kind) not in _PAIRWISE_TOPK_COMPRESS:
+        raise RuntimeError(f"unsupported compress kind {compress_kind}")
+    wps = _cuda_contig("weighted_projected_source", weighted_projected_source)
+    pt = _cuda_contig("projected_target", projected_target).to(wps.dtype)
+    if wps.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise RuntimeError(f"unsupported projection dtype {wps.dtype}")
+    wstate = _cuda_contig("weighted_projected_state", weighted_projected_state).float()
+    wval = _cuda_contig("weighted_projected_val", weighted_projected_val).float()
+    k = min(int(topk), pt.shape[1])
+    if k <= 0:
+        raise RuntimeError("topk must be positive.")
+    d_state, d_val, scores, index = select_aggregate(wps, pt, wstate, wval, k,
+                                                     compress=_PAIRWISE_TOPK_COMPRESS[int(compress_kind)],
+                                                     scatter=True, return_selection=True,
+                                                     score_bias=float(score_bias))
+    return d_state, d_val, scores, index
+
+
+@_entry
+def softmax_backward_cuda(routes, grad_routes):
+    """grad_scores = routes * (grad_routes - sum(routes * grad_routes, -1)) (jk_softmax_backward)."""
+    r = _cuda_contig("routes", routes)
+    g = _cuda_contig("grad_routes", grad_routes).to(r.dtype)
+    out = torch.empty_like(r)
+    n = r.shape[-1] if r.dim() else 1
+    with torch.cuda.device(r.device):
+        check(_LIBRARY.jk_softmax_backward(r.data_ptr(), g.data_ptr(), out.data_ptr(), r.numel() // max(n, 1), n,
+                                           _dtype_code("routes", r), _stream(r.device)), "jk_softmax_backward")
+    return out
+
+
+@_entry
+def softsign_backward_cuda(scores, grad_edges):
+    """grad_scores = grad_edges / (1 + |scores|)^2 (jk_softsign_backward)."""
+    s = _cuda_contig("scores", scores)
+    g = _cuda_contig("grad_edges", grad_edges).to(s.dtype)
+    out = torch.empty_like(s)
+    with torch.cuda.device(s.device):
+        check(_LIBRARY.jk_softsign_backward(s.data_ptr(), g.data_ptr(), out.data_ptr(), s.numel(),
+                                            _dtype_code("scores", s), _stream(s.device)), "jk_softsign_backward")
+    return out
+
+
+def _dense_from_topk(w: Tensor, index: Tensor, n_cols: int) -> Tensor:
+    """[..., rows, k] weights at int64 columns -> dense f32 [..., rows, n_cols] (jk_topk_to_dense)."""
+    w = w.float().contiguous()
+    index = index.contiguous()
+    dense = torch.zeros(w.shape[:-1] + (n_cols,), device=w.device, dtype=torch.float32)
+    with torch.cuda.device(w.device):
+        check(_LIBRARY.jk_topk_to_dense(w.data_ptr(), index.data_ptr(), dense.data_ptr(), w.numel() // w.shape[-1],
+                                        w.shape[-1], n_cols, _stream(w.device)), "jk_topk_to_dense")
+    return dense
+
+
+@_entry
+def query_topk_reduce_backward_cuda(edges, indices, projected_state, projected_val, grad_delta_state, grad_delta_val):
+    """Backward of the top-k reduce out[b, q] = sum_e edges[b, q, e] x[b, indices[b, q, e]]
+    (jakal_net_native.cpp:152-166 contract). Returns (grad_edges [B, Q, k],
+    grad_projected_state [B, S], grad_projected_val [B, S, D]) in the dtype of
+    projected_state. The edge gradients are gathered by jk_topk_reduce_backward_edges; the
+    source gradients are GEMMs of the dense edge matrix (fixed summation order)."""
+    e = _cuda_contig("edges", edges)
+    idx = _cuda_contig("indices", indices).long()
+    dt = projected_state.dtype
+    st = _cuda_contig("projected_state", projected_state)
+    B, S = st.reshape(-1, st.shape[-1]).shape
+    Q, k = e.shape[-2], e.shape[-1]
+    st = st.reshape(B, S)
+    vv = _cuda_contig("projected_val", projected_val).to(dt).reshape(B, S, -1)
+    D = vv.shape[-1]
+    gs = _cuda_contig("grad_delta_state", grad_delta_state).to(dt).reshape(B, Q)
+    gv = _cuda_contig("grad_delta_val", grad_delta_val).to(dt).reshape(B, Q, D)
+    idx = idx.reshape(B, Q, k)
+    grad_edges = torch.empty((B, Q, k), device=e.device, dtype=dt)
+    with torch.cuda.device(e.device):
+        check(_LIBRARY.jk_topk_reduce_backward_edges(idx.data_ptr(), st.data_ptr(), vv.data_ptr(), gs.data_ptr(),
+                                                     gv.data_ptr(), grad_edges.data_ptr(), B, Q, S, k, D,
+                                                     _dtype_code("state", st), _dtype_code("out", grad_edges),
+                                                     _stream(e.device)), "jk_topk_reduce_backward_edges")
+    dense_t = _dense_from_topk(e.reshape(B, Q, k), idx, S).transpose(1, 2)  # [B, S, Q]
+    with _exact_f32_matmul():
+        g_state = torch.bmm(dense_t, gs.float().unsqueeze(-1)).squeeze(-1)
+        g_val = torch.bmm(dense_t, gv.float())
+    return (grad_edges.reshape(e.shape), g_state.to(dt).reshape(projected_state.shape),
+            g_val.to(dt).reshape(projected_val.shape))
+
+
+@_entry
+def low_rank_pairwise_topk_backward_cuda(src_val, dst_val, target_weight, source_weight, core_weight,
+                                         projected_source, projected_target, indices, grad_scores, temperature):
+    """Gradient of the low-rank route logits of a per-source top-k transition (the positional
+    contract native_backend.py:4559-4570 calls): logits[b, s, e] = (ps[b, s] * core / T) .
+    pt[b, indices[b, s, e]] + bias with ps = src_val . W_s^T, pt = dst_val . W_t^T.
+    Returns (grad_src_val, grad_dst_val, grad_W_t, grad_W_s, grad_core, grad_bias).
+    The sparse grad_scores become a dense [B, S, D] matrix (jk_topk_to_dense), so every
+    contraction is a GEMM with f32 accumulation and a fixed summation order."""
+    T = float(temperature)
+    src = _cuda_contig("src_val", src_val).float()
+    dst = _cuda_contig("dst_val", dst_val).float()
+    ps = _cuda_contig("projected_source", projected_source).float()
+    pt = _cuda_contig("projected_target", projected_target).float()
+    c = core_weight.detach().float().reshape(-1)
+    w_t = target_weight.detach().float()
+    w_s = source_weight.detach().float()
+    G = _cuda_contig("grad_scores", grad_scores).float()
+    B, S, _ = ps.shape
+    Dn = pt.shape[1]
+    dense = _dense_from_topk(G, _cuda_contig("indices", indices).long(), Dn)  # [B, S, Dn]
+    with _exact_f32_matmul():
+        g_wps = torch.bmm(dense, pt)                          # d logits / d (ps * c / T)
+        g_pt = torch.bmm(dense.transpose(1, 2), ps * (c / T))  # [B, Dn, R]
+        g_ps = g_wps * (c / T)
+        g_core = (g_wps * ps).sum(dim=(0, 1)) / T
+        grad_src = torch.matmul(g_ps, w_s)
+        grad_dst = torch.matmul(g_pt, w_t)
+        grad_ws = g_ps.reshape(-1, g_ps.shape[-1]).t() @ src.reshape(-1, src.shape[-1])
+        grad_wt = g_pt.reshape(-1, g_pt.shape[-1]).t() @ dst.reshape(-1, dst.shape[-1])
+    grad_bias = G.sum()
+    return (grad_src.to(src_val.dtype), grad_dst.to(dst_val.dtype), grad_wt.to(target_weight.dtype),
+            grad_ws.to(source_weight.dtype), g_core.to(core_weight.dtype).reshape(core_weight.shape),
+            grad_bias.to(core_weight.dtype))

@@ -104,6 +104,21 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _p, _i32, _i64, _f32, _p, _i32,        # src_sender, state_dtype, k, score_bias, bias_dev, compress
          _p, _p],                               # routes, stream
     ),
+    "jk_softmax_backward": (_i32, [_p, _p, _p, _i64, _i64, _i32, _p]),
+    "jk_softsign_backward": (_i32, [_p, _p, _p, _i64, _i32, _p]),
+    "jk_topk_reduce_backward_edges": (
+        _i32,
+        [_p, _p, _p, _p, _p, _p,                # indices, state, val, grad_state, grad_val, grad_edges
+         _i64, _i64, _i64, _i64, _i64,          # B, n_rows, n_src, k, dim
+         _i32, _i32, _p],                       # dtype, out_dtype, stream
+    ),
+    "jk_topk_to_dense": (_i32, [_p, _p, _p, _i64, _i64, _i64, _p]),
+    "jk_debug_window_stalled_producer": (
+        _i32,
+        [_p, _p, _i64, _i64, _i64, _i64, _i32,  # row_proj, col_proj, B, n_rows, n_cols, rp, proj_dtype
+         _p, _i32, _p, _i64, _i64,              # col_state, state_dtype, col_val, dim, window
+         _p, _p, _i32, _p],                     # out_state, out_val, out_dtype, stream
+    ),
     "jk_select_aggregate_forward": (
         _i32,
         [_p, _i64, _i64, _i64, _i64, _i64,      # scores, B, n_rows, n_cols, row_begin, row_count

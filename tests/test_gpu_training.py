@@ -1,0 +1,132 @@
+"""Training through this backend: the per-source sparse transition's autograd route.
+
+With the module advertising low_rank_pairwise_topk_{forward,backward}_cuda and the reduce /
+compressor backwards, the reference's SparseTransition trains through
+_LowRankTransitionPairwiseTopK (native_backend.py:4408-4601, dispatch :5962-5975) on this
+module's kernels. The gradients of the layers' values and states and of every route
+parameter are compared with the reference implementation's own torch autograd
+(implementation="reference") on identical seeded f32 inputs; the module entry points are
+wrapped with mock.patch.object(..., wraps=...) to prove they ran. The row-wise backward
+kernels are also checked one by one against torch.autograd.
+
+The reference's autograd route adds the route bias after the temperature division
+(native_backend.py:4459) while its torch path divides the bias too (TemperatureScaledRoute);
+the comparisons therefore use temperature 1, where the two agree."""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+from unittest import mock
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT / "baseline"))
+import reference_shim  # noqa: E402  (baseline/reference_shim.py)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return torch.device("cuda", 0)
+
+
+def test_softmax_and_softsign_backward_match_autograd(dev):
+    import jakal_net_b200 as jk
+
+    g = torch.Generator(device="cuda").manual_seed(1)
+    for dtype, tol in ((torch.float32, 1e-6), (torch.bfloat16, 2e-2)):
+        s = torch.randn(37, 53, device="cuda", generator=g).to(dtype).requires_grad_(True)
+        gr = torch.randn(37, 53, device="cuda", generator=g).to(dtype)
+        r = torch.softmax(s.float(), -1)
+        (want,) = torch.autograd.grad(r, s, gr.float())
+        got = jk.softmax_backward_cuda(r.detach().to(dtype), gr)
+        assert got.dtype == dtype
+        torch.testing.assert_close(got.float(), want.float(), atol=tol, rtol=tol)
+        e = torch.nn.functional.softsign(s.float())
+        (want,) = torch.autograd.grad(e, s, gr.float())
+        got = jk.softsign_backward_cuda(s.detach(), gr)
+        torch.testing.assert_close(got.float(), want.float(), atol=tol, rtol=tol)
+
+
+def test_query_topk_reduce_backward_matches_autograd(dev):
+    import jakal_net_b200 as jk
+
+    g = torch.Generator(device="cuda").manual_seed(2)
+    B, Q, S, k, D = 3, 40, 300, 12, 48
+    edges = torch.randn(B, Q, k, device="cuda", generator=g, requires_grad=True)
+    idx = torch.stack([torch.randperm(S, device="cuda", generator=g)[:k] for _ in range(B * Q)]).reshape(B, Q, k)
+    state = torch.randn(B, S, device="cuda", generator=g, requires_grad=True)
+    val = torch.randn(B, S, D, device="cuda", generator=g, requires_grad=True)
+    out_s = (edges * torch.gather(state[:, None, :].expand(B, Q, S), -1, idx)).sum(-1)
+    gathered = torch.gather(val[:, None].expand(B, Q, S, D), 2, idx[..., None].expand(B, Q, k, D))
+    out_v = (edges[..., None] * gathered).sum(-2)
+    gs = torch.randn(B, Q, device="cuda", generator=g)
+    gv = torch.randn(B, Q, D, device="cuda", generator=g)
+    want = torch.autograd.grad((out_s, out_v), (edges, state, val), (gs, gv))
+    got = jk.query_topk_reduce_backward_cuda(edges.detach(), idx, state.detach(), val.detach(), gs, gv)
+    for a, b in zip(got, want):
+        torch.testing.assert_close(a, b, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.skipif(not reference_shim.available(), reason="reference not staged (python baseline/stage_reference.py)")
+@pytest.mark.parametrize("compress", ["softmax", "signed_abs_softmax"])
+@pytest.mark.parametrize("shape", [(7, 6, 4, 3, 2), (400, 150, 32, 16, 24)])
+def test_sparse_transition_training_matches_reference(dev, compress, shape):
+    os.environ["JAKAL_NET_NATIVE_MODULE"] = "jakal_net_b200"
+    jn = reference_shim.import_reference()
+    import jakal_net.native_backend as nb
+
+    status = jn.native_status(force_reload=True)
+    assert status.available and status.backend_name == "b200_sm100a"
+    module = nb._native_module()
+    n_src, n_dst, D, R, k = shape
+    g = torch.Generator(device="cuda").manual_seed(n_src + k)
+    base = dict(src_val=torch.randn(2, n_src, D, device="cuda", generator=g),
+                src_state=torch.randn(2, n_src, device="cuda", generator=g),
+                dst_val=torch.randn(2, n_dst, D, device="cuda", generator=g),
+                dst_state=torch.randn(2, n_dst, device="cuda", generator=g))
+    torch.manual_seed(7)
+    route = jn.LowRankBilinearRoute(src_dim=D, dst_dim=D, rank=R).cuda()
+    with torch.no_grad():
+        route.weight.copy_(torch.rand(R, device="cuda", generator=g) + 0.5)
+    weights = (torch.randn(2, n_dst, device="cuda", generator=g), torch.randn(2, n_dst, D, device="cuda", generator=g))
+
+    def run(impl):
+        rf = jn.LowRankBilinearRoute(src_dim=D, dst_dim=D, rank=R).cuda()
+        rf.load_state_dict(route.state_dict())
+        t = {n: v.clone().requires_grad_(True) for n, v in base.items()}
+        src = jn.Layer(dim=D, num_nodes=n_src, state=t["src_state"], val=t["src_val"])
+        dst = jn.Layer(dim=D, num_nodes=n_dst, state=t["dst_state"], val=t["dst_val"])
+        op = jn.SparseTransition(route_fn=rf, topk=k, route_compress_name=compress, implementation=impl)
+        delta = op.compute_delta(src, dst)
+        loss = (delta.delta_state * weights[0]).sum() + (delta.delta_val * weights[1]).sum()
+        loss.backward()
+        grads = {n: v.grad for n, v in t.items()}
+        grads.update({f"route.{n}": p.grad for n, p in rf.named_parameters()})
+        return delta, grads
+
+    want_delta, want = run("reference")
+    with mock.patch.object(module, "low_rank_pairwise_topk_forward_cuda",
+                           wraps=module.low_rank_pairwise_topk_forward_cuda) as fwd, \
+            mock.patch.object(module, "low_rank_pairwise_topk_backward_cuda",
+                              wraps=module.low_rank_pairwise_topk_backward_cuda) as bwd:
+        got_delta, got = run("native")
+    assert fwd.call_count > 0 and bwd.call_count > 0
+    torch.testing.assert_close(got_delta.delta_state, want_delta.delta_state, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(got_delta.delta_val, want_delta.delta_val, atol=1e-4, rtol=1e-4)
+    for name, w in want.items():
+        gv = got[name]
+        if w is None:
+            assert gv is None or torch.count_nonzero(gv) == 0, name
+            continue
+        assert gv is not None, name
+        scale = w.abs().max().clamp_min(1e-6)
+        err = ((gv - w).abs().max() / scale).item()
+        assert err < 1e-4, f"{name}: relative error {err:.2e}"
+    jn.native_status(force_reload=True)
