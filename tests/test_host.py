@@ -62,8 +62,14 @@ def test_native_module_contract():
     assert jk.supported_devices() == ["cuda"]
     ops = jk.supported_ops()
     assert "propagation_topk" in ops and "transition_query_topk" in ops and "transition_pairwise_topk" in ops
-    # forward-only: the autograd entry points must not be advertised (native_backend.py:659-667)
-    assert not any(op.endswith("_backward_cuda") for op in ops)
+    # every advertised op is a callable of the module (the loader calls them by name)
+    assert all(callable(getattr(jk, op, None)) for op in ops)
+    # the training entry points advertised are exactly the per-source transition's autograd
+    # route (native_backend.py:659-667, 5962-5975); the env-gated propagation routes need
+    # low_rank_propagation_*_forward_cuda, which must stay unadvertised
+    assert {"low_rank_pairwise_topk_forward_cuda", "low_rank_pairwise_topk_backward_cuda",
+            "query_topk_reduce_backward_cuda", "softsign_backward_cuda", "softmax_backward_cuda"} <= set(ops)
+    assert not any(op.startswith("low_rank_propagation_") for op in ops)
 
 
 def test_cpu_tensors_raise_instead_of_falling_back():
