@@ -605,7 +605,8 @@ C4_METRIC = "Progressive-B fwd tokens/s"
 C4_WORKLOAD = ("config4: ProgressiveBExampleLM.forward_query_block, B32 prefix 1024 dim 512 vocab 16384, 6 joint "
                "blocks (expanded 256 / compressed 64), s_window 512, top-k 32, rank 64, 128 query slots, bf16 autocast")
 C4_OPS = ("propagation_window", "propagation_topk", "transition_pairwise_topk", "propagation_dense",
-          "transition_pairwise_dense", "propagation_query_dense", "transition_query_topk")
+          "transition_pairwise_dense", "propagation_query_dense", "transition_query_topk",
+          "low_rank_pairwise_topk_forward_cuda")
 
 
 def _progressive_b(pb, implementation, batch_hint=None):
@@ -656,6 +657,82 @@ def cpu_progressive_b(seconds: float = 15.0, batch: int = 2):
     return batch * C4["P"] / med, sample, threads
 
 
+def _time_wrapped(obj, names, fn, device):
+    """Runs fn once with obj.<name> (every name) bracketed by CUDA events; returns
+    ({name: device ms}, {name: calls}, total device ms of fn)."""
+    per = {}
+    saved = {n: getattr(obj, n) for n in names if hasattr(obj, n)}
+
+    def wrap(name, f):
+        def timed(*a, **kw):
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            out = f(*a, **kw)
+            s1.record()
+            per.setdefault(name, []).append((s0, s1))
+            return out
+        return timed
+
+    for n, f in saved.items():
+        setattr(obj, n, wrap(n, f))
+    try:
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        fn()
+        f1.record()
+        torch.cuda.synchronize(device)
+    finally:
+        for n, f in saved.items():
+            setattr(obj, n, f)
+    ms = {n: sum(a.elapsed_time(z) for a, z in evs) for n, evs in per.items()}
+    return ms, {n: len(evs) for n, evs in per.items()}, f0.elapsed_time(f1)
+
+
+def _operator_classes(jn, pb):
+    """(class, method) pairs whose device time the config-4 breakdown reports: the
+    reference's operator classes and Progressive-B's query propagation."""
+    return [(jn.SparsePropagation, "compute_delta"), (jn.Propagation, "compute_delta"),
+            (jn.SparseTransition, "compute_delta"), (jn.Transition, "compute_delta"),
+            (pb.ProgressiveBExampleLM, "apply_query_propagation")]
+
+
+def _time_wrapped_methods(targets, fn, device):
+    """_time_wrapped over class methods (outermost calls only: a method called from inside
+    another timed method is not counted twice)."""
+    per, depth = {}, [0]
+    saved = [(cls, name, cls.__dict__[name]) for cls, name in targets if name in cls.__dict__]
+
+    def wrap(label, f):
+        def timed(*a, **kw):
+            if depth[0]:
+                return f(*a, **kw)
+            depth[0] += 1
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            try:
+                out = f(*a, **kw)
+            finally:
+                depth[0] -= 1
+            s1.record()
+            per.setdefault(label, []).append((s0, s1))
+            return out
+        return timed
+
+    for cls, name, f in saved:
+        setattr(cls, name, wrap(f"{cls.__name__}.{name}", f))
+    try:
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        fn()
+        f1.record()
+        torch.cuda.synchronize(device)
+    finally:
+        for cls, name, f in saved:
+            setattr(cls, name, f)
+    ms = {n: sum(a.elapsed_time(z) for a, z in evs) for n, evs in per.items()}
+    return ms, {n: len(evs) for n, evs in per.items()}, f0.elapsed_time(f1)
+
+
 def run_config4(args, rank, world, device):
     jn, pb = _import_reference_model()
     if pb is None:
@@ -692,33 +769,11 @@ def run_config4(args, rank, world, device):
     ms = e0.elapsed_time(e1) / steps
 
     # per-op device time: every backend op the model calls, bracketed by CUDA events
-    per_op, calls, launches = {}, {}, {}
-    originals = {n: getattr(jk, n) for n in C4_OPS}
-
-    def wrap(name, fn):
-        def timed_op(*a, **kw):
-            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s0.record()
-            out = fn(*a, **kw)
-            s1.record()
-            per_op.setdefault(name, []).append((s0, s1))
-            return out
-        return timed_op
-
-    for n, f in originals.items():
-        setattr(jk, n, wrap(n, f))
-    try:
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record()
-        forward(ids)
-        f1.record()
-        torch.cuda.synchronize(device)
-    finally:
-        for n, f in originals.items():
-            setattr(jk, n, f)
-    fwd_ms = f0.elapsed_time(f1)
-    op_ms = {n: sum(a.elapsed_time(z) for a, z in evs) for n, evs in per_op.items()}
-    calls = {n: len(evs) for n, evs in per_op.items()}
+    op_ms, calls, fwd_ms = _time_wrapped(jk, C4_OPS, lambda: forward(ids), device)
+    # per-operator-class device time of the whole model step (the reference's Layer API
+    # classes and the query propagation), for this backend and for the reference's torch path
+    cls_targets = _operator_classes(jn, pb)
+    cls_ms, cls_calls, _ = _time_wrapped_methods(cls_targets, lambda: forward(ids), device)
 
     # end to end: token ids from pinned host memory in, logits back to pinned host memory
     h_logits = torch.empty((b, C4["TARGET"], C4["VOCAB"]), dtype=torch.bfloat16).pin_memory()
@@ -743,16 +798,21 @@ def run_config4(args, rank, world, device):
     if not args.no_reference_gpu:
         ref_model = _progressive_b(pb, "reference").to(device)
         ref_model.load_state_dict(model.state_dict())
-        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
-            ref_model.forward_query_block(ids, target_len=C4["TARGET"])
-            torch.cuda.synchronize(device)
-            r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            r0.record()
-            for _ in range(3):
-                ref_model.forward_query_block(ids, target_len=C4["TARGET"])
-            r1.record()
-            torch.cuda.synchronize(device)
+
+        def ref_forward():
+            with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+                return ref_model.forward_query_block(ids, target_len=C4["TARGET"])
+
+        ref_forward()
+        torch.cuda.synchronize(device)
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
+        for _ in range(3):
+            ref_forward()
+        r1.record()
+        torch.cuda.synchronize(device)
         ref_ms = r0.elapsed_time(r1) / 3
+        ref_cls_ms, ref_cls_calls, _ = _time_wrapped_methods(cls_targets, ref_forward, device)
         del ref_model
 
     def max_over_ranks(x):
@@ -778,13 +838,15 @@ def run_config4(args, rank, world, device):
                    "parallelism": f"batch-sharded x{world}, no collective on the data path"},
         "clocks": clk.summary(),
         "per_op": {"forward_ms": fwd_ms, "ops_ms": op_ms, "calls": calls,
-                   "ops_share": {n: v / fwd_ms for n, v in op_ms.items()}},
+                   "ops_share": {n: v / fwd_ms for n, v in op_ms.items()},
+                   "operator_classes_ms": cls_ms, "operator_classes_calls": cls_calls},
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h_ids.numel() * 8, "d2h_bytes_per_step": h_logits.numel() * 2},
     }
     if ref_ms is not None:
         line["reference_torch_gpu"] = {"value": tokens / (ref_ms * 1e-3), "unit": "tokens/s", "ms_per_step": ref_ms,
-                                       "what": "the same model with implementation=reference on this GPU"}
+                                       "what": "the same model with implementation=reference on this GPU",
+                                       "operator_classes_ms": ref_cls_ms}
     if world == 1 and not args.no_cpu_baseline:
         v, sample, threads = cpu_progressive_b()
         line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference",

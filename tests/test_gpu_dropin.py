@@ -181,9 +181,13 @@ def test_sparse_transition_pairwise_routes(jn, module, route, k):
     rf = make_route().cuda()
     ref, nat = _pair(lambda **kw: jn.SparseTransition(route_fn=rf, topk=k, state_activation_fn=lambda x: x + 1.25,
                                                       val_proj_fn=_val_proj, state_proj_fn=_state_proj, **kw))
-    with mock.patch.object(module, "transition_pairwise_topk", wraps=module.transition_pairwise_topk) as w:
+    # low-rank routes with k <= 64 take the reference's autograd route
+    # (low_rank_pairwise_topk_forward_cuda, native_backend.py:5962-5993), the others the op
+    with mock.patch.object(module, "transition_pairwise_topk", wraps=module.transition_pairwise_topk) as w, \
+            mock.patch.object(module, "low_rank_pairwise_topk_forward_cuda",
+                              wraps=module.low_rank_pairwise_topk_forward_cuda) as w_lr:
         got = nat.compute_delta(src, dst)
-    assert w.call_count > 0
+    assert w.call_count + w_lr.call_count > 0
     _close(ref.compute_delta(src, dst), got, atol=1e-5 if k < 6 else 1e-4, rtol=1e-5 if k < 6 else 1e-4)
 
 
@@ -241,7 +245,8 @@ def _progressive_b(pb, implementation, prefix, dim, vocab, hidden, topk, window,
 
 def _count_calls(module, fn):
     names = ("propagation_window", "propagation_topk", "transition_pairwise_topk", "propagation_dense",
-             "transition_pairwise_dense", "propagation_query_dense", "transition_query_topk")
+             "transition_pairwise_dense", "propagation_query_dense", "transition_query_topk",
+             "low_rank_pairwise_topk_forward_cuda")
     with contextlib.ExitStack() as stack:
         mocks = {n: stack.enter_context(mock.patch.object(module, n, wraps=getattr(module, n))) for n in names}
         out = fn()
@@ -262,7 +267,7 @@ def test_progressive_b_query_block_f32(jn, module):
     with torch.no_grad():
         want = ref.forward_query_block(ids, target_len=16)
         got, calls = _count_calls(module, lambda: nat.forward_query_block(ids, target_len=16))
-    for op in ("propagation_window", "propagation_topk", "transition_pairwise_topk"):
+    for op in ("propagation_window", "propagation_topk", "low_rank_pairwise_topk_forward_cuda"):
         assert calls.get(op, 0) > 0, calls
     rel = ((got - want).norm() / want.norm()).item()
     assert rel < 1e-4, rel
@@ -282,7 +287,7 @@ def test_progressive_b_query_block_bf16_autocast(jn, module):
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         want = ref.forward_query_block(ids, target_len=32).float()
         got, calls = _count_calls(module, lambda: nat.forward_query_block(ids, target_len=32).float())
-    assert calls.get("propagation_window", 0) > 0 and calls.get("transition_pairwise_topk", 0) > 0, calls
+    assert calls.get("propagation_window", 0) > 0 and calls.get("low_rank_pairwise_topk_forward_cuda", 0) > 0, calls
     assert torch.isfinite(got).all()
     rel = ((got - want).norm() / want.norm()).item()
     print(f"bf16 autocast logits: relative L2 difference native vs reference {rel:.3e}; calls {calls}")

@@ -126,6 +126,11 @@ def test_sparse_transition_training_matches_reference(dev, compress, shape):
             assert gv is None or torch.count_nonzero(gv) == 0, name
             continue
         assert gv is not None, name
+        if name == "route.bias":
+            # a sum over every selected pair whose terms largely cancel (exactly, for softmax
+            # routes): compared in absolute terms
+            torch.testing.assert_close(gv, w, atol=1e-4, rtol=1e-4)
+            continue
         scale = w.abs().max().clamp_min(1e-6)
         err = ((gv - w).abs().max() / scale).item()
         assert err < 1e-4, f"{name}: relative error {err:.2e}"
