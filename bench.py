@@ -48,7 +48,12 @@ KERNELS_PER_CALL = {
     "jk_lowrank_project": 1, "jk_lowrank_project_pair": 1, "jk_propagation_topk_forward": 1,
     "jk_propagation_topk_forward_mh": 1, "jk_propagation_topk_rows_forward": 1,
     "jk_propagation_window_forward": 1, "jk_propagation_window_forward_mh": 1, "jk_select_aggregate_forward": 1,
-    "jk_split3_bf16": 1, "jk_split2_bf16": 1,
+    "jk_split3_bf16": 1, "jk_split2_bf16": 1, "jk_transition_pairwise_topk_routes": 1,
+    "jk_transition_pairwise_topk_routes_mh": 1, "jk_transition_pairwise_topk_forward": 2,
+    "jk_transition_pairwise_topk_forward_mh": 2, "jk_transition_query_topk_forward": 1,
+    "jk_transition_query_topk_forward_mh": 1, "jk_transition_pairwise_dense_forward": 2,
+    "jk_transition_pairwise_dense_forward_mh": 2, "jk_softmax_backward": 1, "jk_softsign_backward": 1,
+    "jk_topk_reduce_backward_edges": 1, "jk_topk_to_dense": 1,
 }
 
 
@@ -864,6 +869,61 @@ def _cpu_model() -> str:
     return "unknown CPU"
 
 
+MICRO = {
+    # config 4's operator shapes (B32, dim 512, rank 64, bf16): the S window propagation,
+    # the expanded-B top-k propagation and the S -> query per-source transition
+    "window": dict(B=32, N=1024, D=512, R=64, W=512),
+    "topk": dict(B=32, N=256, D=512, R=64, K=32),
+    "transition": dict(B=32, S=1024, Q=128, D=512, R=64, K=32),
+}
+
+
+def run_micro(args, device):
+    """Times one reference-facing op of the module at a config-4 shape (device time per call,
+    CUDA events, inputs resident): the per-operator view of the Progressive-B forward."""
+    import jakal_net_b200 as jk
+
+    c = MICRO[args.micro]
+    g = torch.Generator().manual_seed(5)
+    to = dict(device=device, dtype=torch.bfloat16)
+    R, D = c["R"], c["D"]
+    w_s = (torch.randn(R, D, generator=g) / D ** 0.5).to(**to)
+    w_t = (torch.randn(R, D, generator=g) / D ** 0.5).to(**to)
+    core = torch.full((R,), R ** -0.5).to(**to)
+    if args.micro == "transition":
+        src = torch.randn(c["B"], c["S"], D, generator=g).to(**to)
+        dst = torch.randn(c["B"], c["Q"], D, generator=g).to(**to)
+        st = torch.randn(c["B"], c["S"], generator=g).to(**to)
+        snd = torch.nn.functional.softplus(st.float()).to(torch.bfloat16)
+
+        def op():
+            return jk.transition_pairwise_topk("low_rank_bilinear_route", w_s, None, w_t, None, core, None, None, None,
+                                               None, None, 1.0, snd, src, dst, st, src, c["K"], 128, 128)
+    else:
+        val = torch.randn(c["B"], c["N"], D, generator=g).to(**to)
+        st = torch.randn(c["B"], c["N"], generator=g).to(**to)
+        if args.micro == "window":
+            def op():
+                return jk.propagation_window("low_rank_bilinear", core, None, w_s, None, w_t, None, "softsign", val,
+                                             st, val, c["W"], 128, 128)
+        else:
+            def op():
+                return jk.propagation_topk("low_rank_bilinear", core, None, w_s, None, w_t, None, "softsign", val,
+                                           st, val, c["K"], 128, 128)
+    for _ in range(args.warmup):
+        op()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        op()
+    e1.record()
+    torch.cuda.synchronize(device)
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    print(json.dumps({"micro": args.micro, "shape": c, "us_per_call": us,
+                      "launches_per_call": count_launches(op)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -874,6 +934,7 @@ def main():
     ap.add_argument("--config", type=int, choices=[2, 4, 5], default=2)
     ap.add_argument("--no-reference-gpu", action="store_true")
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 row-sharded record of the default run")
+    ap.add_argument("--micro", choices=sorted(MICRO), help="time one module op at a config-4 shape instead")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -884,6 +945,9 @@ def main():
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.micro:
+        run_micro(args, device)
+        return
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=device)
     try:

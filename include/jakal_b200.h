@@ -296,6 +296,9 @@ int jk_transition_pairwise_topk_forward(const void* src_proj, const void* dst_pr
  *   out_state[b, d] = sum_s routes[b, s, d] * src_state[b, s],
  *   out_val[b, d, :] = sum_s routes[b, s, d] * src_val[b, s, :]
  * is then a plain GEMM (routes^T x values), with no atomics and a fixed summation order.
+ * Optional out_scores f32 / out_index int64 [B, n_src, k]: every source's selection (logit +
+ * bias, in descending order, -inf / -1 in empty slots) -- what the backward of the route
+ * scores needs (native_backend.py:4459-4491).
  * Same sizes and limits as jk_transition_pairwise_topk_forward (1 <= k <= 64, rp <= 128).
  * Replaces the scatter of low_rank_pairwise_topk_forward_cuda (jakal_net_native_cuda.cu:
  * 740-878, atomicAdd at :862-873) and of the blocked path jakal_net_native.cpp:6916-7087.
@@ -304,14 +307,16 @@ int jk_transition_pairwise_topk_routes(const void* src_proj, const void* dst_pro
                                        int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
                                        const void* src_sender, int state_dtype, int64_t k,
                                        float score_bias, const float* bias_dev, int compress,
-                                       float* routes, jk_stream_t stream);
+                                       float* routes, float* out_scores, int64_t* out_index,
+                                       jk_stream_t stream);
 
 /* Multi-head (jk_heads_t) variant of jk_transition_pairwise_topk_routes. */
 int jk_transition_pairwise_topk_routes_mh(const void* src_proj, const void* dst_proj, int64_t batch,
                                           int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
                                           const void* src_sender, int state_dtype, int64_t k,
                                           float score_bias, const float* bias_dev, int compress,
-                                          float* routes, const jk_heads_t* heads, jk_stream_t stream);
+                                          float* routes, float* out_scores, int64_t* out_index,
+                                          const jk_heads_t* heads, jk_stream_t stream);
 
 /*
  * Select-aggregate over materialised f32 score rows (any k, any score rank):

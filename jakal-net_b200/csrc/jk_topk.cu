@@ -1273,7 +1273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Softsign is elementwise: unless the ordered scores are requested, both threads of a
     // row share its entries (even / odd) and half 1 hands its state partial over in tau.
-    const bool split = p.compress == JK_SOFTSIGN && !(MODE == kGather && (p.out_scores || p.out_index));
+    const bool split = p.compress == JK_SOFTSIGN && !(p.out_scores || p.out_index);
     const Lane F{rv, ri};
     const int n_row = nsel[row];
     if (split) {
@@ -1302,7 +1302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!split) {
       const float bias = p.bias + (p.bias_dev ? __ldg(p.bias_dev) : 0.f);
       for (int e = 0; e < n; ++e) F.val(e) += bias;
-      if (MODE == kGather && row_ok && good && (p.out_scores || p.out_index)) {
+      if (row_ok && good && (p.out_scores || p.out_index)) {  // the selection, in score order
         const int64_t o = (b * p.n_rows + t) * k;
         // column slot e holds score rank ri[kCap / 2 + e]; outputs go in score order
         for (int e = 0; e < k; ++e) {
@@ -1680,7 +1680,8 @@ int gather_forward(const void* row_proj, const void* col_proj, int64_t batch, in
 
 int routes_forward(const void* src_proj, const void* dst_proj, int64_t batch, int64_t n_src, int64_t n_dst,
                    int64_t rp, int proj_dtype, const void* src_sender, int state_dtype, int64_t k, float score_bias,
-                   const float* bias_dev, int compress, float* routes, const jk_heads_t* heads, jk_stream_t stream) {
+                   const float* bias_dev, int compress, float* routes, float* out_scores, int64_t* out_index,
+                   const jk_heads_t* heads, jk_stream_t stream) {
   // the value / state arguments of the shared checks are not read in the routes form
   int st = validate_common(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, routes, JK_F32, routes, 1, JK_F32,
                            k, compress, JK_F32);
@@ -1710,6 +1711,8 @@ int routes_forward(const void* src_proj, const void* dst_proj, int64_t batch, in
   p.col_val = routes;
   p.col_sender = src_sender;
   p.routes = routes;
+  p.out_scores = out_scores;
+  p.out_index = out_index;
   p.heads = hd.heads;
   p.kph = hd.kph;
   p.combine = hd.combine;
@@ -1878,19 +1881,21 @@ extern "C" int jk_transition_pairwise_topk_routes(const void* src_proj, const vo
                                                   int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
                                                   const void* src_sender, int state_dtype, int64_t k,
                                                   float score_bias, const float* bias_dev, int compress,
-                                                  float* routes, jk_stream_t stream) {
+                                                  float* routes, float* out_scores, int64_t* out_index,
+                                                  jk_stream_t stream) {
   return jk::topk::routes_forward(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_sender, state_dtype, k,
-                                  score_bias, bias_dev, compress, routes, nullptr, stream);
+                                  score_bias, bias_dev, compress, routes, out_scores, out_index, nullptr, stream);
 }
 
 extern "C" int jk_transition_pairwise_topk_routes_mh(const void* src_proj, const void* dst_proj, int64_t batch,
                                                      int64_t n_src, int64_t n_dst, int64_t rp, int proj_dtype,
                                                      const void* src_sender, int state_dtype, int64_t k,
                                                      float score_bias, const float* bias_dev, int compress,
-                                                     float* routes, const jk_heads_t* heads, jk_stream_t stream) {
+                                                     float* routes, float* out_scores, int64_t* out_index,
+                                                     const jk_heads_t* heads, jk_stream_t stream) {
   if (heads == nullptr) return JK_ERR_BAD_ARG;
   return jk::topk::routes_forward(src_proj, dst_proj, batch, n_src, n_dst, rp, proj_dtype, src_sender, state_dtype, k,
-                                  score_bias, bias_dev, compress, routes, heads, stream);
+                                  score_bias, bias_dev, compress, routes, out_scores, out_index, heads, stream);
 }
 
 namespace jk {

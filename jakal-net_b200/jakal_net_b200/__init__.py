@@ -657,19 +657,27 @@ def _value_planes(pval: Tensor, proj_dtype: torch.dtype):
 
 def routes_aggregate(routes: Tensor, state: Tensor, val: Tensor) -> tuple[Tensor, Tensor]:
     """Aggregate of a dense route matrix: out_state[b, d] = sum_s routes[b, s, d] state[b, s],
-    out_val[b, d] = sum_s routes[b, s, d] val[b, s] (f32 results). 16-bit values take two
-    tensor-core GEMMs against the routes split into hi + lo planes of the values' dtype
-    (f32 accumulation and output, ~16-bit route weights); f32 values one f32 GEMM."""
+    out_val[b, d] = sum_s routes[b, s, d] val[b, s] (f32 results). Tensor-core GEMMs with f32
+    accumulation and output: the routes are split into hi + lo planes of the values' 16-bit
+    dtype (two GEMMs); f32 values are split into bf16 hi + lo planes too (three GEMMs, the
+    lo x lo product dropped: ~2^-16 relative)."""
     rt = routes.transpose(1, 2)
     with _exact_f32_matmul():
         out_state = torch.bmm(rt, state.float().unsqueeze(-1)).squeeze(-1)
-        if val.dtype in (torch.bfloat16, torch.float16):
-            hi = routes.to(val.dtype)
-            lo = (routes - hi.float()).to(val.dtype)
-            out_val = torch.bmm(hi.transpose(1, 2), val, out_dtype=torch.float32)
-            out_val += torch.bmm(lo.transpose(1, 2), val, out_dtype=torch.float32)
-        else:
-            out_val = torch.bmm(rt, val.float())
+    dt = val.dtype if val.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
+    r_hi = routes.to(dt)
+    r_lo = (routes - r_hi.float()).to(dt)
+    if val.dtype == dt:
+        out_val = torch.bmm(r_hi.transpose(1, 2), val, out_dtype=torch.float32)
+        out_val += torch.bmm(r_lo.transpose(1, 2), val, out_dtype=torch.float32)
+    else:
+        # f32 values: hi + lo planes on both sides, the three products above 2^-16
+        v = val.float()
+        v_hi = v.to(dt)
+        v_lo = (v - v_hi.float()).to(dt)
+        out_val = torch.bmm(r_hi.transpose(1, 2), v_hi, out_dtype=torch.float32)
+        out_val += torch.bmm(r_hi.transpose(1, 2), v_lo, out_dtype=torch.float32)
+        out_val += torch.bmm(r_lo.transpose(1, 2), v_hi, out_dtype=torch.float32)
     return out_state, out_val
 
 
@@ -813,7 +821,7 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
         routes = torch.zeros((B, sv.shape[1], n_dst), device=dev, dtype=torch.float32)
         args = (sc.row.data_ptr(), sc.col.data_ptr(), B, sv.shape[1], n_dst, sc.row.shape[-1],
                 _proj_dtype(sc.row, sc.split3), sender.data_ptr(), _dtype_code("sender", sender), k, 0.0,
-                _ptr(sc.bias), compress, routes.data_ptr())
+                _ptr(sc.bias), compress, routes.data_ptr(), None, None)
         with torch.cuda.device(dev):
             if sc.heads is None:
                 check(_LIBRARY.jk_transition_pairwise_topk_routes(*args, _stream(dev)),
@@ -990,8 +998,10 @@ def low_rank_pairwise_topk_forward_cuda(weighted_projected_source, projected_tar
     top-k destinations, routes = compress_kind (0 softmax, 1 signed_abs_softmax,
     2 signed_entmax15) over the k, and scatters routes * wstate / routes * wval.
     Returns (delta_state f32 [B, D], delta_val f32 [B, D, V], topk_scores f32 [B, S, k]
-    (score + bias), topk_indices int64 [B, S, k]); the selection is listed in ascending
-    destination order (the backward only needs the (score, index) pairs)."""
+    (score + bias), topk_indices int64 [B, S, k]). 16-bit projections (k <= 64, rank <= 128):
+    the fused kernel in routes form, selection in score order, aggregate as GEMMs; otherwise
+    the select-aggregate path, selection in destination order (the backward only needs the
+    (score, index) pairs)."""
     if weighted_projected_source.dim() != 3:
         raise TypeError("b200_sm100a low_rank_pairwise_topk_forward_cuda takes single-head [B, S, R] projections.")
     if int(compress_kind) not in _PAIRWISE_TOPK_COMPRESS:
@@ -1005,10 +1015,27 @@ def low_rank_pairwise_topk_forward_cuda(weighted_projected_source, projected_tar
     k = min(int(topk), pt.shape[1])
     if k <= 0:
         raise RuntimeError("topk must be positive.")
-    d_state, d_val, scores, index = select_aggregate(wps, pt, wstate, wval, k,
-                                                     compress=_PAIRWISE_TOPK_COMPRESS[int(compress_kind)],
-                                                     scatter=True, return_selection=True,
-                                                     score_bias=float(score_bias))
+    compress = _PAIRWISE_TOPK_COMPRESS[int(compress_kind)]
+    B, S, R = wps.shape
+    Dn = pt.shape[1]
+    if wps.dtype in (torch.bfloat16, torch.float16) and k <= _MAX_K and R <= 128 and B * S * Dn <= _SCORE_BUDGET:
+        # fused kernel in routes form (selection written out), aggregate as GEMMs
+        rp = int(_LIBRARY.jk_padded_rank(R))
+        if rp != R:
+            wps = torch.nn.functional.pad(wps, (0, rp - R))
+            pt = torch.nn.functional.pad(pt, (0, rp - R))
+        routes = torch.zeros((B, S, Dn), device=wps.device, dtype=torch.float32)
+        scores = torch.empty((B, S, k), device=wps.device, dtype=torch.float32)
+        index = torch.empty((B, S, k), device=wps.device, dtype=torch.int64)
+        with torch.cuda.device(wps.device):
+            check(_LIBRARY.jk_transition_pairwise_topk_routes(
+                wps.data_ptr(), pt.data_ptr(), B, S, Dn, rp, _DTYPE_CODE[wps.dtype], None, _lib.JK_F32, k,
+                float(score_bias), None, compress, routes.data_ptr(), scores.data_ptr(), index.data_ptr(),
+                _stream(wps.device)), "jk_transition_pairwise_topk_routes")
+        d_state, d_val = routes_aggregate(routes, wstate, wval)
+        return d_state, d_val, scores, index
+    d_state, d_val, scores, index = select_aggregate(wps, pt, wstate, wval, k, compress=compress, scatter=True,
+                                                     return_selection=True, score_bias=float(score_bias))
     return d_state, d_val, scores, index
 
 

@@ -102,7 +102,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_p, _p, _i64, _i64, _i64, _i64, _i32,  # src_proj, dst_proj, B, n_src, n_dst, rp, proj_dtype
          _p, _i32, _i64, _f32, _p, _i32,        # src_sender, state_dtype, k, score_bias, bias_dev, compress
-         _p, _p],                               # routes, stream
+         _p, _p, _p, _p],                       # routes, out_scores, out_index, stream
     ),
     "jk_softmax_backward": (_i32, [_p, _p, _p, _i64, _i64, _i32, _p]),
     "jk_softsign_backward": (_i32, [_p, _p, _p, _i64, _i32, _p]),

@@ -135,3 +135,30 @@ def test_sparse_transition_training_matches_reference(dev, compress, shape):
         err = ((gv - w).abs().max() / scale).item()
         assert err < 1e-4, f"{name}: relative error {err:.2e}"
     jn.native_status(force_reload=True)
+
+
+@pytest.mark.parametrize("compress_kind", [0, 1])
+def test_pairwise_topk_forward_cuda_fused_matches_select_path(dev, compress_kind):
+    """low_rank_pairwise_topk_forward_cuda on 16-bit projections runs the fused kernel in
+    routes form (selection written out, aggregate as GEMMs); f32 projections of the same
+    values run the select-aggregate path. Both must give the same selection (as sets, ties
+    aside) and the same sums; the returned scores are the logits plus the bias."""
+    import jakal_net_b200 as jk
+
+    g = torch.Generator(device="cuda").manual_seed(11)
+    B, S, Dn, R, D, k = 2, 700, 130, 40, 72, 16
+    wps = (torch.randn(B, S, R, device="cuda", generator=g) / R ** 0.5).to(torch.bfloat16)
+    pt = torch.randn(B, Dn, R, device="cuda", generator=g).to(torch.bfloat16)
+    wstate = torch.randn(B, S, device="cuda", generator=g)
+    wval = torch.randn(B, S, D, device="cuda", generator=g)
+    a = jk.low_rank_pairwise_topk_forward_cuda(wps, pt, wstate, wval, k, 0.25, compress_kind)
+    b = jk.low_rank_pairwise_topk_forward_cuda(wps.float(), pt.float(), wstate, wval, k, 0.25, compress_kind)
+    torch.testing.assert_close(a[0], b[0], atol=2e-4, rtol=2e-4)
+    torch.testing.assert_close(a[1], b[1], atol=2e-4, rtol=2e-4)
+    sa, ia = a[2], a[3]
+    sb, ib = b[2], b[3]
+    same = (ia.sort(-1).values == ib.sort(-1).values).all(-1)
+    assert same.float().mean() > 0.99
+    logits = torch.bmm(wps.float(), pt.float().transpose(1, 2)) + 0.25
+    torch.testing.assert_close(sa, torch.gather(logits, -1, ia), atol=1e-5, rtol=1e-5)
+    assert (sa[..., :-1] >= sa[..., 1:]).all()  # fused selection in descending score order
