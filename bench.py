@@ -875,6 +875,8 @@ MICRO = {
     "window": dict(B=32, N=1024, D=512, R=64, W=512),
     "topk": dict(B=32, N=256, D=512, R=64, K=32),
     "transition": dict(B=32, S=1024, Q=128, D=512, R=64, K=32),
+    # the same top-k propagation through the select-aggregate kernel (path comparison)
+    "topk_select": dict(B=32, N=256, D=512, R=64, K=32),
 }
 
 
@@ -906,6 +908,10 @@ def run_micro(args, device):
             def op():
                 return jk.propagation_window("low_rank_bilinear", core, None, w_s, None, w_t, None, "softsign", val,
                                              st, val, c["W"], 128, 128)
+        elif args.micro == "topk_select":
+            def op():
+                rp, cp = jk.lowrank_project_pair(val, w_t, w_s, core=core)
+                return jk.select_aggregate(rp, cp, st, val, c["K"])
         else:
             def op():
                 return jk.propagation_topk("low_rank_bilinear", core, None, w_s, None, w_t, None, "softsign", val,

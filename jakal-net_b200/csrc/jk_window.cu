@@ -41,6 +41,7 @@ constexpr int kSelWarps = 8;
 constexpr int kThreads = (kSelWarps + 1) * 32;
 constexpr int kMaxSlice = 192;   // value columns per CTA
 constexpr int kMaxEntIters = 48;  // cap on threshold iterations (converges in a few)
+constexpr int kStageCols = 1024;  // source states staged in shared memory when the CTA's columns fit
 
 enum PassType { kDone = 0, kStatsMax = 1, kStatsEnt = 2, kFinal = 3 };
 
@@ -96,7 +97,8 @@ struct Layout {
   static constexpr int kVStage = (kMaxSlice / 64) * kAtom;         // 3 boxes of 64 columns
   static constexpr int kV = kVStages * kVStage;
   static constexpr int kRowArrays = 16 * kRows * 4;
-  static constexpr int kTotal = 1024 + kA + kPs + kE + kV + kRowArrays + 512;
+  static constexpr int kStage = kStageCols * 4;  // the CTA's source states, f32
+  static constexpr int kTotal = 1024 + kA + kPs + kE + kV + kRowArrays + 512 + kStage;
 };
 
 __device__ __forceinline__ void sel_barrier() {
@@ -156,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* vote = abort_flag + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(vote) + 1);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(arr) + 16 * kRows * 4 + 64);
+  float* st_stage = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(arr) + 16 * kRows * 4 + 512);
   uint64_t* bar_a = bars;
   uint64_t* decide = bars + 1;
   uint64_t* eready = bars + 2;
@@ -346,6 +349,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     int g = 0;
     bool ok = true;
 
+    // The CTA's source states, staged once (f32, coalesced) when its columns fit: the final
+    // pass's state sum then reads shared memory instead of one global load per edge. The
+    // condition is the same in every thread of the CTA, so every edge warp reaches the barrier.
+    const int c_lo = static_cast<int>(j_lo * kCols);
+    int n_stage = 0;
+    if (ntiles > 0 && p.stats_out == nullptr) {
+      int64_t c_hi = (j_hi + 1) * kCols;
+      if (c_hi > p.n_cols) c_hi = p.n_cols;
+      const int64_t cnt = c_hi - c_lo;
+      if (cnt > 0 && cnt <= kStageCols) {
+        n_stage = static_cast<int>(cnt);
+        for (int i = threadIdx.x; i < n_stage; i += kSelWarps * 32)
+          st_stage[i] = ld_elem(p.col_state, cb + c_lo + i, p.state_dtype);
+        sel_barrier();
+      }
+    }
+
     const int nbuf = p.heads > 1 ? 1 : 2;
     auto load_tile = [&](float (&x)[64]) -> bool {
       const int buf = g % nbuf;
@@ -519,6 +539,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float w = edge_of(x[e], p.compress, __ldg(cs), __ldg(cs + 1), __ldg(cs + 2));
             ev[e] = static_cast<uint32_t>(col - lo_t) <= span ? w : 0.f;
           }
+        } else if (p.compress == JK_SOFTSIGN) {  // one loop per compressor: a tight hot loop
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const float w = x[e] / (1.f + fabsf(x[e]));
+            ev[e] = static_cast<uint32_t>(col0 + e - lo_t) <= span ? w : 0.f;
+          }
+        } else if (p.compress == JK_SIGNED_ABS_SOFTMAX) {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const float sg = x[e] > 0.f ? 1.f : (x[e] < 0.f ? -1.f : 0.f);
+            const float w = sg * expf(fabsf(x[e]) - mrow) * inv;
+            ev[e] = static_cast<uint32_t>(col0 + e - lo_t) <= span ? w : 0.f;
+          }
         } else {
 #pragma unroll
           for (int e = 0; e < 64; ++e) {
@@ -527,15 +560,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         // state: sum_s e * state[s] over this thread's visible columns
-        for (int e0 = 0; e0 < 64; e0 += 8) {
-          float sv[8];
+        if (n_stage > 0) {
+          const float* sv = st_stage + (col0 - c_lo);  // col0 - c_lo + 64 <= n_stage or masked
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int col = col0 + e0 + u;
-            sv[u] = (ev[e0 + u] != 0.f && col < p.n_cols) ? ld_elem(p.col_state, cb + col, p.state_dtype) : 0.f;
+          for (int e = 0; e < 64; ++e) {
+            const bool in = col0 + e - c_lo < n_stage;
+            state_acc = fmaf(ev[e], in ? sv[in ? e : 0] : 0.f, state_acc);
           }
+        } else {
+          for (int e0 = 0; e0 < 64; e0 += 8) {
+            float sv[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) state_acc = fmaf(ev[e0 + u], sv[u], state_acc);
+            for (int u = 0; u < 8; ++u) {
+              const int col = col0 + e0 + u;
+              sv[u] = (ev[e0 + u] != 0.f && col < p.n_cols) ? ld_elem(p.col_state, cb + col, p.state_dtype) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) state_acc = fmaf(ev[e0 + u], sv[u], state_acc);
+          }
         }
         if (it > 0 && !mbar_wait(efree, (it - 1) & 1)) { ok = false; break; }
 #pragma unroll
