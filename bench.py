@@ -206,10 +206,11 @@ def cpu_port_time(seconds: float = 10.0):
     return pairs / el / 1e9, sample, threads
 
 
-def _median_rate(run, work, seconds: float, min_reps: int = 3):
+def _median_rate(run, work, seconds: float, min_reps: int = 3, warmup: bool = True):
     """Times run() until `seconds` have passed and at least min_reps runs were made (after
-    an untimed warm-up run); returns (work / median run time, number of runs)."""
-    run()
+    an untimed warm-up run unless warmup is False); returns (work / median run time, runs)."""
+    if warmup:
+        run()
     times = []
     t_end = time.perf_counter() + seconds
     while time.perf_counter() < t_end or len(times) < min_reps:
@@ -280,6 +281,31 @@ def cpu_port_time(seconds: float = 10.0):
     sample = (f"median of {reps} runs of 1 of the 8 batch items (N=2048, window 512, k 32), blocked torch CPU "
               f"port; torch threads {torch.get_num_threads()}, {_cpu_model()}")
     return rate / 1e9, sample, threads
+
+
+def cpu_native_window(seconds: float = 3.0):
+    """The reference's C++ CPU extension (built from its sources by oracle/build_ref.py) on the
+    closest single reference op to config 2: propagation_window (window 512, no top-k, softsign,
+    f32) on one batch item, all host threads. Returns (Gpairs/s, runs) or None."""
+    from oracle import build_ref
+
+    if not build_ref.available("cpu"):
+        return None
+    native = build_ref.load_built("cpu")
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(SEED)
+    val = torch.randn(1, N, D, generator=g)
+    state = torch.randn(1, N, generator=g)
+    w_s = torch.randn(R, D, generator=g) / D ** 0.5
+    w_t = torch.randn(R, D, generator=g) / D ** 0.5
+    core = torch.full((R,), R ** -0.5)
+
+    def run():
+        native.propagation_window("low_rank_bilinear", core, None, w_s, None, w_t, None, "softsign", val, state, val,
+                                  WINDOW, 128, 128)
+
+    rate, reps = _median_rate(run, pairs_per_batch_item(N, WINDOW), seconds, min_reps=1, warmup=False)
+    return rate / 1e9, reps
 
 
 def cpu_baseline_config2(seconds: float = 10.0):
@@ -487,6 +513,12 @@ def run_b200(args, rank, world, device):
     if world == 1 and not args.no_cpu_baseline:
         v, sample, threads, kind = cpu_baseline_config2(10.0)
         line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample}
+        nat = cpu_native_window()
+        if nat is not None:
+            line["cpu_baseline"]["native_cpp_window512"] = {
+                "value": nat[0], "unit": UNIT, "runs": nat[1],
+                "what": "the reference's C++ CPU extension, propagation_window (window 512, no top-k), one batch "
+                        "item, median run (no warm-up: it takes seconds per run)"}
     print(json.dumps(line), flush=True)
 
 

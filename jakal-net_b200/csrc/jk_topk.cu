@@ -801,7 +801,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ntiles = j_hi >= j_lo ? static_cast<int>(j_hi - j_lo + 1) : 0;
   // Pass A is needed when some row can see more columns than its buffer holds.
   const int64_t max_visible = p.window >= 0 ? (p.window + 1 < p.n_cols ? p.window + 1 : p.n_cols) : p.n_cols;
-  const bool has_a = max_visible > kCap;
+  // Pass A (a threshold from the row statistics) runs when some row sees more columns than its
+  // buffer holds, and also when it sees at least twice the threshold's target count: the
+  // select step then ranks ~k + 3 sqrt(k) + 8 candidates instead of every visible column.
+  const float sel_target = fminf(static_cast<float>(k) + 3.f * sqrtf(static_cast<float>(k)) + 8.f, 0.75f * kCap);
+  const bool has_a = max_visible > kCap || static_cast<float>(max_visible) >= 2.f * sel_target;
   const int pre_passes = has_a ? 2 : 1;
 
   if (threadIdx.x == 0) {
@@ -1079,13 +1083,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       sel_barrier();
       if (half == 0) {
         float th = -INFINITY;
-        if (visible > kCap) {
+        if (visible > kCap || static_cast<float>(visible) >= 2.f * sel_target) {
           const float n = static_cast<float>(visible);
           const float mean = (s1[row] + s1[kRows + row]) / n;
           const float var = fmaxf((s2[row] + s2[kRows + row]) / n - mean * mean, 0.f);
           // Expected survivors: k plus ~3 standard deviations of the count, so that too few
           // is rare (the exact fallback pass covers it) and most rows fit a 64-key sort.
-          const float target = fminf(static_cast<float>(k) + 3.f * sqrtf(static_cast<float>(k)) + 8.f, 0.75f * kCap);
+          const float target = sel_target;
           const float z = 1.41421356f * erfinvf(1.f - 2.f * target / n);
           th = mean + z * sqrtf(var);
         }
