@@ -315,3 +315,42 @@ def test_config1_causal_dense_against_reference(jn, module, edge):
         got = nat.compute_delta(layer)
     assert w.call_count > 0
     _close(ref.compute_delta(layer), got, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("direction_only", [False, True])
+def test_hierarchical_memory_level_write_and_propagation(jn, module, direction_only):
+    """A causal-memory consumer (hierarchical_memory.py:35-136): one memory level's write
+    (SparseTransition, signed-abs routes, softplus senders) from a sequence layer into the
+    slots, then the slots' top-k propagation (signed-abs edges), native against reference,
+    with every module entry point the level reaches wrapped."""
+    from jakal_net.hierarchical_memory import _MemoryLevel
+
+    def level(impl):
+        torch.manual_seed(9)
+        return _MemoryLevel(dim=32, num_slots=48, pairwise_kind="low_rank_bilinear", route_kind="low_rank_bilinear",
+                            pairwise_rank=16, route_rank=16, pairwise_heads=1, route_heads=1,
+                            pairwise_frozen_heads=0, route_frozen_heads=0, pairwise_anchor_heads=0,
+                            route_anchor_heads=0, pairwise_anchor_kind="scaled_cosine",
+                            route_anchor_kind="fixed_projection", memory_topk=6, memory_train_mode="topk",
+                            memory_eval_mode="topk", eval_topk=None, implementation=impl,
+                            direction_only_values=direction_only).cuda().eval()
+
+    ref, nat = level("reference"), level("native")
+    nat.load_state_dict(ref.state_dict())
+    seq = _layer(jn, 200, 32, 90)
+    names = ("propagation_topk", "transition_pairwise_topk", "low_rank_pairwise_topk_forward_cuda")
+    with torch.no_grad():
+        want_mem = ref.initialize(batch_size=2, device="cuda", dtype=torch.float32)
+        want_w = ref.write.compute_delta(seq, want_mem)
+        got_mem = nat.initialize(batch_size=2, device="cuda", dtype=torch.float32)
+        with contextlib.ExitStack() as stack:
+            mocks = {n: stack.enter_context(mock.patch.object(module, n, wraps=getattr(module, n))) for n in names}
+            got_w = nat.write.compute_delta(seq, got_mem)
+            mem = jn.Layer(dim=32, num_nodes=48, state=want_mem.state + want_w.delta_state,
+                           val=want_mem.val + want_w.delta_val)
+            got_p = nat.compute_propagation_delta(mem)
+        want_p = ref.compute_propagation_delta(mem)
+    assert mocks["propagation_topk"].call_count > 0, {n: m.call_count for n, m in mocks.items()}
+    assert mocks["transition_pairwise_topk"].call_count + mocks["low_rank_pairwise_topk_forward_cuda"].call_count > 0
+    _close(want_w, got_w, atol=1e-4, rtol=1e-4)
+    _close(want_p, got_p, atol=1e-4, rtol=1e-4)
