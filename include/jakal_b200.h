@@ -376,9 +376,11 @@ int jk_topk_reduce_backward_edges(const int64_t* indices, const void* state, con
                                   int64_t batch, int64_t n_rows, int64_t n_src, int64_t k, int64_t dim,
                                   int dtype, int out_dtype, jk_stream_t stream);
 
-/* dense[r, indices[r, e]] = w[r, e] for rows x k selections (f32 w, int64 indices, -1
- * skipped); dense f32 [rows, n_cols] zeroed by the caller. Turns the scatters of the
- * backward into GEMMs with a fixed summation order. */
+/* dense[r, indices[r, e]] += w[r, e] for rows x k selections (f32 w, int64 indices, -1 and
+ * zero weights skipped); dense f32 [rows, n_cols] zeroed by the caller. A selection names
+ * each column once; padded window index lists may repeat a placeholder column with weight 0,
+ * which adds nothing. Turns the scatters of the backward into GEMMs with a fixed summation
+ * order. */
 int jk_topk_to_dense(const float* w, const int64_t* indices, float* dense, int64_t rows, int64_t k,
                      int64_t n_cols, jk_stream_t stream);
 

@@ -9,7 +9,7 @@
 //   * top-k reduce backward   g_e[q, e] = g_state[q] * state[idx] + g_val[q, :] . val[idx, :]
 //                             (the gather half of the reduce's backward; the scatter half
 //                             is a GEMM of the dense edge matrix, see jk_topk_to_dense)
-//   * top-k to dense          dense[r, idx[r, e]] = w[r, e]  (k non-zeros per row; the dense
+//   * top-k to dense          dense[r, idx[r, e]] += w[r, e]  (k non-zeros per row; the dense
 //                             matrix turns every scatter of the backward into a GEMM with a
 //                             fixed summation order)
 // One warp per row for the row-wise kernels; f32 accumulation throughout.
@@ -75,14 +75,17 @@ __global__ void topk_reduce_backward_kernel(const int64_t* indices, const void* 
   }
 }
 
-// dense[row, indices[row, e]] = w[row, e] for every e with indices >= 0 (dense zeroed by
-// the caller; the k columns of a row are distinct, so every entry is written once).
+// dense[row, indices[row, e]] += w[row, e] for every e with indices >= 0 (dense zeroed by
+// the caller). A selection names each column once, but a window's padded index lists repeat a
+// placeholder column with zero weight: adding keeps those entries exact (adding zero to the
+// one real weight changes nothing, whatever the order).
 __global__ void topk_to_dense_kernel(const float* w, const int64_t* indices, float* dense, int64_t rows, int64_t k,
                                      int64_t n_cols) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * k; i += stride) {
     const int64_t j = indices[i];
-    if (j >= 0 && j < n_cols) dense[(i / k) * n_cols + j] = w[i];
+    const float v = w[i];
+    if (j >= 0 && j < n_cols && v != 0.f) atomicAdd(dense + (i / k) * n_cols + j, v);
   }
 }
 

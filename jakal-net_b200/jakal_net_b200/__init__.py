@@ -99,15 +99,22 @@ _SUPPORTED_OPS = (
     "query_topk_reduce_backward_cuda",
     "softsign_backward_cuda",
     "softmax_backward_cuda",
+    # the propagation autograd routes (behind the reference's experimental-training switch,
+    # native_backend.py:5512-5565, 5600-5612)
+    "low_rank_propagation_topk_forward_cuda",
+    "low_rank_propagation_window_forward_cuda",
+    "low_rank_propagation_window_signed_abs_forward_cuda",
+    "low_rank_propagation_causal_dense_signed_abs_forward_cuda",
 )
 
 
 def supported_ops() -> list[str]:
     """Ops this module implements (jakal_net_native.cpp:5863-5912 contract), including the
-    CUDA entry points of the per-source sparse transition's autograd route
-    (native_backend.py:659-667, 4408-4601, 5962-5975). The propagation autograd routes stay
-    on the reference: they are behind its experimental-training switch and need entry
-    points this module does not export (low_rank_propagation_*_forward_cuda)."""
+    CUDA entry points of the autograd routes: the per-source sparse transition's
+    (native_backend.py:659-667, 4408-4601, 5962-5975) and the top-k / window propagation's
+    (:4815-4966, 5143-5357; the reference takes those only under its experimental-training
+    switch). The signed_entmax15 routes also need the reference's torch.ops.jakal_net
+    entmax ops, so they stay on the reference."""
     return list(_SUPPORTED_OPS)
 
 
@@ -1142,3 +1149,85 @@ def low_rank_pairwise_topk_backward_cuda(src_val, dst_val, target_weight, source
     return (grad_src.to(src_val.dtype), grad_dst.to(dst_val.dtype), grad_wt.to(target_weight.dtype),
             grad_ws.to(source_weight.dtype), g_core.to(core_weight.dtype).reshape(core_weight.shape),
             grad_bias.to(core_weight.dtype))
+
+
+def _projected_propagation(weighted_projected_source, projected_target, projected_state, projected_val, *,
+                           k: Optional[int], window: int, score_bias: float, compress: int):
+    """A propagation over given projections (the contract of the reference's
+    low_rank_propagation_*_forward_cuda entry points, jakal_net_native_cuda.cu:2545-3350):
+    score[b, t, s] = projected_target[b, t] . wps[b, s] + score_bias, causal window (or none),
+    top-k (k None: every visible source), edges, f32 aggregate of f32 state / values.
+    16-bit projections of rank <= 128 take the fused kernels; f32 projections the exact
+    select-aggregate path."""
+    wps = _cuda_contig("weighted_projected_source", weighted_projected_source)
+    pt = _cuda_contig("projected_target", projected_target).to(wps.dtype)
+    if wps.dim() != 3:
+        raise TypeError("b200_sm100a propagation entry points take single-head [B, N, R] projections.")
+    st = _cuda_contig("projected_state", projected_state).float()
+    vv = _cuda_contig("projected_val", projected_val).float()
+    B, N, R = wps.shape
+    sb = torch.full((1,), float(score_bias), device=wps.device, dtype=torch.float32)
+    n_k = N if k is None else min(int(k), N)
+    fused = wps.dtype in (torch.bfloat16, torch.float16) and R <= 128
+    if fused:
+        rp = int(_LIBRARY.jk_padded_rank(R))
+        if rp != R:
+            wps = torch.nn.functional.pad(wps, (0, rp - R))
+            pt = torch.nn.functional.pad(pt, (0, rp - R))
+        if k is not None and n_k <= _MAX_K:
+            return topk_aggregate(pt, wps, st, vv, n_k, window=window, compress=compress, bias=sb,
+                                  out_dtype=torch.float32)
+        if k is None:
+            pv, pv_lo, pad = _value_planes(vv, wps.dtype)
+            out_s, out_v = masked_aggregate(pt, wps, st, pv, window=window, compress=compress, bias=sb,
+                                            out_dtype=torch.float32, col_val_lo=pv_lo)
+            return out_s, (out_v[..., :vv.shape[-1]] if pad else out_v)
+    return select_aggregate(pt.float() if not fused else pt, wps.float() if not fused else wps, st, vv, n_k,
+                            window=window, compress=compress, bias=sb, out_dtype=torch.float32)
+
+
+_PROP_TOPK_COMPRESS = {0: _lib.JK_SOFTSIGN, 1: _lib.JK_SIGNED_ABS_SOFTMAX, 2: _lib.JK_SIGNED_ENTMAX15}
+
+
+@_entry
+def low_rank_propagation_topk_forward_cuda(weighted_projected_source, projected_target, projected_state,
+                                           projected_val, topk, score_bias, compress_kind):
+    """Top-k propagation over given projections (native_backend.py:4840-4857 contract,
+    jakal_net_native_cuda.cu:2545-2660): per target, the top-k sources over every source (no
+    mask), edges compress_kind (0 softsign, 1 signed_abs_softmax, 2 signed_entmax15),
+    f32 (delta_state [B, N], delta_val [B, N, D])."""
+    if int(compress_kind) not in _PROP_TOPK_COMPRESS:
+        raise RuntimeError(f"unsupported compress kind {compress_kind}")
+    return _projected_propagation(weighted_projected_source, projected_target, projected_state, projected_val,
+                                  k=int(topk), window=-1, score_bias=score_bias,
+                                  compress=_PROP_TOPK_COMPRESS[int(compress_kind)])
+
+
+@_entry
+def low_rank_propagation_window_forward_cuda(weighted_projected_source, projected_target, projected_state,
+                                             projected_val, window, score_bias):
+    """Causal-window softsign propagation over given projections (native_backend.py:5205-5212
+    contract, jakal_net_native_cuda.cu:2926): every source in [t - window, t]."""
+    return _projected_propagation(weighted_projected_source, projected_target, projected_state, projected_val,
+                                  k=None, window=int(window), score_bias=score_bias, compress=_lib.JK_SOFTSIGN)
+
+
+@_entry
+def low_rank_propagation_window_signed_abs_forward_cuda(weighted_projected_source, projected_target,
+                                                        projected_state, projected_val, window, score_bias):
+    """Causal-window signed_abs_softmax propagation over given projections
+    (native_backend.py:5195-5202 contract): edges normalised over each row's visible sources."""
+    return _projected_propagation(weighted_projected_source, projected_target, projected_state, projected_val,
+                                  k=None, window=int(window), score_bias=score_bias,
+                                  compress=_lib.JK_SIGNED_ABS_SOFTMAX)
+
+
+@_entry
+def low_rank_propagation_causal_dense_signed_abs_forward_cuda(weighted_projected_source, projected_target,
+                                                              projected_state, projected_val, score_bias):
+    """Causal-dense (window N - 1) signed_abs_softmax propagation over given projections
+    (native_backend.py:5187-5193 contract)."""
+    n = int(projected_target.shape[-2])
+    return _projected_propagation(weighted_projected_source, projected_target, projected_state, projected_val,
+                                  k=None, window=max(n - 1, 0), score_bias=score_bias,
+                                  compress=_lib.JK_SIGNED_ABS_SOFTMAX)

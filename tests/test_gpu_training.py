@@ -14,6 +14,7 @@ The reference's autograd route adds the route bias after the temperature divisio
 the comparisons therefore use temperature 1, where the two agree."""
 from __future__ import annotations
 
+import contextlib
 import os
 import sys
 from pathlib import Path
@@ -162,3 +163,78 @@ def test_pairwise_topk_forward_cuda_fused_matches_select_path(dev, compress_kind
     logits = torch.bmm(wps.float(), pt.float().transpose(1, 2)) + 0.25
     torch.testing.assert_close(sa, torch.gather(logits, -1, ia), atol=1e-5, rtol=1e-5)
     assert (sa[..., :-1] >= sa[..., 1:]).all()  # fused selection in descending score order
+
+
+@pytest.mark.skipif(not reference_shim.available(), reason="reference not staged (python baseline/stage_reference.py)")
+@pytest.mark.parametrize("case", ["topk_softsign", "topk_signed_abs", "window_softsign", "window_signed_abs",
+                                  "causal_dense_signed_abs"])
+def test_sparse_propagation_training_matches_reference(dev, case, monkeypatch):
+    """The propagation autograd routes (_LowRankPropagationTopK, _LowRankPropagationWindow,
+    native_backend.py:4815-4966, 5143-5357), which the reference takes under its
+    experimental-training switches, on this module's forward entry points and backward
+    kernels; gradients against the reference implementation's torch autograd. Those routes
+    pass the raw core weight where the module normalises it (native_backend.py:5549-5556,
+    5613-5621), so the test uses a unit-norm core weight, where the two agree."""
+    monkeypatch.setenv("JAKAL_NET_ENABLE_EXPERIMENTAL_FUSED_TRAINING", "1")
+    monkeypatch.setenv("JAKAL_NET_ENABLE_CAUSAL_DENSE_PROP_FORWARD_CUDA", "1")
+    monkeypatch.setenv("JAKAL_NET_NATIVE_MODULE", "jakal_net_b200")
+    jn = reference_shim.import_reference()
+    import jakal_net.native_backend as nb
+    from jakal_net.propagation import _compress_edges  # noqa: F401  (the reference's edges)
+
+    status = jn.native_status(force_reload=True)
+    assert status.available and status.backend_name == "b200_sm100a"
+    module = nb._native_module()
+    N, D, R = 160, 32, 16
+    g = torch.Generator(device="cuda").manual_seed(50)
+    base = dict(val=torch.randn(2, N, D, device="cuda", generator=g),
+                state=torch.randn(2, N, device="cuda", generator=g))
+    torch.manual_seed(8)
+    pw = jn.LowRankBilinearPairwise(dim=D, rank=R).cuda()
+    with torch.no_grad():
+        w = torch.rand(R, device="cuda", generator=g) + 0.5
+        pw.weight.copy_(w / w.norm())
+        pw.bias.fill_(0.1)
+
+    def signed_abs_softmax_edges(scores):
+        clean = torch.nan_to_num(scores)
+        return torch.sign(clean) * torch.softmax(clean.abs(), dim=-1)
+
+    kind, compress = case.split("_", 1) if not case.startswith("causal") else ("dense", "signed_abs")
+    edge = {} if compress == "softsign" else {"edge_compress_fn": signed_abs_softmax_edges}
+    sparse = dict(sparse_type="topk", topk=12) if kind == "topk" else \
+        dict(sparse_type="window", window=40 if kind == "window" else N - 1)
+    wg = (torch.randn(2, N, device="cuda", generator=g), torch.randn(2, N, D, device="cuda", generator=g))
+
+    def run(impl):
+        p = jn.LowRankBilinearPairwise(dim=D, rank=R).cuda()
+        p.load_state_dict(pw.state_dict())
+        t = {n: v.clone().requires_grad_(True) for n, v in base.items()}
+        layer = jn.Layer(dim=D, num_nodes=N, state=t["state"], val=t["val"])
+        op = jn.SparsePropagation(pairwise_fn=p, implementation=impl, **sparse, **edge)
+        delta = op.compute_delta(layer)
+        ((delta.delta_state * wg[0]).sum() + (delta.delta_val * wg[1]).sum()).backward()
+        grads = {n: v.grad for n, v in t.items()}
+        grads.update({f"pairwise.{n}": q.grad for n, q in p.named_parameters()})
+        return delta, grads
+
+    want_delta, want = run("reference")
+    names = ("low_rank_propagation_topk_forward_cuda", "low_rank_propagation_window_forward_cuda",
+             "low_rank_propagation_window_signed_abs_forward_cuda",
+             "low_rank_propagation_causal_dense_signed_abs_forward_cuda", "low_rank_pairwise_topk_backward_cuda")
+    with contextlib.ExitStack() as stack:
+        mocks = {n: stack.enter_context(mock.patch.object(module, n, wraps=getattr(module, n))) for n in names}
+        got_delta, got = run("native")
+    assert mocks["low_rank_pairwise_topk_backward_cuda"].call_count > 0
+    assert sum(m.call_count for n, m in mocks.items() if "forward" in n) > 0
+    torch.testing.assert_close(got_delta.delta_state, want_delta.delta_state, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(got_delta.delta_val, want_delta.delta_val, atol=1e-4, rtol=1e-4)
+    for name, w_ in want.items():
+        gv = got[name]
+        assert gv is not None and w_ is not None, name
+        if name == "pairwise.bias":
+            torch.testing.assert_close(gv, w_, atol=1e-4, rtol=1e-4)
+            continue
+        err = ((gv - w_).abs().max() / w_.abs().max().clamp_min(1e-6)).item()
+        assert err < 1e-4, f"{name}: relative error {err:.2e}"
+    jn.native_status(force_reload=True)

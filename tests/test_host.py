@@ -64,12 +64,12 @@ def test_native_module_contract():
     assert "propagation_topk" in ops and "transition_query_topk" in ops and "transition_pairwise_topk" in ops
     # every advertised op is a callable of the module (the loader calls them by name)
     assert all(callable(getattr(jk, op, None)) for op in ops)
-    # the training entry points advertised are exactly the per-source transition's autograd
-    # route (native_backend.py:659-667, 5962-5975); the env-gated propagation routes need
-    # low_rank_propagation_*_forward_cuda, which must stay unadvertised
+    # the training entry points of the autograd routes (native_backend.py:659-667, 5962-5975,
+    # 5512-5612); the entmax window route needs the reference's own torch ops and stays off
     assert {"low_rank_pairwise_topk_forward_cuda", "low_rank_pairwise_topk_backward_cuda",
-            "query_topk_reduce_backward_cuda", "softsign_backward_cuda", "softmax_backward_cuda"} <= set(ops)
-    assert not any(op.startswith("low_rank_propagation_") for op in ops)
+            "query_topk_reduce_backward_cuda", "softsign_backward_cuda", "softmax_backward_cuda",
+            "low_rank_propagation_topk_forward_cuda", "low_rank_propagation_window_forward_cuda"} <= set(ops)
+    assert "low_rank_propagation_window_entmax15_forward_cuda" not in ops
 
 
 def test_cpu_tensors_raise_instead_of_falling_back():
