@@ -3,8 +3,8 @@
 The reference checkout has neither setup.py nor pyproject.toml, so
 ``pip install --target baseline/_ref`` refuses it ("Directory ... is not installable").
 This recipe does what that install would do: it copies the importable package
-``src/jakal_net`` and the model script ``scripts/progressive_b_example.py`` unchanged into
-``baseline/_ref/``. The folder is git-ignored (never committed) but travels with the tree
+``src/jakal_net``, the model script ``scripts/progressive_b_example.py`` and the reference's
+native-backend test suite ``tests/test_native_backend.py`` unchanged into ``baseline/_ref/``. The folder is git-ignored (never committed) but travels with the tree
 to the GPU host, where the reference checkout itself does not exist.
 
 Only tests/ and bench.py's reference arm import what lands there (through
@@ -21,7 +21,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 DEST = HERE / "_ref"
 DEFAULT_SRC = Path("/root/reference")
-ITEMS = (("src/jakal_net", "jakal_net"), ("scripts/progressive_b_example.py", "progressive_b_example.py"))
+ITEMS = (("src/jakal_net", "jakal_net"), ("scripts/progressive_b_example.py", "progressive_b_example.py"),
+         ("tests/test_native_backend.py", "reference_tests/test_native_backend.py"))
 
 
 def stage(src: Path = DEFAULT_SRC, dest: Path = DEST) -> bool:
@@ -36,6 +37,7 @@ def stage(src: Path = DEFAULT_SRC, dest: Path = DEST) -> bool:
                 shutil.rmtree(d)
             shutil.copytree(s, d, ignore=shutil.ignore_patterns("__pycache__", "*.pyc"))
         else:
+            d.parent.mkdir(parents=True, exist_ok=True)
             shutil.copy2(s, d)
     return True
 

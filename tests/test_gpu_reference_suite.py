@@ -1,0 +1,63 @@
+"""The reference's own native-backend test suite, unchanged, against this module.
+
+tests/test_native_backend.py of the reference (staged into baseline/_ref/reference_tests by
+baseline/stage_reference.py) is run in a child process with
+JAKAL_NET_NATIVE_MODULE=jakal_net_b200. Its CUDA class exercises every native op through the
+Layer API, wraps the module ops with mock.patch.object(..., wraps=...) and compares with
+implementation="reference" at 1e-5. The cases on scorer / route kinds this backend does not
+implement (hadamard MLP pairwise and routes, MLP / linear routes and the full-bilinear route,
+which the reference's own module serves through transition_dense / transition_topk and the
+hadamard Functions) are expected to fail; every other case must pass."""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+SUITE = ROOT / "baseline" / "_ref" / "reference_tests" / "test_native_backend.py"
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not SUITE.exists(), reason="reference suite not staged")]
+
+# CUDA cases on kinds outside this backend (hadamard MLP, MLP / linear / full-bilinear routes)
+OUT_OF_SCOPE = {
+    "test_dense_propagation_native_hadamard_mlp_matches_reference_on_cuda",
+    "test_query_dense_propagation_native_hadamard_mlp_matches_reference_on_cuda",
+    "test_dense_propagation_native_hadamard_mlp_backward_matches_reference_on_cuda",
+    "test_query_dense_propagation_native_hadamard_mlp_backward_matches_reference_on_cuda",
+    "test_dense_transition_native_matches_reference_with_mlp_route_on_cuda",
+    "test_dense_transition_native_signed_abs_route_matches_reference_on_cuda",
+    "test_dense_transition_native_pairwise_routes_match_reference_on_cuda",
+    "test_dense_transition_native_hadamard_route_backward_matches_reference_on_cuda",
+    "test_sparse_transition_native_matches_reference_on_cuda",
+    "test_sparse_transition_native_pairwise_routes_match_reference_on_cuda",
+}
+
+RUNNER = """
+import sys
+sys.path.insert(0, {baseline!r}); sys.path.insert(0, {pkg!r})
+import reference_shim
+reference_shim.import_reference()
+import pytest
+sys.exit(pytest.main([{suite!r}, "-q", "-rA", "-p", "no:cacheprovider", "-k", "CudaNativeBackendTests"]))
+"""
+
+
+def test_reference_native_backend_suite_on_this_module():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    env = dict(os.environ, JAKAL_NET_NATIVE_MODULE="jakal_net_b200")
+    code = RUNNER.format(baseline=str(ROOT / "baseline"), pkg=str(ROOT / "jakal-net_b200"), suite=str(SUITE))
+    proc = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=900,
+                          cwd=str(SUITE.parent))
+    out = proc.stdout + proc.stderr
+    passed = {ln.split("::")[-1].strip() for ln in out.splitlines() if ln.startswith("PASSED")}
+    failed = {ln.split("::")[-1].split(" ")[0].strip() for ln in out.splitlines() if ln.startswith(("FAILED", "ERROR"))}
+    print(f"reference suite: {len(passed)} passed, {len(failed)} failed")
+    assert passed, out[-3000:]
+    unexpected = failed - OUT_OF_SCOPE
+    assert not unexpected, (sorted(unexpected), out[-4000:])
