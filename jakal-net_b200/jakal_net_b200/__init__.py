@@ -93,6 +93,8 @@ _SUPPORTED_OPS = (
     "transition_pairwise_dense",
     "transition_pairwise_topk",
     "transition_query_topk",
+    "transition_dense",
+    "transition_topk",
     # training: the per-source sparse transition's autograd route (native_backend.py:5962-5975)
     "low_rank_pairwise_topk_forward_cuda",
     "low_rank_pairwise_topk_backward_cuda",
@@ -1231,3 +1233,74 @@ def low_rank_propagation_causal_dense_signed_abs_forward_cuda(weighted_projected
     return _projected_propagation(weighted_projected_source, projected_target, projected_state, projected_val,
                                   k=None, window=max(n - 1, 0), score_bias=score_bias,
                                   compress=_lib.JK_SIGNED_ABS_SOFTMAX)
+
+
+# ----------------------------------------------------------------------------- node routes
+def _node_route_features(kind, in_weight, in_bias, out_weight, out_bias, src: Tensor):
+    """Route logits over a fixed set of destination nodes (route_kernel_spec,
+    kernel_common.py:214-232): linear (logits = src W^T + b) or mlp (logits =
+    silu(src W1^T + b1) W2^T + b2), written as the product of per-source features [h, 1]
+    and per-destination columns [W, b] so the select-aggregate kernel scores them. Returns
+    (row features [B, S, F + 1], destination columns [Dst, F + 1]) in f32."""
+    if kind not in ("linear", "mlp"):
+        raise TypeError(f"Unsupported route kind for b200_sm100a: {kind}")
+    x = src.float()
+    with _exact_f32_matmul():
+        if kind == "mlp":
+            if out_weight is None:
+                raise RuntimeError("MLP route kernel is missing its output layer.")
+            h = torch.matmul(x, in_weight.detach().float().t())
+            if in_bias is not None:
+                h = h + in_bias.detach().float()
+            h = torch.nn.functional.silu(h)
+            w, b = out_weight.detach().float(), out_bias
+        else:
+            h, w, b = x, in_weight.detach().float(), in_bias
+    ones = torch.ones(h.shape[:-1] + (1,), device=h.device, dtype=h.dtype)
+    bias = b.detach().float().reshape(-1, 1) if b is not None else torch.zeros((w.shape[0], 1), device=w.device)
+    return torch.cat([h, ones], -1).contiguous(), torch.cat([w, bias], -1).contiguous()
+
+
+def _node_transition(kind, in_weight, in_bias, out_weight, out_bias, compress, sender_strength, src_val,
+                     projected_state, projected_val, dst_nodes, k):
+    for name, t in (("sender_strength", sender_strength), ("src_val", src_val), ("projected_state", projected_state),
+                    ("projected_val", projected_val)):
+        _require_cuda(name, t)
+    batch_shape = src_val.shape[:-2]
+    out_dim = projected_val.shape[-1]
+    sv = _flatten_val(src_val)
+    pstate = _flatten_state(projected_state)
+    pval = _flatten_val(projected_val)
+    sender = _flatten_state(sender_strength).to(pstate.dtype)
+    rows, cols = _node_route_features(kind, in_weight, in_bias, out_weight, out_bias, sv)
+    if cols.shape[0] != int(dst_nodes):
+        raise RuntimeError(f"route produces {cols.shape[0]} destinations, expected {dst_nodes}")
+    cols = cols.unsqueeze(0).expand(sv.shape[0], -1, -1).contiguous()
+    st, vv = select_aggregate(rows, cols, pstate, pval, min(int(k), int(dst_nodes)), compress=compress,
+                              sender=sender, scatter=True)
+    return (st.to(projected_state.dtype).reshape(*batch_shape, int(dst_nodes)),
+            vv.to(projected_val.dtype).reshape(*batch_shape, int(dst_nodes), out_dim))
+
+
+@_entry
+def transition_dense(kind, in_weight, in_bias, out_weight, out_bias, route_compress_name, sender_strength, src_val,
+                     projected_state, projected_val, dst_nodes, src_block_size, dst_block_size):
+    """Dense Transition with a node route (LinearRoute / MLPRoute; jakal_net_native.cpp
+    transition_dense, transition.py:238-254): every source's routes over all destinations,
+    compressed, sender-weighted, summed into the destinations (select-aggregate kernel,
+    every destination selected)."""
+    if route_compress_name not in _ROUTE_CODE:
+        raise RuntimeError(f"Unsupported route compress {route_compress_name!r}")
+    return _node_transition(kind, in_weight, in_bias, out_weight, out_bias, _ROUTE_CODE[route_compress_name],
+                            sender_strength, src_val, projected_state, projected_val, dst_nodes, dst_nodes)
+
+
+@_entry
+def transition_topk(kind, in_weight, in_bias, out_weight, out_bias, sender_strength, src_val, projected_state,
+                    projected_val, dst_nodes, topk, src_block_size, dst_block_size):
+    """Sparse Transition with a node route (transition_topk_native, native_backend.py:5825-5855):
+    each source's top-k destinations, softmax over the k, sender-weighted scatter."""
+    if topk <= 0:
+        raise RuntimeError("topk must be positive.")
+    return _node_transition(kind, in_weight, in_bias, out_weight, out_bias, _lib.JK_SOFTMAX, sender_strength,
+                            src_val, projected_state, projected_val, dst_nodes, topk)

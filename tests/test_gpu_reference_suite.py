@@ -5,9 +5,8 @@ baseline/stage_reference.py) is run in a child process with
 JAKAL_NET_NATIVE_MODULE=jakal_net_b200. Its CUDA class exercises every native op through the
 Layer API, wraps the module ops with mock.patch.object(..., wraps=...) and compares with
 implementation="reference" at 1e-5. The cases on scorer / route kinds this backend does not
-implement (hadamard MLP pairwise and routes, MLP / linear routes and the full-bilinear route,
-which the reference's own module serves through transition_dense / transition_topk and the
-hadamard Functions) are expected to fail; every other case must pass."""
+implement (hadamard MLP pairwise and routes, the full-bilinear route) are expected to fail;
+every other case must pass."""
 from __future__ import annotations
 
 import os
@@ -23,17 +22,14 @@ SUITE = ROOT / "baseline" / "_ref" / "reference_tests" / "test_native_backend.py
 
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not SUITE.exists(), reason="reference suite not staged")]
 
-# CUDA cases on kinds outside this backend (hadamard MLP, MLP / linear / full-bilinear routes)
+# CUDA cases on kinds outside this backend (hadamard MLP pairwise / routes, full-bilinear route)
 OUT_OF_SCOPE = {
     "test_dense_propagation_native_hadamard_mlp_matches_reference_on_cuda",
     "test_query_dense_propagation_native_hadamard_mlp_matches_reference_on_cuda",
     "test_dense_propagation_native_hadamard_mlp_backward_matches_reference_on_cuda",
     "test_query_dense_propagation_native_hadamard_mlp_backward_matches_reference_on_cuda",
-    "test_dense_transition_native_matches_reference_with_mlp_route_on_cuda",
-    "test_dense_transition_native_signed_abs_route_matches_reference_on_cuda",
     "test_dense_transition_native_pairwise_routes_match_reference_on_cuda",
     "test_dense_transition_native_hadamard_route_backward_matches_reference_on_cuda",
-    "test_sparse_transition_native_matches_reference_on_cuda",
     "test_sparse_transition_native_pairwise_routes_match_reference_on_cuda",
 }
 
