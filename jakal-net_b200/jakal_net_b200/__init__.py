@@ -463,7 +463,7 @@ def _route_projections(route_kind, source_weight, source_bias, target_weight, ta
     (ps . pd + b) / T. Returns a Scorer whose row side is the source (src_proj / T) and
     column side the destination. Other route kinds raise TypeError."""
     if route_kind not in ("low_rank_bilinear_route", "multihead_max_low_rank_bilinear_route",
-                          "diagonal_bilinear_route"):
+                          "diagonal_bilinear_route", "full_bilinear_route"):
         raise TypeError(f"Unsupported pairwise route kind for b200_sm100a: {route_kind}")
     temperature = float(temperature)
     if temperature <= 0.0:
@@ -480,6 +480,16 @@ def _route_projections(route_kind, source_weight, source_bias, target_weight, ta
         raise RuntimeError("Low-rank route kernel is missing projection weights.")
     if any(t is not None for t in (source_bias, target_bias, hidden_weight, hidden_bias, out_weight, out_bias)):
         raise TypeError("Low-rank route projections take no bias / hidden layers.")
+    if route_kind == "full_bilinear_route":
+        # BilinearPairwiseRoute (modules.py:533-564): logits = (src W_s^T) W (dst W_t^T)^T + b, i.e.
+        # the source projection against the destination features (dst W_t^T) W^T; f32 features
+        # on the select-aggregate path
+        ps = _generic_project(sx.reshape(-1, sx.shape[-1]).float(), source_weight, None, temperature)
+        with _exact_f32_matmul():
+            pd = torch.matmul(_generic_project(dx.reshape(-1, dx.shape[-1]).float(), target_weight),
+                              core_weight.detach().float().t())
+        return Scorer(ps.reshape(*sx.shape[:-1], -1), pd.reshape(*dx.shape[:-1], -1).contiguous(),
+                      _bias_tensor(bias, dev, temperature), False)
     if route_kind == "multihead_max_low_rank_bilinear_route":
         if not fused:
             raise TypeError("b200_sm100a multi-head routes run in the fused kernels only (k <= 64).")

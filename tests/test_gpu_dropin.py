@@ -354,3 +354,31 @@ def test_hierarchical_memory_level_write_and_propagation(jn, module, direction_o
     assert mocks["transition_pairwise_topk"].call_count + mocks["low_rank_pairwise_topk_forward_cuda"].call_count > 0
     _close(want_w, got_w, atol=1e-4, rtol=1e-4)
     _close(want_p, got_p, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("route", ["linear", "mlp", "full_bilinear"])
+@pytest.mark.parametrize("k", [3, 0])
+def test_node_and_full_bilinear_routes(jn, module, route, k):
+    """Linear / MLP node routes (transition_dense, transition_topk) and the full-bilinear
+    pairwise route, dense (k = 0) and sparse, native against reference."""
+    src = _layer(jn, 40, 6, 60)
+    dst = _layer(jn, 9, 6, 61)
+    if route == "linear":
+        make = lambda: jn.LinearRoute(src_dim=6, dst_nodes=9)  # noqa: E731
+    elif route == "mlp":
+        make = lambda: jn.MLPRoute(src_dim=6, dst_nodes=9, hidden_dim=11)  # noqa: E731
+    else:
+        make = lambda: jn.BilinearPairwiseRoute(src_dim=6, dst_dim=6, route_dim=5)  # noqa: E731
+    rf = make().cuda()
+    if k:
+        ref, nat = _pair(lambda **kw: jn.SparseTransition(route_fn=rf, topk=k, state_activation_fn=lambda x: x + 1.25,
+                                                          val_proj_fn=_val_proj, state_proj_fn=_state_proj, **kw))
+        op = "transition_pairwise_topk" if route == "full_bilinear" else "transition_topk"
+    else:
+        ref, nat = _pair(lambda **kw: jn.Transition(route_fn=rf, state_activation_fn=lambda x: x + 1.25,
+                                                    val_proj_fn=_val_proj, state_proj_fn=_state_proj, **kw))
+        op = "transition_pairwise_dense" if route == "full_bilinear" else "transition_dense"
+    with mock.patch.object(module, op, wraps=getattr(module, op)) as w:
+        got = nat.compute_delta(src, dst)
+    assert w.call_count > 0
+    _close(ref.compute_delta(src, dst), got)
