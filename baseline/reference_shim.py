@@ -41,7 +41,14 @@ def import_reference(src: Path = STAGED):
             del sys.modules[name]
     if str(src) not in sys.path:
         sys.path.insert(0, str(src))
-    return importlib.import_module("jakal_net")
+    pkg = importlib.import_module("jakal_net")
+    # The pre-loaded _architectural_common still holds the classes of the stub-time import of
+    # jakal_net.modules; re-executing it in place binds the package's own classes (functions
+    # other modules imported from it read its globals, so they follow), and keeps the alias.
+    common = importlib.reload(sys.modules["jakal_net._architectural_common"])
+    if not hasattr(common, "unit_normalize_values"):
+        common.unit_normalize_values = common.normalize_value_directions
+    return pkg
 
 
 def import_progressive_b(src: Path = STAGED):
