@@ -709,8 +709,11 @@ __device__ __forceinline__ void sel_barrier() {
 // Source window of a CTA's tensor-core aggregate: rows [s_lo, s_lo + n) of the values,
 // s_lo on the score-tile grid, so that 64-row source tile kt is the first (even kt) or the
 // second (odd kt) half of a score tile -- the columns of candidate stack 0 or 1.
-// Taken when the CTA's sources form a window of at most 1024 rows of 16-bit values whose
-// width fits the TMEM accumulator beside the edge tiles (identical in every thread).
+// Taken for 16-bit values whose width fits the TMEM accumulator beside the edge tiles, when
+// the CTA's sources (its causal window, or every column without a window) are few enough
+// that the dense edge-tile MMAs (4 * n * dim * 128 FLOP) beat the latency-bound CUDA-core
+// gather of the k selected rows: n <= 1024, or n <= 128 * k + 1024 (identical in every
+// thread).
 struct SlabRange {
   int s_lo, n;
   bool on;
@@ -719,13 +722,15 @@ struct SlabRange {
 template <typename VT>
 __device__ __forceinline__ SlabRange slab_range(const Params& p, int64_t t0) {
   SlabRange r{0, 0, false};
-  if (p.slab_ok && p.window >= 0 && sizeof(VT) == 2 && (p.dim % 64) == 0) {
-    const int64_t lo = t0 - p.window;
-    r.s_lo = static_cast<int>((lo > 0 ? lo : 0) / kCols * kCols);  // on the score-tile grid
-    int64_t hi_col = t0 + kRows - 1;
-    if (hi_col > p.n_cols - 1) hi_col = p.n_cols - 1;
+  if (p.slab_ok && sizeof(VT) == 2 && (p.dim % 64) == 0) {
+    int64_t hi_col = p.n_cols - 1;
+    if (p.window >= 0) {
+      const int64_t lo = t0 - p.window;
+      r.s_lo = static_cast<int>((lo > 0 ? lo : 0) / kCols * kCols);  // on the score-tile grid
+      if (t0 + kRows - 1 < hi_col) hi_col = t0 + kRows - 1;
+    }
     r.n = static_cast<int>(hi_col - r.s_lo + 1);
-    r.on = r.n > 0 && r.n <= 1024 && p.dim <= kOCols;
+    r.on = r.n > 0 && (r.n <= 1024 || r.n <= 128 * p.k + 1024) && p.dim <= kOCols;
   }
   return r;
 }
@@ -1068,15 +1073,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t v[2][32];
         if (!load_tile(v)) { ok = false; break; }
         const int col0 = static_cast<int>((j_lo + it) * kCols) + half * kHalfCols;
+        if (static_cast<uint32_t>(col0 - lo_t) <= span && static_cast<uint32_t>(col0 + kHalfCols - 1 - lo_t) <= span) {
+          // every column of this thread's share is visible (the interior of a window)
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float x = __uint_as_float(v[c][e]);
-            const bool vis = static_cast<uint32_t>(col0 + c * 32 + e - lo_t) <= span;
-            a1 += vis ? x : 0.f;
-            a2 = vis ? fmaf(x, x, a2) : a2;
-          }
+            for (int e = 0; e < 32; ++e) {
+              const float x = __uint_as_float(v[c][e]);
+              a1 += x;
+              a2 = fmaf(x, x, a2);
+            }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float x = __uint_as_float(v[c][e]);
+              const bool vis = static_cast<uint32_t>(col0 + c * 32 + e - lo_t) <= span;
+              a1 += vis ? x : 0.f;
+              a2 = vis ? fmaf(x, x, a2) : a2;
+            }
+        }
       }
       s1[half * kRows + row] = a1;
       s2[half * kRows + row] = a2;
@@ -1106,31 +1123,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     // register counter (no atomics); a row whose stacks meet takes the exact fallback pass.
     {
       const float th = tau[row];
-      const uint32_t rv_s = smem_u32(rv), ri_s = smem_u32(ri);
+      // slot myc of this half's stack: byte offset o_base + o_step * myc
+      const int o_base = half == 0 ? 0 : (kCap - 1) * 4;
+      const int o_step = half == 0 ? 4 : -4;
+      const uint32_t rv_s = smem_u32(rv) + o_base, ri_s = smem_u32(ri) + o_base;
       int myc = 0;
+      // predicated append (no branch): a passing column goes to slot myc of this half's
+      // stack while it has room; myc counts every passing column
+      auto append = [&](bool pass, float x, int col) {
+        const uint32_t off = static_cast<uint32_t>(o_step * myc);
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %0, 0;\n\t"
+            "@p st.shared.f32 [%1], %2;\n\t"
+            "@p st.shared.b32 [%3], %4;\n\t}" ::"r"(static_cast<int>(pass && myc < kCap)),
+            "r"(rv_s + off), "f"(x), "r"(ri_s + off), "r"(col)
+            : "memory");
+        myc += pass ? 1 : 0;
+      };
       for (int it = 0; it < ntiles && ok; ++it) {
         uint32_t v[2][32];
         if (!load_tile(v)) { ok = false; break; }
         const int col0 = static_cast<int>((j_lo + it) * kCols) + half * kHalfCols;
+        if (static_cast<uint32_t>(col0 - lo_t) <= span && static_cast<uint32_t>(col0 + kHalfCols - 1 - lo_t) <= span) {
+          // interior: every column of this thread's share is visible
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            // predicated append (no branch): a passing column goes to slot myc of this
-            // half's stack while it has room; myc counts every passing column
-            const int col = col0 + c * 32 + e;
-            const float x = __uint_as_float(v[c][e]);
-            const bool pass = static_cast<uint32_t>(col - lo_t) <= span && x >= th;
-            const uint32_t off = static_cast<uint32_t>(half == 0 ? myc : kCap - 1 - myc) * 4u;
-            asm volatile(
-                "{\n\t.reg .pred p;\n\t"
-                "setp.ne.b32 p, %0, 0;\n\t"
-                "@p st.shared.f32 [%1], %2;\n\t"
-                "@p st.shared.b32 [%3], %4;\n\t}" ::"r"(static_cast<int>(pass && myc < kCap)),
-                "r"(rv_s + off), "f"(x), "r"(ri_s + off), "r"(col)
-                : "memory");
-            myc += pass ? 1 : 0;
-          }
+            for (int e = 0; e < 32; ++e) {
+              const float x = __uint_as_float(v[c][e]);
+              append(x >= th, x, col0 + c * 32 + e);
+            }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int col = col0 + c * 32 + e;
+              const float x = __uint_as_float(v[c][e]);
+              append(static_cast<uint32_t>(col - lo_t) <= span && x >= th, x, col);
+            }
+        }
       }
       (half == 0 ? cnt : nsel)[row] = myc;
     }
@@ -1589,7 +1622,7 @@ int launch(const void* row_proj, const void* col_proj, int64_t batch, int64_t n_
   if (status != JK_OK) return status;
   tv = tc;  // placeholder when the slab path is off
   p.slab_ok = 0;
-  if (MODE == kGather && p.window >= 0 && p.val_dtype != JK_F32 && p.dim % 64 == 0 && aligned16(p.col_val)) {
+  if (MODE == kGather && p.val_dtype != JK_F32 && p.dim % 64 == 0 && aligned16(p.col_val)) {
     if (make_tmap_3d_16bit(&tv, p.col_val, p.dim, n_cols, batch, 64, kEK, p.val_dtype == JK_BF16, true) == JK_OK)
       p.slab_ok = 1;
   }
