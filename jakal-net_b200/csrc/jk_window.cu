@@ -11,7 +11,8 @@
 // the CUDA window kernels jakal_net_native_cuda.cu:1579-1750 (softsign / signed-abs) and
 // :2023-2109 (entmax, O(W^2) serial sort there) and the dense kernels :1388-1576.
 //
-// Flash-style on tcgen05. One CTA = 128 target rows x one slice of <= 192 value columns.
+// Flash-style on tcgen05. One CTA = 128 target rows x one slice of <= 256 value columns
+// (<= 128 when f32 values come as hi + lo planes).
 //   warp 8: TMA of the target projection tile, source projection tiles (ring), value tiles
 //           (ring, MN-major 128B-swizzled boxes); tcgen05.mma S = Pt . Ps^T into two TMEM
 //           score buffers, and in the final pass O += E . V into a TMEM accumulator.
@@ -39,7 +40,7 @@ constexpr int kCols = 128;
 constexpr int kHalfCols = 64;
 constexpr int kSelWarps = 8;
 constexpr int kThreads = (kSelWarps + 1) * 32;
-constexpr int kMaxSlice = 192;   // value columns per CTA
+constexpr int kMaxSlice = 256;   // value columns per CTA (TMEM: 2 x 128 score + 256 output columns)
 constexpr int kMaxEntIters = 48;  // cap on threshold iterations (converges in a few)
 constexpr int kStageCols = 1024;  // source states staged in shared memory when the CTA's columns fit
 
@@ -90,11 +91,13 @@ template <int KATOMS>
 struct Layout {
   static constexpr int kAtom = kRows * 128;  // 16 KB: 128 rows x 128 B
   static constexpr int kPsStages = KATOMS == 1 ? 2 : 1;
-  static constexpr int kVStages = KATOMS == 1 ? 2 : 1;
+  // one value stage: the edge tiles are single-buffered, so the next value tile is only
+  // needed once the edges of its source tile exist, which takes longer than its load
+  static constexpr int kVStages = 1;
   static constexpr int kA = KATOMS * kAtom;
   static constexpr int kPs = kPsStages * KATOMS * kAtom;
   static constexpr int kE = 2 * 2 * kAtom;                        // hi + lo, 2 K atoms each
-  static constexpr int kVStage = (kMaxSlice / 64) * kAtom;         // 3 boxes of 64 columns
+  static constexpr int kVStage = (kMaxSlice / 64) * kAtom;         // 4 boxes of 64 columns
   static constexpr int kV = kVStages * kVStage;
   static constexpr int kRowArrays = 16 * kRows * 4;
   static constexpr int kStage = kStageCols * 4;  // the CTA's source states, f32
@@ -266,10 +269,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_v = [&](int it) {  // value tile `it` of the final pass into stage it % VS
         const int s = it % VS;
         const int col0 = static_cast<int>((j_lo + it) * kCols);
-        if (p.vsplit) {  // one 64-column slice: hi plane box, then lo plane box
-          mbar_arrive_expect_tx(&vfull[s], 2 * L::kAtom);
-          tma_load_3d(v_ring + s * L::kVStage, &tm_val, &vfull[s], d0, col0, static_cast<int>(b));
-          tma_load_3d(v_ring + s * L::kVStage + L::kAtom, &tm_val_lo, &vfull[s], d0, col0, static_cast<int>(b));
+        if (p.vsplit) {  // <= 128 columns: the hi plane boxes, then the lo plane boxes from atom 2
+          mbar_arrive_expect_tx(&vfull[s], 2 * nbox * L::kAtom);
+          for (int a = 0; a < nbox; ++a) {
+            tma_load_3d(v_ring + s * L::kVStage + a * L::kAtom, &tm_val, &vfull[s], d0 + a * 64, col0,
+                        static_cast<int>(b));
+            tma_load_3d(v_ring + s * L::kVStage + (2 + a) * L::kAtom, &tm_val_lo, &vfull[s], d0 + a * 64, col0,
+                        static_cast<int>(b));
+          }
         } else {
           mbar_arrive_expect_tx(&vfull[s], nbox * L::kAtom);
           for (int a = 0; a < nbox; ++a)
@@ -302,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int nprod = p.vsplit ? 3 : 2;
           for (int q = 0; q < nprod; ++q) {
             const uint32_t e_addr = smem_u32(q == 1 ? e_lo : e_hi);
-            const uint32_t vb = v_addr + (q == 2 ? L::kAtom : 0u);
+            const uint32_t vb = v_addr + (q == 2 ? 2u * L::kAtom : 0u);
             for (int kk = 0; kk < 8; ++kk) {
               const uint32_t aoff = (kk >> 2) * L::kAtom + (kk & 3) * 32;
               mma_f16_ss(tmem_o, sdesc_kmajor_sw128(e_addr + aoff), sdesc_mnmajor_sw128(vb + kk * 2048, L::kAtom),
@@ -665,7 +672,9 @@ int launch(const void* row_proj, const void* col_proj, const void* col_val, cons
     if (status != JK_OK) return status;
   }
   const int nslice = static_cast<int>((p.dim + kMaxSlice - 1) / kMaxSlice);
-  const int per = p.vsplit ? 64 : static_cast<int>(((p.dim / 64 + nslice - 1) / nslice) * 64);
+  const int nslice_split = static_cast<int>((p.dim + 127) / 128);  // hi + lo planes: <= 128 columns
+  const int per = p.vsplit ? static_cast<int>(((p.dim / 64 + nslice_split - 1) / nslice_split) * 64)
+                           : static_cast<int>(((p.dim / 64 + nslice - 1) / nslice) * 64);
   const uint32_t fmt = bf16 ? 1u : 0u;
   const uint32_t idesc_s = idesc_f16(kRows, kCols, fmt);
   constexpr int sm = Layout<KATOMS>::kTotal;

@@ -674,29 +674,44 @@ def _value_planes(pval: Tensor, proj_dtype: torch.dtype):
     return pval.contiguous(), pval_lo, pad
 
 
+def _split2_bf16(x: Tensor) -> tuple[Tensor, Tensor]:
+    """x (f32) = hi + lo as two bf16 planes, one pass (jk_split2_bf16)."""
+    x = x.contiguous()
+    hi = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
+    lo = torch.empty_like(hi)
+    with torch.cuda.device(x.device):
+        check(_LIBRARY.jk_split2_bf16(x.data_ptr(), x.numel(), hi.data_ptr(), lo.data_ptr(), _stream(x.device)),
+              "jk_split2_bf16")
+    return hi, lo
+
+
 def routes_aggregate(routes: Tensor, state: Tensor, val: Tensor) -> tuple[Tensor, Tensor]:
     """Aggregate of a dense route matrix: out_state[b, d] = sum_s routes[b, s, d] state[b, s],
     out_val[b, d] = sum_s routes[b, s, d] val[b, s] (f32 results). Tensor-core GEMMs with f32
     accumulation and output: the routes are split into hi + lo planes of the values' 16-bit
     dtype (two GEMMs); f32 values are split into bf16 hi + lo planes too (three GEMMs, the
-    lo x lo product dropped: ~2^-16 relative)."""
+    lo x lo product dropped: ~2^-16 relative). The bf16 splits are single passes of the
+    library's split kernel."""
     rt = routes.transpose(1, 2)
     with _exact_f32_matmul():
         out_state = torch.bmm(rt, state.float().unsqueeze(-1)).squeeze(-1)
-    dt = val.dtype if val.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
-    r_hi = routes.to(dt)
-    r_lo = (routes - r_hi.float()).to(dt)
-    if val.dtype == dt:
+    if val.dtype == torch.float16:
+        r_hi = routes.to(torch.float16)
+        r_lo = (routes - r_hi.float()).to(torch.float16)
         out_val = torch.bmm(r_hi.transpose(1, 2), val, out_dtype=torch.float32)
         out_val += torch.bmm(r_lo.transpose(1, 2), val, out_dtype=torch.float32)
+        return out_state, out_val
+    r_hi, r_lo = _split2_bf16(routes)
+    r_hi, r_lo = r_hi.transpose(1, 2), r_lo.transpose(1, 2)
+    if val.dtype == torch.bfloat16:
+        out_val = torch.bmm(r_hi, val, out_dtype=torch.float32)
+        out_val += torch.bmm(r_lo, val, out_dtype=torch.float32)
     else:
         # f32 values: hi + lo planes on both sides, the three products above 2^-16
-        v = val.float()
-        v_hi = v.to(dt)
-        v_lo = (v - v_hi.float()).to(dt)
-        out_val = torch.bmm(r_hi.transpose(1, 2), v_hi, out_dtype=torch.float32)
-        out_val += torch.bmm(r_hi.transpose(1, 2), v_lo, out_dtype=torch.float32)
-        out_val += torch.bmm(r_lo.transpose(1, 2), v_hi, out_dtype=torch.float32)
+        v_hi, v_lo = _split2_bf16(val.float())
+        out_val = torch.bmm(r_hi, v_hi, out_dtype=torch.float32)
+        out_val += torch.bmm(r_hi, v_lo, out_dtype=torch.float32)
+        out_val += torch.bmm(r_lo, v_hi, out_dtype=torch.float32)
     return out_state, out_val
 
 
