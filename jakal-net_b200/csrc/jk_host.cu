@@ -94,7 +94,8 @@ int jk_device_status(jk_stream_t stream, int* device_status) {
     cudaGetLastError();
     return JK_ERR_LAUNCH;
   }
-  int (*readers[])(int*) = {jk::read_error_project, jk::read_error_topk, jk::read_error_window};
+  int (*readers[])(int*) = {jk::read_error_project,  jk::read_error_topk,     jk::read_error_topk_bf16,
+                            jk::read_error_topk_f16, jk::read_error_topk_f32, jk::read_error_window};
   int combined = JK_OK;
   for (auto read : readers) {
     int value = JK_OK;

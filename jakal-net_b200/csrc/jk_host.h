@@ -29,10 +29,13 @@ static __device__ int g_device_error = 0;
     return JK_OK;                                                                       \
   }
 
-// Readers of the units that launch kernels with bounded waits (jk_project.cu, jk_topk.cu,
-// jk_window.cu).
+// Readers of the units that launch kernels with bounded waits (jk_project.cu, jk_topk.cu and
+// its per-value-type units jk_topk_vt_*.cu, jk_window.cu).
 int read_error_project(int* value);
 int read_error_topk(int* value);
+int read_error_topk_bf16(int* value);
+int read_error_topk_f16(int* value);
+int read_error_topk_f32(int* value);
 int read_error_window(int* value);
 
 // Returns JK_OK when the current device is sm_100 (cached per device ordinal).

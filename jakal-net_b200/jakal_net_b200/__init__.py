@@ -703,15 +703,16 @@ def routes_aggregate(routes: Tensor, state: Tensor, val: Tensor) -> tuple[Tensor
         return out_state, out_val
     r_hi, r_lo = _split2_bf16(routes)
     r_hi, r_lo = r_hi.transpose(1, 2), r_lo.transpose(1, 2)
+    # the later products accumulate into the f32 result inside the GEMM (beta = 1)
     if val.dtype == torch.bfloat16:
         out_val = torch.bmm(r_hi, val, out_dtype=torch.float32)
-        out_val += torch.bmm(r_lo, val, out_dtype=torch.float32)
+        out_val = torch.baddbmm(out_val, r_lo, val, out_dtype=torch.float32)
     else:
         # f32 values: hi + lo planes on both sides, the three products above 2^-16
         v_hi, v_lo = _split2_bf16(val.float())
         out_val = torch.bmm(r_hi, v_hi, out_dtype=torch.float32)
-        out_val += torch.bmm(r_hi, v_lo, out_dtype=torch.float32)
-        out_val += torch.bmm(r_lo, v_hi, out_dtype=torch.float32)
+        out_val = torch.baddbmm(out_val, r_hi, v_lo, out_dtype=torch.float32)
+        out_val = torch.baddbmm(out_val, r_lo, v_hi, out_dtype=torch.float32)
     return out_state, out_val
 
 
