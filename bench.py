@@ -909,6 +909,9 @@ MICRO = {
     "transition": dict(B=32, S=1024, Q=128, D=512, R=64, K=32),
     # the same top-k propagation through the select-aggregate kernel (path comparison)
     "topk_select": dict(B=32, N=256, D=512, R=64, K=32),
+    # one batch item of config 5 (window 4096 intersect top-k 64): the small case of the
+    # fused kernel's long-window form for profiling
+    "window_topk": dict(B=1, N=32768, D=512, R=64, K=64, W=4096),
 }
 
 
@@ -940,6 +943,10 @@ def run_micro(args, device):
             def op():
                 return jk.propagation_window("low_rank_bilinear", core, None, w_s, None, w_t, None, "softsign", val,
                                              st, val, c["W"], 128, 128)
+        elif args.micro == "window_topk":
+            def op():
+                return jk.propagation_window_topk("low_rank_bilinear", core, None, w_s, None, w_t, None, "softsign",
+                                                  val, st, val, c["W"], c["K"], 128, 128)
         elif args.micro == "topk_select":
             def op():
                 rp, cp = jk.lowrank_project_pair(val, w_t, w_s, core=core)

@@ -644,21 +644,32 @@ __device__ void warp_rank_pair(float* const (&rv)[2], int* const (&ri)[2], const
     n4[r] = (n[r] + 3) & ~3;
   }
   const int nmax = n4[0] > n4[1] ? n4[0] : n4[1];
+#ifdef JK_PHASE_PROFILE
+  const long long tp0 = clock64();
+#endif
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
 #pragma unroll
     for (int q = 0; q < NQ; ++q) {
       const int i = q * 32 + lane;
       const int e = i < c0[r] ? i : kCap - 1 - (i - c0[r]);
-      const bool real_i = i < n[r] && ri[r][e] != kSentinel;
-      sc[r][q] = real_i ? rv[r][e] : 0.f;
-      col[r][q] = real_i ? ri[r][e] : 0;
+      // both reads unconditional (e stays inside the row's buffer), so they overlap
+      const int ci = ri[r][e];
+      const float cv = rv[r][e];
+      const bool real_i = i < n[r] && ci != kSentinel;
+      sc[r][q] = real_i ? cv : 0.f;
+      col[r][q] = real_i ? ci : 0;
       u[r][q] = real_i ? static_cast<uint32_t>(make_key(sc[r][q], col[r][q]) >> 32) : 0u;
       if (i < nmax) ku[r * kCap + i] = u[r][q];  // zero beyond the row: never beats a key
       rank[r][q] = 0;
     }
   }
   __syncwarp();
+#ifdef JK_PHASE_PROFILE
+  const long long tp1 = clock64();
+#endif
+  // four broadcast reads per row in flight per step
+#pragma unroll 4
   for (int j = 0; j < nmax; j += 4) {
     const uint4 a = *reinterpret_cast<const uint4*>(ku + j);
     const uint4 b = *reinterpret_cast<const uint4*>(ku + kCap + j);
@@ -668,6 +679,9 @@ __device__ void warp_rank_pair(float* const (&rv)[2], int* const (&ri)[2], const
       rank[1][q] += (b.x > u[1][q]) + (b.y > u[1][q]) + (b.z > u[1][q]) + (b.w > u[1][q]);
     }
   }
+#ifdef JK_PHASE_PROFILE
+  const long long tp2 = clock64();
+#endif
   const uint32_t lt = (1u << lane) - 1u;
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -704,6 +718,16 @@ __device__ void warp_rank_pair(float* const (&rv)[2], int* const (&ri)[2], const
     }
   }
   __syncwarp();
+#ifdef JK_PHASE_PROFILE
+  if (threadIdx.x == 0) {
+    const int cta = blockIdx.y * gridDim.x + blockIdx.x;
+    if (cta < kTraceCtas) {
+      g_trace[cta][29] += tp1 - tp0;
+      g_trace[cta][30] += tp2 - tp1;
+      g_trace[cta][31] += clock64() - tp2;
+    }
+  }
+#endif
 }
 
 __device__ __forceinline__ void sel_barrier() {

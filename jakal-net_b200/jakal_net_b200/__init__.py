@@ -137,12 +137,23 @@ def _entry(fn):
 
     @functools.wraps(fn)
     def wrapper(*args, **kwargs):
+        # plain flag toggles (not the context managers): an op is called per layer of a model
+        # step, and the host time of every call adds to the step when the GPU waits on it
         prev = getattr(_TLS, "autocast", None)
-        _TLS.autocast = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else None
+        ac_on = torch.is_autocast_enabled("cuda")
+        grad_on = torch.is_grad_enabled()
+        _TLS.autocast = torch.get_autocast_dtype("cuda") if ac_on else None
+        if ac_on:
+            torch.set_autocast_enabled("cuda", False)
+        if grad_on:
+            torch.set_grad_enabled(False)
         try:
-            with torch.autocast("cuda", enabled=False), torch.no_grad():
-                return fn(*args, **kwargs)
+            return fn(*args, **kwargs)
         finally:
+            if grad_on:
+                torch.set_grad_enabled(True)
+            if ac_on:
+                torch.set_autocast_enabled("cuda", True)
             _TLS.autocast = prev
 
     return wrapper
@@ -187,7 +198,15 @@ def _ptr(t: Optional[Tensor]) -> Optional[int]:
 
 
 def _stream(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The raw handle of the current torch stream of `device`."""
+    return torch._C._cuda_getCurrentRawStream(device.index if device.index is not None else torch.cuda.current_device())
+
+
+def _on(device: torch.device):
+    """Makes `device` current for the block (no guard when it already is)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def _require_cuda(name: str, t: Tensor) -> None:
@@ -252,7 +271,7 @@ def lowrank_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None,
             raise RuntimeError(f"b200_sm100a three-plane f32 scoring supports score rank <= 32 (got {rank}).")
         proj = _generic_project(x2, weight, core, temperature)
         out = torch.empty((x2.shape[0], 128), device=x.device, dtype=torch.bfloat16)
-        with torch.cuda.device(x.device):
+        with _on(x.device):
             check(_LIBRARY.jk_split3_bf16(proj.data_ptr(), x2.shape[0], rank, out.data_ptr(), _stream(x.device)),
                   "jk_split3_bf16")
         return out.reshape(*x.shape[:-1], 128)
@@ -263,7 +282,7 @@ def lowrank_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None,
     c = None if core is None else core.detach().reshape(-1).to(device=x.device, dtype=x.dtype).contiguous()
     rp = int(_LIBRARY.jk_padded_rank(rank))
     out = torch.empty((x2.shape[0], rp), device=x.device, dtype=x.dtype)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         check(
             _LIBRARY.jk_lowrank_project(x2.data_ptr(), x2.shape[0], x2.shape[1], w.data_ptr(), rank, _ptr(c),
                                         float(temperature), code, out.data_ptr(), rp, _stream(x.device)),
@@ -286,7 +305,7 @@ def lowrank_project_pair(x: Tensor, weight: Tensor, weight2: Tensor, core: Optio
     c = None if core is None else core.detach().reshape(-1).to(device=x.device, dtype=x.dtype).contiguous()
     out = torch.empty((x2.shape[0], 64), device=x.device, dtype=x.dtype)
     out2 = torch.empty((x2.shape[0], 64), device=x.device, dtype=x.dtype)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         check(
             _LIBRARY.jk_lowrank_project_pair(x2.data_ptr(), x2.shape[0], x2.shape[1], w.data_ptr(), w2.data_ptr(),
                                              rank, _ptr(c), float(temperature), _proj_dtype(x), out.data_ptr(),
@@ -538,7 +557,7 @@ def topk_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_va
             k, window, float(score_bias), _ptr(bias), compress,
             out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state),
             _ptr(scores), _ptr(index))
-    with torch.cuda.device(dev):
+    with _on(dev):
         if rows is not None:
             if heads is not None:
                 raise RuntimeError("row blocks take the single-head scorer")
@@ -595,7 +614,7 @@ def select_aggregate(row_f: Tensor, col_f: Tensor, state: Tensor, val: Tensor, k
     sel_s = torch.empty((B, chunk, kk), device=dev, dtype=torch.float32)
     sel_i = torch.empty((B, chunk, kk), device=dev, dtype=torch.int64)
     col_t = col_f.transpose(1, 2)
-    with torch.cuda.device(dev):
+    with _on(dev):
         for r0 in range(0, T, chunk):
             rc = min(chunk, T - r0)
             if row_f.dtype in (torch.bfloat16, torch.float16):
@@ -639,7 +658,7 @@ def masked_aggregate(row_proj: Tensor, col_proj: Tensor, col_state: Tensor, col_
             col_state.data_ptr(), _dtype_code("state", col_state), col_val.data_ptr(), _ptr(col_val_lo), D,
             int(window), float(score_bias), _ptr(bias), compress,
             out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
-    with torch.cuda.device(dev):
+    with _on(dev):
         if heads is None:
             check(_LIBRARY.jk_propagation_window_forward(*args, _stream(dev)), "jk_propagation_window_forward")
         else:
@@ -663,7 +682,7 @@ def _value_planes(pval: Tensor, proj_dtype: torch.dtype):
         pval = pval.contiguous()
         hi = torch.empty(pval.shape, device=pval.device, dtype=torch.bfloat16)
         pval_lo = torch.empty_like(hi)
-        with torch.cuda.device(pval.device):
+        with _on(pval.device):
             check(_LIBRARY.jk_split2_bf16(pval.data_ptr(), pval.numel(), hi.data_ptr(), pval_lo.data_ptr(),
                                           _stream(pval.device)), "jk_split2_bf16")
         pval = hi
@@ -679,7 +698,7 @@ def _split2_bf16(x: Tensor) -> tuple[Tensor, Tensor]:
     x = x.contiguous()
     hi = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
     lo = torch.empty_like(hi)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         check(_LIBRARY.jk_split2_bf16(x.data_ptr(), x.numel(), hi.data_ptr(), lo.data_ptr(), _stream(x.device)),
               "jk_split2_bf16")
     return hi, lo
@@ -857,7 +876,7 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
         args = (sc.row.data_ptr(), sc.col.data_ptr(), B, sv.shape[1], n_dst, sc.row.shape[-1],
                 _proj_dtype(sc.row, sc.split3), sender.data_ptr(), _dtype_code("sender", sender), k, 0.0,
                 _ptr(sc.bias), compress, routes.data_ptr(), None, None)
-        with torch.cuda.device(dev):
+        with _on(dev):
             if sc.heads is None:
                 check(_LIBRARY.jk_transition_pairwise_topk_routes(*args, _stream(dev)),
                       "jk_transition_pairwise_topk_routes")
@@ -875,7 +894,7 @@ def transition_pairwise_topk(route_kind, source_weight, source_bias, target_weig
                 pval.data_ptr(), out_dim, _dtype_code("val", pval),
                 k, 0.0, _ptr(sc.bias), compress, accum.data_ptr(),
                 out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
-        with torch.cuda.device(dev):
+        with _on(dev):
             if sc.heads is None:
                 check(_LIBRARY.jk_transition_pairwise_topk_forward(*args, _stream(dev)),
                       "jk_transition_pairwise_topk_forward")
@@ -930,7 +949,7 @@ def transition_pairwise_dense(route_kind, source_weight, source_bias, target_wei
             pval.data_ptr(), _ptr(pval_lo), pval.shape[-1],
             0.0, _ptr(sc.bias), compress, stats.data_ptr(),
             out_state.data_ptr(), out_val.data_ptr(), _dtype_code("out", out_state))
-    with torch.cuda.device(dev):
+    with _on(dev):
         if sc.heads is None:
             check(_LIBRARY.jk_transition_pairwise_dense_forward(*args, _stream(dev)),
                   "jk_transition_pairwise_dense_forward")
@@ -1062,7 +1081,7 @@ def low_rank_pairwise_topk_forward_cuda(weighted_projected_source, projected_tar
         routes = torch.zeros((B, S, Dn), device=wps.device, dtype=torch.float32)
         scores = torch.empty((B, S, k), device=wps.device, dtype=torch.float32)
         index = torch.empty((B, S, k), device=wps.device, dtype=torch.int64)
-        with torch.cuda.device(wps.device):
+        with _on(wps.device):
             check(_LIBRARY.jk_transition_pairwise_topk_routes(
                 wps.data_ptr(), pt.data_ptr(), B, S, Dn, rp, _DTYPE_CODE[wps.dtype], None, _lib.JK_F32, k,
                 float(score_bias), None, compress, routes.data_ptr(), scores.data_ptr(), index.data_ptr(),
@@ -1081,7 +1100,7 @@ def softmax_backward_cuda(routes, grad_routes):
     g = _cuda_contig("grad_routes", grad_routes).to(r.dtype)
     out = torch.empty_like(r)
     n = r.shape[-1] if r.dim() else 1
-    with torch.cuda.device(r.device):
+    with _on(r.device):
         check(_LIBRARY.jk_softmax_backward(r.data_ptr(), g.data_ptr(), out.data_ptr(), r.numel() // max(n, 1), n,
                                            _dtype_code("routes", r), _stream(r.device)), "jk_softmax_backward")
     return out
@@ -1093,7 +1112,7 @@ def softsign_backward_cuda(scores, grad_edges):
     s = _cuda_contig("scores", scores)
     g = _cuda_contig("grad_edges", grad_edges).to(s.dtype)
     out = torch.empty_like(s)
-    with torch.cuda.device(s.device):
+    with _on(s.device):
         check(_LIBRARY.jk_softsign_backward(s.data_ptr(), g.data_ptr(), out.data_ptr(), s.numel(),
                                             _dtype_code("scores", s), _stream(s.device)), "jk_softsign_backward")
     return out
@@ -1104,7 +1123,7 @@ def _dense_from_topk(w: Tensor, index: Tensor, n_cols: int) -> Tensor:
     w = w.float().contiguous()
     index = index.contiguous()
     dense = torch.zeros(w.shape[:-1] + (n_cols,), device=w.device, dtype=torch.float32)
-    with torch.cuda.device(w.device):
+    with _on(w.device):
         check(_LIBRARY.jk_topk_to_dense(w.data_ptr(), index.data_ptr(), dense.data_ptr(), w.numel() // w.shape[-1],
                                         w.shape[-1], n_cols, _stream(w.device)), "jk_topk_to_dense")
     return dense
@@ -1130,7 +1149,7 @@ def query_topk_reduce_backward_cuda(edges, indices, projected_state, projected_v
     gv = _cuda_contig("grad_delta_val", grad_delta_val).to(dt).reshape(B, Q, D)
     idx = idx.reshape(B, Q, k)
     grad_edges = torch.empty((B, Q, k), device=e.device, dtype=dt)
-    with torch.cuda.device(e.device):
+    with _on(e.device):
         check(_LIBRARY.jk_topk_reduce_backward_edges(idx.data_ptr(), st.data_ptr(), vv.data_ptr(), gs.data_ptr(),
                                                      gv.data_ptr(), grad_edges.data_ptr(), B, Q, S, k, D,
                                                      _dtype_code("state", st), _dtype_code("out", grad_edges),
