@@ -66,10 +66,11 @@ def _kernel_block(row_proj, col_proj, col_state, col_val, k, window, begin, coun
 def gather_row_blocks(out_state: Tensor, out_val: Tensor, blocks: list[tuple[int, int]], group=None,
                       stream: Optional[torch.cuda.Stream] = None):
     """Assembles the row blocks every rank wrote into its own out_state [B, N] / out_val
-    [B, N, D] so that every rank holds the full outputs: one rank-major all-gather per
-    tensor (the rank's block of every batch item packed into a [B, blk, ...] buffer,
-    gathered into [world, B, blk, ...]) -- two collectives whatever the batch size -- then
-    the blocks are copied into place. With `stream` the exchange runs on that stream
+    [B, N, D] so that every rank holds the full outputs. Equal blocks that tile the rows (the
+    usual case) are gathered in place, one all-gather per batch item and tensor, with no
+    copies; otherwise one rank-major all-gather per tensor (the rank's block of every batch
+    item packed into a [B, blk, ...] buffer, gathered into [world, B, blk, ...]) -- two
+    collectives whatever the batch size -- then the blocks are copied into place. With `stream` the exchange runs on that stream
     (ordered after the current stream's work), so a caller can overlap it with compute."""
     world = len(blocks)
     rank = dist.get_rank(group)
@@ -80,6 +81,15 @@ def gather_row_blocks(out_state: Tensor, out_val: Tensor, blocks: list[tuple[int
     if stream is not None:
         stream.wait_stream(torch.cuda.current_stream(out_val.device))
     with ctx:
+        if all(c == blk and b0 == r * blk for r, (b0, c) in enumerate(blocks)):
+            # equal blocks tiling the rows: every batch item's rows are already rank-major,
+            # so each item is gathered in place (the rank's block is the input, the whole
+            # item the output) -- no packing or unpacking copies
+            for full in (out_state, out_val):
+                for b in range(B):
+                    item = full[b]
+                    dist.all_gather_into_tensor(item.view(-1), item[begin:begin + count].reshape(-1), group=group)
+            return out_state, out_val
         for full in (out_state, out_val):
             send = full.new_zeros((B, blk) + tuple(full.shape[2:]))
             send[:, :count] = full[:, begin:begin + count]
