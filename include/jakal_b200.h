@@ -244,6 +244,16 @@ int jk_split3_bf16(const float* x, int64_t rows, int64_t rank, void* out, jk_str
 /* f32 -> bf16 hi plane + bf16 lo plane (x - hi), n elements each, for f32 values. */
 int jk_split2_bf16(const float* x, int64_t n, void* hi, void* lo, jk_stream_t stream);
 
+/* f32 x [batch, rows, cols] (plus, when extra_col is not NULL, extra_col [batch, rows] as
+ * column cols) -> bf16 out [batch, nblk * rows, out_cols]: block k (rows [k * rows,
+ * (k + 1) * rows) of every batch item) holds the hi plane bf16(x) when bit k of plane_bits is
+ * 0, the lo plane bf16(x - hi) when it is 1; columns past the data are zero. Stacking the
+ * route matrix as (hi, hi, lo) and the values as (hi, lo, hi) makes one GEMM over the stacked
+ * dimension sum the three products of an f32-accurate split GEMM. nblk <= 4. Replaces
+ * nothing in the reference (its scatter adds f32 routes into f32 accumulators). */
+int jk_split_stack_bf16(const float* x, const float* extra_col, int64_t batch, int64_t rows, int64_t cols,
+                        int64_t out_cols, int nblk, unsigned plane_bits, void* out, jk_stream_t stream);
+
 /*
  * Per-query ("query top-k") transition: identical contract to
  * jk_propagation_topk_forward with rows = query slots (row_proj = target-side route

@@ -41,6 +41,27 @@ __global__ void split2_kernel(const float* __restrict__ x, int64_t n, __nv_bfloa
   }
 }
 
+// out[b, i * rows + r, c] = plane (bits >> i) & 1 (0 = hi, 1 = lo) of v, where v = x[b, r, c]
+// for c < cols, extra[b, r] at c == cols (when given), 0 beyond.
+__global__ void split_stack_kernel(const float* __restrict__ x, const float* __restrict__ extra, int64_t batch,
+                                   int64_t rows, int64_t cols, int64_t out_cols, int nblk, unsigned bits,
+                                   __nv_bfloat16* __restrict__ out) {
+  const int64_t n = batch * rows * out_cols;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const int64_t c = i % out_cols;
+    const int64_t br = i / out_cols;  // b * rows + r
+    float v = 0.f;
+    if (c < cols) v = x[br * cols + c];
+    else if (c == cols && extra != nullptr) v = extra[br];
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    const __nv_bfloat16 l = __float2bfloat16_rn(v - __bfloat162float(h));
+    const int64_t b = br / rows, r = br % rows;
+    for (int k = 0; k < nblk; ++k)
+      out[((b * nblk + k) * rows + r) * out_cols + c] = ((bits >> k) & 1u) ? l : h;
+  }
+}
+
 }  // namespace split
 }  // namespace jk
 
@@ -67,5 +88,22 @@ extern "C" int jk_split2_bf16(const float* x, int64_t n, void* hi, void* lo, jk_
   if (blocks > 148 * 32) blocks = 148 * 32;
   split::split2_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, n, reinterpret_cast<__nv_bfloat16*>(hi), reinterpret_cast<__nv_bfloat16*>(lo));
+  return launch_status();
+}
+
+extern "C" int jk_split_stack_bf16(const float* x, const float* extra_col, int64_t batch, int64_t rows,
+                                   int64_t cols, int64_t out_cols, int nblk, unsigned plane_bits, void* out,
+                                   jk_stream_t stream) {
+  using namespace jk;
+  if (x == nullptr || out == nullptr) return JK_ERR_BAD_ARG;
+  if (batch <= 0 || rows <= 0 || cols <= 0 || nblk < 1 || nblk > 4) return JK_ERR_BAD_SHAPE;
+  if (out_cols < cols + (extra_col != nullptr ? 1 : 0)) return JK_ERR_BAD_SHAPE;
+  int st = check_device();
+  if (st != JK_OK) return st;
+  const int64_t n = batch * rows * out_cols;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  split::split_stack_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, extra_col, batch, rows, cols, out_cols, nblk, plane_bits, reinterpret_cast<__nv_bfloat16*>(out));
   return launch_status();
 }

@@ -704,13 +704,36 @@ def _split2_bf16(x: Tensor) -> tuple[Tensor, Tensor]:
     return hi, lo
 
 
+def _split_stack(x: Tensor, extra: Optional[Tensor], out_cols: int, planes: tuple[int, ...]) -> Tensor:
+    """bf16 [B, len(planes) * rows, out_cols]: the planes (0 hi, 1 lo) of f32 x [B, rows, cols]
+    (with `extra` [B, rows] as column cols) stacked along the rows (jk_split_stack_bf16)."""
+    x = x.contiguous()
+    B, rows, cols = x.shape
+    out = torch.empty((B, len(planes) * rows, out_cols), device=x.device, dtype=torch.bfloat16)
+    bits = sum(p << i for i, p in enumerate(planes))
+    with _on(x.device):
+        check(_LIBRARY.jk_split_stack_bf16(x.data_ptr(), _ptr(extra), B, rows, cols, out_cols, len(planes), bits,
+                                           out.data_ptr(), _stream(x.device)), "jk_split_stack_bf16")
+    return out
+
+
 def routes_aggregate(routes: Tensor, state: Tensor, val: Tensor) -> tuple[Tensor, Tensor]:
     """Aggregate of a dense route matrix: out_state[b, d] = sum_s routes[b, s, d] state[b, s],
-    out_val[b, d] = sum_s routes[b, s, d] val[b, s] (f32 results). Tensor-core GEMMs with f32
-    accumulation and output: the routes are split into hi + lo planes of the values' 16-bit
-    dtype (two GEMMs); f32 values are split into bf16 hi + lo planes too (three GEMMs, the
-    lo x lo product dropped: ~2^-16 relative). The bf16 splits are single passes of the
-    library's split kernel."""
+    out_val[b, d] = sum_s routes[b, s, d] val[b, s] (f32 results), on the tensor cores with f32
+    accumulation and output.
+    f32 values: one GEMM. The routes are stacked as bf16 (hi, hi, lo) planes along the source
+    dimension and the values, with the state as one more column, as (hi, lo, hi): the GEMM over
+    the stacked dimension sums hi.hi + hi.lo + lo.hi (the lo.lo product dropped: ~2^-16
+    relative). 16-bit values: the routes split into hi + lo planes of the values' dtype, two
+    GEMMs, and the state aggregate as an f32 GEMM."""
+    if val.dtype == torch.float32:
+        B, S, Dn = routes.shape
+        D = val.shape[-1]
+        dp = -(-(D + 1) // 8) * 8  # values, state column, zero padding to 16-byte rows
+        r3 = _split_stack(routes, None, Dn, (0, 0, 1))
+        v3 = _split_stack(val, state.float().contiguous(), dp, (0, 1, 0))
+        out = torch.bmm(r3.transpose(1, 2), v3, out_dtype=torch.float32)
+        return out[..., D].contiguous(), out[..., :D].contiguous()
     rt = routes.transpose(1, 2)
     with _exact_f32_matmul():
         out_state = torch.bmm(rt, state.float().unsqueeze(-1)).squeeze(-1)
@@ -718,20 +741,11 @@ def routes_aggregate(routes: Tensor, state: Tensor, val: Tensor) -> tuple[Tensor
         r_hi = routes.to(torch.float16)
         r_lo = (routes - r_hi.float()).to(torch.float16)
         out_val = torch.bmm(r_hi.transpose(1, 2), val, out_dtype=torch.float32)
-        out_val += torch.bmm(r_lo.transpose(1, 2), val, out_dtype=torch.float32)
+        out_val = torch.baddbmm(out_val, r_lo.transpose(1, 2), val, out_dtype=torch.float32)
         return out_state, out_val
     r_hi, r_lo = _split2_bf16(routes)
-    r_hi, r_lo = r_hi.transpose(1, 2), r_lo.transpose(1, 2)
-    # the later products accumulate into the f32 result inside the GEMM (beta = 1)
-    if val.dtype == torch.bfloat16:
-        out_val = torch.bmm(r_hi, val, out_dtype=torch.float32)
-        out_val = torch.baddbmm(out_val, r_lo, val, out_dtype=torch.float32)
-    else:
-        # f32 values: hi + lo planes on both sides, the three products above 2^-16
-        v_hi, v_lo = _split2_bf16(val.float())
-        out_val = torch.bmm(r_hi, v_hi, out_dtype=torch.float32)
-        out_val = torch.baddbmm(out_val, r_hi, v_lo, out_dtype=torch.float32)
-        out_val = torch.baddbmm(out_val, r_lo, v_hi, out_dtype=torch.float32)
+    out_val = torch.bmm(r_hi.transpose(1, 2), val, out_dtype=torch.float32)
+    out_val = torch.baddbmm(out_val, r_lo.transpose(1, 2), val, out_dtype=torch.float32)
     return out_state, out_val
 
 

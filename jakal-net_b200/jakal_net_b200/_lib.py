@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "jk_split3_bf16": (_i32, [_p, _i64, _i64, _p, _p]),
     "jk_split2_bf16": (_i32, [_p, _i64, _p, _p, _p]),
+    "jk_split_stack_bf16": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i32, ctypes.c_uint, _p, _p]),
     "jk_transition_query_topk_forward": (
         _i32,
         [_p, _p, _i64, _i64, _i64, _i64, _i32,
