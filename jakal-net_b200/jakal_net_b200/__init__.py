@@ -140,6 +140,8 @@ def _entry(fn):
         # plain flag toggles (not the context managers): an op is called per layer of a model
         # step, and the host time of every call adds to the step when the GPU waits on it
         prev = getattr(_TLS, "autocast", None)
+        prev_casts = getattr(_TLS, "casts", None)
+        _TLS.casts = {}
         ac_on = torch.is_autocast_enabled("cuda")
         grad_on = torch.is_grad_enabled()
         _TLS.autocast = torch.get_autocast_dtype("cuda") if ac_on else None
@@ -155,8 +157,22 @@ def _entry(fn):
             if ac_on:
                 torch.set_autocast_enabled("cuda", True)
             _TLS.autocast = prev
+            _TLS.casts = prev_casts
 
     return wrapper
+
+
+def _autocast_cast(x: Tensor, ac: torch.dtype) -> Tensor:
+    """x.to(ac), computed once per op call for one tensor (an op often scores and aggregates
+    the same layer values, and reshaped views of it share the key)."""
+    casts = getattr(_TLS, "casts", None)
+    if casts is None:
+        return x.to(ac)
+    key = (x.data_ptr(), tuple(x.shape), tuple(x.stride()), ac)
+    hit = casts.get(key)
+    if hit is None:
+        hit = casts[key] = x.to(ac)
+    return hit
 
 
 def _scorer_input(x: Tensor) -> Tensor:
@@ -165,7 +181,7 @@ def _scorer_input(x: Tensor) -> Tensor:
     autocast."""
     ac = getattr(_TLS, "autocast", None)
     if ac is not None and x.dtype == torch.float32:
-        return x.to(ac)
+        return _autocast_cast(x, ac)
     return x
 
 
@@ -177,7 +193,7 @@ def _aggregate_input(x: Tensor) -> Tensor:
     the projected inputs."""
     ac = getattr(_TLS, "autocast", None)
     if ac is not None and x.dtype == torch.float32:
-        return x.to(ac)
+        return _autocast_cast(x, ac)
     return x
 
 
