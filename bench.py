@@ -332,8 +332,16 @@ def run_reference(args, rank):
         value, sample, threads, kind = cpu_baseline_config2(max(5.0, min(30.0, 0.05 * args.steps)))
         metric, unit, cfg, dtype = METRIC, UNIT, WORKLOAD, "f32"
         ms = PAIRS_PER_STEP / (value * 1e9) * 1e3
+    elif args.config == 3:
+        cb = cpu_config3(max(5.0, min(30.0, 0.05 * args.steps)))
+        if cb is None:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference's native CPU build is absent"}))
+            return
+        value, sample, threads = cb
+        metric, unit, cfg, dtype, kind = C3_METRIC, UNIT, C3_WORKLOAD, "f32", "reference"
+        ms = C3["B"] * C3["Q"] * C3["S"] / (value * 1e9) * 1e3
     else:
-        print(json.dumps({"impl": "reference", "unavailable": "the reference arm covers configs 2 and 4"}))
+        print(json.dumps({"impl": "reference", "unavailable": "the reference arm covers configs 2, 3 and 4"}))
         return
     line = {
         "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
@@ -633,6 +641,136 @@ def run_config5(args, rank, world, device):
         "e2e": {"value": pairs / (e2e_ms * 1e-3) / 1e9, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": m["h2d"], "d2h_bytes_per_step": m["d2h"]},
     }
+    print(json.dumps(line), flush=True)
+
+
+C3 = dict(B=16, S=4096, Q=512, D=512, R=64, K=16, SEED=2)
+C3_METRIC = "per-query transition Gpairs/s"
+C3_WORKLOAD = ("config3: transition S -> expanded B query-top-k routing, B16 S4096 Q512 D512 R64 k16, bf16, "
+               "softmax routes, sender-weighted")
+
+
+def _config3_inputs(batch, device=None, dtype=torch.bfloat16):
+    """Config 3's inputs (S val ~ N(0,1), B slots ~ N(0, 0.02), projection weights ~ N(0,
+    1/sqrt(D)), seed 2); `batch` items of the B16 batch. The sender strength is softplus of the
+    source state, as the reference's SparseTransition forms it from Layer.state."""
+    c = C3
+    g = torch.Generator().manual_seed(c["SEED"])
+    to = dict(dtype=dtype) if device is None else dict(device=device, dtype=dtype)
+    src = torch.randn(c["B"], c["S"], c["D"], generator=g)[:batch]
+    slots = (0.02 * torch.randn(c["B"], c["Q"], c["D"], generator=g))[:batch]
+    state = torch.randn(c["B"], c["S"], generator=g)[:batch]
+    w_s = torch.randn(c["R"], c["D"], generator=g) / c["D"] ** 0.5
+    w_t = torch.randn(c["R"], c["D"], generator=g) / c["D"] ** 0.5
+    core = torch.full((c["R"],), c["R"] ** -0.5)
+    sender = torch.nn.functional.softplus(state)
+    return [t.to(**to) for t in (src, slots, state, sender, w_s, w_t, core)]
+
+
+def _config3_call(mod, src, slots, state, sender, w_s, w_t, core):
+    """One per-query transition through a module's reference-facing op (this backend or the
+    reference's native extension): rows = query slots, columns = sources."""
+    return mod.transition_query_topk("low_rank_bilinear_route", w_s, None, w_t, None, core, None, None, None, None,
+                                     None, 1.0, sender, src, slots, state, src, C3["K"], 128, 128, False)
+
+
+def cpu_config3(seconds: float = 10.0):
+    """The reference's C++ CPU extension (oracle/build_ref.py, from its own sources) on one
+    batch item of config 3 in f32, all host threads: (Gpairs/s, sample, threads) or None."""
+    from oracle import build_ref
+
+    if not build_ref.available("cpu"):
+        return None
+    native = build_ref.load_built("cpu")
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    args = _config3_inputs(1, dtype=torch.float32)
+    pairs = C3["Q"] * C3["S"]
+    rate, reps = _median_rate(lambda: _config3_call(native, *args), pairs, seconds, min_reps=3)
+    sample = (f"median of {reps} runs of 1 of the 16 batch items (S4096 Q512 D512 k16, f32) through the reference's "
+              f"native CPU transition_query_topk; torch threads {torch.get_num_threads()}, {_cpu_model()}")
+    return rate / 1e9, sample, threads
+
+
+def run_config3(args, rank, world, device):
+    """Config 3 on this backend: batch-sharded (weak scaling), every rank its own B16 batch."""
+    import jakal_net_b200 as jk
+
+    c = C3
+    src, slots, state, sender, w_s, w_t, core = _config3_inputs(c["B"], device)
+    pairs = c["B"] * c["Q"] * c["S"]
+
+    def step():
+        return _config3_call(jk, src, slots, state, sender, w_s, w_t, core)
+
+    launches = count_launches(step)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    steps = max(1, args.steps)
+    ms = []
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        for _ in range(steps):
+            flush.add_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step()
+            e1.record()
+            torch.cuda.synchronize(device)
+            ms.append(e0.elapsed_time(e1))
+    step_ms = sum(ms) / len(ms)
+    # end to end: host (pinned) sources and slots in, outputs back, every step
+    h_src, h_slots = src.cpu().pin_memory(), slots.cpu().pin_memory()
+    h_state = state.cpu().pin_memory()
+    st0, vv0 = step()
+    h_out_s = torch.empty(st0.shape, dtype=st0.dtype).pin_memory()
+    h_out_v = torch.empty(vv0.shape, dtype=vv0.dtype).pin_memory()
+
+    def e2e():
+        d_src = h_src.to(device, non_blocking=True)
+        d_slots = h_slots.to(device, non_blocking=True)
+        d_state = h_state.to(device, non_blocking=True)
+        snd = torch.nn.functional.softplus(d_state.float()).to(d_state.dtype)
+        st, vv = _config3_call(jk, d_src, d_slots, d_state, snd, w_s, w_t, core)
+        h_out_s.copy_(st, non_blocking=True)
+        h_out_v.copy_(vv, non_blocking=True)
+
+    e2e()
+    torch.cuda.synchronize(device)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(steps):
+        e2e()
+    g1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = g0.elapsed_time(g1) / steps
+    if world > 1:
+        t = torch.tensor([step_ms, e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        step_ms, e2e_ms = (float(x) for x in t.tolist())
+    if rank != 0:
+        return
+    line = {
+        "metric": C3_METRIC, "value": world * pairs / (step_ms * 1e-3) / 1e9, "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded inputs of the config-3 shapes and distributions, random-init weights)",
+        "config": {"workload": C3_WORKLOAD, "pairs_per_step": pairs, "l2": "256 MiB write between timed steps",
+                   "timing": "CUDA events per step (public op: projections + fused kernel), max over ranks",
+                   "parallelism": f"batch-sharded x{world}, no collective"},
+        "gpu_launches": launches * steps, "clocks": clk.summary(),
+        "e2e": {"value": world * pairs / (e2e_ms * 1e-3) / 1e9, "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": (h_src.numel() + h_slots.numel() + h_state.numel()) * 2,
+                "d2h_bytes_per_step": (h_out_s.numel() + h_out_v.numel()) * h_out_v.element_size()},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cb = cpu_config3()
+        if cb is not None:
+            line["cpu_baseline"] = {"value": cb[0], "unit": UNIT, "cores": cb[2], "kind": "reference",
+                                    "sample": cb[1]}
     print(json.dumps(line), flush=True)
 
 
@@ -976,7 +1114,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[2, 4, 5], default=2)
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2)
     ap.add_argument("--no-reference-gpu", action="store_true")
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 row-sharded record of the default run")
     ap.add_argument("--micro", choices=sorted(MICRO), help="time one module op at a config-4 shape instead")
@@ -996,7 +1134,7 @@ def main():
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=device)
     try:
-        {2: run_b200, 4: run_config4, 5: run_config5}[args.config](args, rank, world, device)
+        {2: run_b200, 3: run_config3, 4: run_config4, 5: run_config5}[args.config](args, rank, world, device)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()
