@@ -267,3 +267,32 @@ def test_transition_routes_form_is_deterministic_and_matches_the_scatter(dev, co
     torch.cuda.synchronize()
     parity.assert_rows_close(_np(a[1]), _np(vv), rtol=OUT_RTOL, what="routes vs scatter val")
     parity.assert_rows_close(_np(a[0]), _np(st), rtol=OUT_RTOL, what="routes vs scatter state")
+
+
+def test_split_stack_planes_and_route_aggregate(dev):
+    """jk_split_stack_bf16 stacks hi / lo planes (with the extra column and zero padding) as
+    asked, and the one-GEMM route aggregate of f32 values built on it matches an f64 aggregate
+    of the same routes to the split's ~2^-16 relative accuracy."""
+    import jakal_net_b200 as jk
+
+    g = torch.Generator().manual_seed(11)
+    B, S, C, Dn = 3, 37, 20, 9
+    x = torch.randn(B, S, C, generator=g).to(dev)
+    extra = torch.randn(B, S, generator=g).to(dev)
+    out = jk._split_stack(x, extra, 24, (0, 1, 0))
+    hi = x.to(torch.bfloat16)
+    lo = (x - hi.float()).to(torch.bfloat16)
+    e_hi = extra.to(torch.bfloat16)
+    e_lo = (extra - e_hi.float()).to(torch.bfloat16)
+    for blk, (pl, ex) in enumerate(((hi, e_hi), (lo, e_lo), (hi, e_hi))):
+        part = out[:, blk * S:(blk + 1) * S]
+        assert torch.equal(part[..., :C], pl)
+        assert torch.equal(part[..., C], ex)
+        assert not part[..., C + 1:].any()
+    routes = torch.rand(B, S, Dn, generator=g).to(dev) * (torch.rand(B, S, Dn, generator=g) < 0.3).to(dev)
+    st, vv = jk.routes_aggregate(routes, extra, x)
+    want_v = torch.einsum("bsd,bsc->bdc", routes.double(), x.double())
+    want_s = torch.einsum("bsd,bs->bd", routes.double(), extra.double())
+    scale_v = want_v.abs() + want_v.pow(2).mean(dim=-1, keepdim=True).sqrt()
+    assert ((vv.double() - want_v).abs() / scale_v).max().item() < 1e-4
+    assert ((st.double() - want_s).abs() / (want_s.abs() + want_s.pow(2).mean().sqrt())).max().item() < 1e-4
