@@ -34,6 +34,7 @@ import contextlib
 import ctypes
 import functools
 import threading
+import weakref
 from typing import Optional
 
 import torch
@@ -258,6 +259,27 @@ def _flatten_state(t: Tensor) -> Tensor:
     return t.reshape(-1, t.shape[-1]).contiguous()
 
 
+_PARAM_CASTS: dict = {}
+
+
+def _cast_param(w: Tensor, device: torch.device, dtype: torch.dtype) -> Tensor:
+    """w (a weight the caller owns, e.g. a module parameter) detached, on `device` in `dtype`,
+    contiguous. Casts are kept per tensor object and reused while its version counter is
+    unchanged (every in-place update, such as an optimizer step, bumps it), so a model's
+    f32 weights are not cast again on every call."""
+    if w.dtype == dtype and w.device == device:
+        return w.detach().contiguous()
+    key = (id(w), dtype, device)
+    hit = _PARAM_CASTS.get(key)
+    if hit is not None and hit[0]() is w and hit[1] == w._version:
+        return hit[2]
+    out = w.detach().to(device=device, dtype=dtype).contiguous()
+    if len(_PARAM_CASTS) > 1024:
+        _PARAM_CASTS.clear()
+    _PARAM_CASTS[key] = (weakref.ref(w), w._version, out)
+    return out
+
+
 def _pad_dim8(x2: Tensor, w: Tensor) -> tuple[Tensor, Tensor]:
     """Zero-pads the contraction dim of a projection to a multiple of 8 (16-byte TMA rows);
     the padded columns add exact zeros to every dot product."""
@@ -294,8 +316,8 @@ def lowrank_project(x: Tensor, weight: Tensor, core: Optional[Tensor] = None,
     code = _proj_dtype(x)
     if rank > 128:
         raise RuntimeError(f"b200_sm100a fused projections support score rank <= 128 (got {rank}).")
-    x2, w = _pad_dim8(x2, weight.detach().to(device=x.device, dtype=x.dtype))
-    c = None if core is None else core.detach().reshape(-1).to(device=x.device, dtype=x.dtype).contiguous()
+    x2, w = _pad_dim8(x2, _cast_param(weight, x.device, x.dtype))
+    c = None if core is None else _cast_param(core, x.device, x.dtype).reshape(-1)
     rp = int(_LIBRARY.jk_padded_rank(rank))
     out = torch.empty((x2.shape[0], rp), device=x.device, dtype=x.dtype)
     with _on(x.device):
@@ -316,9 +338,9 @@ def lowrank_project_pair(x: Tensor, weight: Tensor, weight2: Tensor, core: Optio
     rank, dim = weight.shape
     if (x.dtype == torch.float32 or rank > 64 or tuple(weight2.shape) != (rank, dim) or x.shape[-1] != dim):
         return lowrank_project(x, weight), lowrank_project(x, weight2, core=core, temperature=temperature)
-    x2, w = _pad_dim8(x.reshape(-1, dim), weight.detach().to(device=x.device, dtype=x.dtype))
-    _, w2 = _pad_dim8(x2[:0, :dim], weight2.detach().to(device=x.device, dtype=x.dtype))
-    c = None if core is None else core.detach().reshape(-1).to(device=x.device, dtype=x.dtype).contiguous()
+    x2, w = _pad_dim8(x.reshape(-1, dim), _cast_param(weight, x.device, x.dtype))
+    _, w2 = _pad_dim8(x2[:0, :dim], _cast_param(weight2, x.device, x.dtype))
+    c = None if core is None else _cast_param(core, x.device, x.dtype).reshape(-1)
     out = torch.empty((x2.shape[0], 64), device=x.device, dtype=x.dtype)
     out2 = torch.empty((x2.shape[0], 64), device=x.device, dtype=x.dtype)
     with _on(x.device):
