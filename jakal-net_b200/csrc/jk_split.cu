@@ -46,19 +46,18 @@ __global__ void split2_kernel(const float* __restrict__ x, int64_t n, __nv_bfloa
 __global__ void split_stack_kernel(const float* __restrict__ x, const float* __restrict__ extra, int64_t batch,
                                    int64_t rows, int64_t cols, int64_t out_cols, int nblk, unsigned bits,
                                    __nv_bfloat16* __restrict__ out) {
-  const int64_t n = batch * rows * out_cols;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const int64_t c = i % out_cols;
-    const int64_t br = i / out_cols;  // b * rows + r
-    float v = 0.f;
-    if (c < cols) v = x[br * cols + c];
-    else if (c == cols && extra != nullptr) v = extra[br];
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    const __nv_bfloat16 l = __float2bfloat16_rn(v - __bfloat162float(h));
-    const int64_t b = br / rows, r = br % rows;
-    for (int k = 0; k < nblk; ++k)
-      out[((b * nblk + k) * rows + r) * out_cols + c] = ((bits >> k) & 1u) ? l : h;
+  // one (batch item, row) per block iteration, the threads across its columns (coalesced)
+  for (int64_t br = blockIdx.x; br < batch * rows; br += gridDim.x) {
+    const int64_t b = br / rows, r = br - b * rows;
+    const float* xr = x + br * cols;
+    const float ex = (extra != nullptr) ? extra[br] : 0.f;
+    for (int64_t c = threadIdx.x; c < out_cols; c += blockDim.x) {
+      const float v = c < cols ? xr[c] : (c == cols ? ex : 0.f);
+      const __nv_bfloat16 h = __float2bfloat16_rn(v);
+      const __nv_bfloat16 l = __float2bfloat16_rn(v - __bfloat162float(h));
+      for (int k = 0; k < nblk; ++k)
+        out[((b * nblk + k) * rows + r) * out_cols + c] = ((bits >> k) & 1u) ? l : h;
+    }
   }
 }
 
@@ -100,10 +99,10 @@ extern "C" int jk_split_stack_bf16(const float* x, const float* extra_col, int64
   if (out_cols < cols + (extra_col != nullptr ? 1 : 0)) return JK_ERR_BAD_SHAPE;
   int st = check_device();
   if (st != JK_OK) return st;
-  const int64_t n = batch * rows * out_cols;
-  int64_t blocks = (n + 255) / 256;
-  if (blocks > 148 * 32) blocks = 148 * 32;
-  split::split_stack_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  int64_t blocks = batch * rows;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  const int threads = out_cols >= 256 ? 256 : (out_cols >= 128 ? 128 : 64);
+  split::split_stack_kernel<<<static_cast<unsigned>(blocks), threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, extra_col, batch, rows, cols, out_cols, nblk, plane_bits, reinterpret_cast<__nv_bfloat16*>(out));
   return launch_status();
 }
